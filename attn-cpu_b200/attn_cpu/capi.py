@@ -1,0 +1,143 @@
+"""capi -- ctypes access to the C ABI of libattnb.so (include/attnb.h).
+
+The device-pointer entry points (``*_dev``) take raw device addresses and a
+CUDA stream; the helpers below accept torch CUDA tensors (torch is used only
+for device memory and streams) and enqueue on the current torch stream.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libattnb.so")
+
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_RUNTIME = 2
+ERR_CUDA = 3
+ERR_DEVICE_TIMEOUT = 4
+
+PREC = {None: -1, "default": -1, "3xtf32": 0, "tf32": 1}
+
+# Every symbol include/attnb.h declares.
+EXPORTED = [
+    "attnb_last_error", "attnb_version", "attnb_stream_status",
+    "attnb_sgemm", "attnb_gemm_jit", "attnb_sgemm_dev", "attnb_linear_dev",
+    "attnb_attn_step_dense", "attnb_attn_step_dense_dev",
+    "attnb_attn_block_dense", "attnb_attn_block_dense_dev",
+    "attnb_mha_block_dense", "attnb_mha_block_dense_dev",
+]
+
+
+class Tensor(ctypes.Structure):
+    """attnb_tensor / attnb_mtensor: data, H, T, Dh, strideH, strideT, strideDh."""
+    _fields_ = [("data", ctypes.c_void_p), ("H", ctypes.c_int), ("T", ctypes.c_int),
+                ("Dh", ctypes.c_int), ("strideH", ctypes.c_int64), ("strideT", ctypes.c_int64),
+                ("strideDh", ctypes.c_int64)]
+
+
+class AttnbError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"attnb error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} is missing: run attn-cpu_b200/build.py")
+        L = ctypes.CDLL(LIB_PATH)
+        vp, i, f, i64 = ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_int64
+        T = ctypes.POINTER(Tensor)
+        L.attnb_last_error.restype = ctypes.c_char_p
+        L.attnb_version.restype = ctypes.c_char_p
+        L.attnb_stream_status.argtypes = [vp]
+        L.attnb_sgemm.argtypes = [vp, i, i, vp, i, vp, f, f, i]
+        L.attnb_gemm_jit.argtypes = [vp, i, i, vp, i, vp, f, f, i]
+        L.attnb_sgemm_dev.argtypes = [vp, i, vp, i, vp, i, i, i, i, f, f, i, vp]
+        L.attnb_linear_dev.argtypes = [vp, i, vp, i, vp, vp, i, i, i, i, i, vp]
+        L.attnb_attn_step_dense.argtypes = [T, T, T, T]
+        L.attnb_attn_step_dense_dev.argtypes = [T, T, T, T, vp]
+        L.attnb_attn_block_dense.argtypes = [T, T, T, T, i, i]
+        L.attnb_attn_block_dense_dev.argtypes = [T, T, T, T, i, i, vp]
+        L.attnb_mha_block_dense.argtypes = [vp, i, i, vp, vp, vp, vp, i, i, vp, i]
+        L.attnb_mha_block_dense_dev.argtypes = [vp, i, i, i, vp, vp, vp, vp, i, i, vp, i, vp]
+        for name in EXPORTED:
+            if name not in ("attnb_last_error", "attnb_version"):
+                getattr(L, name).restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != OK:
+        raise AttnbError(rc, lib().attnb_last_error().decode())
+
+
+def _stream(stream=None) -> int:
+    import torch
+
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return s.cuda_stream
+
+
+def tensor3(t, as_2d: bool = False) -> Tensor:
+    """attnb_tensor view of a float32 CUDA tensor [H,T,Dh] (or [H,Dh] with as_2d)."""
+    if as_2d:
+        H, Dh = t.shape
+        return Tensor(t.data_ptr(), H, 1, Dh, t.stride(0), 0, t.stride(1))
+    H, T_, Dh = t.shape
+    return Tensor(t.data_ptr(), H, T_, Dh, t.stride(0), t.stride(1), t.stride(2))
+
+
+def sgemm_dev(A, B, C, alpha=1.0, beta=0.0, precision=None, stream=None) -> None:
+    """C = alpha * A @ B + beta * C on 2-D float32 CUDA tensors with unit column stride."""
+    M, K = A.shape
+    N = B.shape[1]
+    check(lib().attnb_sgemm_dev(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0),
+                                C.data_ptr(), C.stride(0), M, N, K, alpha, beta,
+                                PREC[precision], _stream(stream)))
+
+
+def linear_dev(x, W, b, y, precision=None, stream=None) -> None:
+    """y = x @ W^T + b (b may be None)."""
+    T_, K = x.shape
+    N = W.shape[0]
+    check(lib().attnb_linear_dev(x.data_ptr(), x.stride(0), W.data_ptr(), W.stride(0),
+                                 b.data_ptr() if b is not None else None, y.data_ptr(),
+                                 y.stride(0), T_, N, K, PREC[precision], _stream(stream)))
+
+
+def attn_step_dense_dev(Q, K, V, O, stream=None) -> None:
+    q, k, v, o = tensor3(Q, True), tensor3(K), tensor3(V), tensor3(O, True)
+    check(lib().attnb_attn_step_dense_dev(ctypes.byref(q), ctypes.byref(k), ctypes.byref(v),
+                                          ctypes.byref(o), _stream(stream)))
+
+
+def attn_block_dense_dev(Q, K, V, O, causal=False, precision=None, stream=None) -> None:
+    q, k, v, o = tensor3(Q), tensor3(K), tensor3(V), tensor3(O)
+    check(lib().attnb_attn_block_dense_dev(ctypes.byref(q), ctypes.byref(k), ctypes.byref(v),
+                                           ctypes.byref(o), int(causal), PREC[precision],
+                                           _stream(stream)))
+
+
+def mha_block_dense_dev(x, W_in, b_in, W_out, b_out, num_heads, y, causal=False,
+                        precision=None, stream=None) -> None:
+    """x, y: [batch, T, D] (or [T, D]) contiguous float32 CUDA tensors."""
+    if x.dim() == 2:
+        batch, (T_, D) = 1, x.shape
+    else:
+        batch, T_, D = x.shape
+    check(lib().attnb_mha_block_dense_dev(x.data_ptr(), batch, T_, D, W_in.data_ptr(),
+                                          b_in.data_ptr(), W_out.data_ptr(), b_out.data_ptr(),
+                                          num_heads, int(causal), y.data_ptr(), PREC[precision],
+                                          _stream(stream)))
+
+
+def stream_status(stream=None) -> None:
+    check(lib().attnb_stream_status(_stream(stream)))

@@ -1,0 +1,435 @@
+// capi.cu -- the C ABI (include/attnb.h): validation with the reference's
+// messages, host<->device staging for the host-pointer entry points, and
+// dispatch to the kernels.
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "kernels.h"
+#include "runtime.h"
+
+namespace attnb {
+const char* last_error_cstr();
+}
+
+using namespace attnb;
+
+namespace {
+
+template <class F>
+int guarded(F&& f) {
+  try {
+    f();
+    return ATTNB_OK;
+  } catch (const Error& e) {
+    return set_last_error(e.code, e.msg);
+  } catch (const std::exception& e) {
+    return set_last_error(ATTNB_ERR_RUNTIME, e.what());
+  } catch (...) {
+    return set_last_error(ATTNB_ERR_RUNTIME, "unknown error");
+  }
+}
+
+cudaStream_t as_stream(void* s) { return static_cast<cudaStream_t>(s); }
+
+// ------------------------------------------------------------- validation
+// attn::validate_dense_shapes, include/attn.h:54-83 of the reference.
+void validate_step(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
+                   const attnb_mtensor* O) {
+  if (!Q || !K || !V || !O) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null tensor descriptor");
+  if (!Q->data || !K->data || !V->data || !O->data)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+  if (Q->H <= 0 || Q->Dh <= 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "Q has invalid H/Dh");
+  if (K->H != Q->H || V->H != Q->H) fail(ATTNB_ERR_INVALID_ARGUMENT, "K/V H must match Q.H");
+  if (K->Dh != Q->Dh || V->Dh != Q->Dh)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "K/V Dh must match Q.Dh");
+  if (K->T <= 0 || V->T != K->T)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "K/V T must be positive and equal");
+  if (O->H != Q->H || O->Dh != Q->Dh)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "O must be [H, Dh] matching Q");
+  if (Q->strideH == 0 || Q->strideDh == 0 || K->strideH == 0 || K->strideT == 0 ||
+      K->strideDh == 0 || V->strideH == 0 || V->strideT == 0 || V->strideDh == 0 ||
+      O->strideH == 0 || O->strideDh == 0)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "Zero stride encountered");
+}
+
+// attn::attn_block_dense checks, src/attn_block.cpp:109-120 of the reference.
+void validate_block(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
+                    const attnb_mtensor* O, int causal) {
+  if (!Q || !K || !V || !O) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null tensor descriptor");
+  if (!Q->data || !K->data || !V->data || !O->data)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+  if (Q->H <= 0 || Q->Dh <= 0 || K->H != Q->H || V->H != Q->H)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "H mismatch");
+  if (K->Dh != Q->Dh || V->Dh != Q->Dh) fail(ATTNB_ERR_INVALID_ARGUMENT, "Dh mismatch");
+  if (K->T <= 0 || V->T != K->T) fail(ATTNB_ERR_INVALID_ARGUMENT, "K/V T mismatch");
+  if (O->H != Q->H || O->Dh != Q->Dh || O->T != Q->T)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "O must be [H,L,Dh] matching Q");
+  if (causal && Q->T != K->T) fail(ATTNB_ERR_INVALID_ARGUMENT, "causal=true requires L==T");
+  if (Q->T < 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "H mismatch");
+}
+
+// attn::mha_block_dense checks, src/attn_dispatch.cpp:22,45,132 of the reference.
+void validate_mha(const float* x, int T, int D, const float* W_in, const float* b_in,
+                  const float* W_out, const float* b_out, int H, const float* y) {
+  if (H <= 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "num_heads must be positive");
+  if (D % H != 0) fail(ATTNB_ERR_RUNTIME, "D must be divisible by H");
+  if (D <= 0 || D % 16 != 0)
+    fail(ATTNB_ERR_RUNTIME, "D not multiple of 16 fast path not implemented yet.");
+  if (T < 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "T must be non-negative");
+  if (T > 0 && (!x || !W_in || !b_in || !W_out || !b_out || !y))
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+}
+
+View3 view(const attnb_tensor* t, int T) {
+  return View3{t->data, t->H, T, t->Dh, t->strideH, t->strideT, t->strideDh};
+}
+MView3 mview(const attnb_mtensor* t, int T) {
+  return MView3{t->data, t->H, T, t->Dh, t->strideH, t->strideT, t->strideDh};
+}
+
+// ------------------------------------------------------------ host staging
+// Element-offset range [lo, hi] a strided view touches.
+struct Span {
+  int64_t lo = 0, hi = 0;
+  int64_t count() const { return hi - lo + 1; }
+};
+Span span_of(int H, int T, int Dh, int64_t sH, int64_t sT, int64_t sD) {
+  Span s;
+  auto add = [&](int n, int64_t st) {
+    if (n <= 1) return;
+    const int64_t e = (int64_t)(n - 1) * st;
+    if (e < 0) s.lo += e;
+    else s.hi += e;
+  };
+  add(H, sH);
+  add(T, sT);
+  add(Dh, sD);
+  return s;
+}
+
+// Carves 256-byte-aligned pieces out of one device allocation.
+struct Carver {
+  size_t off = 0;
+  size_t take(size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  }
+};
+
+struct Staged {
+  Span span;
+  size_t off;
+};
+
+template <class Fn>
+void with_host_ctx(Fn&& fn) {
+  DeviceCtx& c = current_ctx();
+  std::lock_guard<std::mutex> g(c.mu);
+  fn(c);
+}
+
+void finish_host_call(DeviceCtx& c) {
+  ATTNB_CUDA(cudaGetLastError());
+  if (consume_status(c, c.stream) != ATTNB_OK)
+    fail(ATTNB_ERR_DEVICE_TIMEOUT, "a bounded device wait expired");
+}
+
+// ------------------------------------------------------------------ decode
+void step_dev(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
+              const attnb_mtensor* O, DeviceCtx& c, cudaStream_t s, void* scratch_override,
+              size_t scratch_bytes) {
+  const View3 q = view(Q, 1), k = view(K, K->T), v = view(V, V->T);
+  const MView3 o = mview(O, 1);
+  const DecodePlan p = decode_plan(q, k, v, c.num_sms);
+  const size_t need = decode_workspace_bytes(p, K->H, K->Dh);
+  void* ws = scratch_override;
+  if (!ws) ws = dev_scratch(c, need, s);
+  else if (need > scratch_bytes) fail(ATTNB_ERR_RUNTIME, "scratch too small");
+  decode_launch(p, q, k, v, o, ws, s);
+  ATTNB_CUDA(cudaGetLastError());
+}
+
+// ---------------------------------------------------------------- prefill
+void block_dev(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
+               const attnb_mtensor* O, int causal, int precision, cudaStream_t s) {
+  (void)precision;
+  if (Q->T == 0) return;
+  attn_block_simt_launch(view(Q, Q->T), view(K, K->T), view(V, V->T), mview(O, O->T),
+                         causal != 0, s);
+  ATTNB_CUDA(cudaGetLastError());
+}
+
+// -------------------------------------------------------------------- MHA
+void mha_dev(const float* x, int batch, int T, int D, const float* W_in, const float* b_in,
+             const float* W_out, const float* b_out, int H, int causal, float* y, int prec,
+             DeviceCtx& c, cudaStream_t s) {
+  if (batch <= 0 || T <= 0) return;
+  const int Dh = D / H;
+  const int rows = batch * T;
+  const GemmPlan p_in = gemm_plan(rows, 3 * D, D, x, D, true, W_in, D, true, prec);
+  Carver cv;
+  const size_t off_qkv = cv.take((size_t)rows * 3 * D * sizeof(float));
+  const size_t off_ctx = cv.take((size_t)rows * D * sizeof(float));
+  const size_t off_g = cv.take(0);
+  // The two projections run one after the other and share the GEMM scratch.
+  const size_t g_bytes = std::max(p_in.ws_bytes, gemm_workspace_bound(rows, D, D, prec));
+  char* w = static_cast<char*>(dev_scratch(c, off_g + g_bytes, s));
+  float* qkv = reinterpret_cast<float*>(w + off_qkv);
+  float* ctx = reinterpret_cast<float*>(w + off_ctx);
+  void* gws = w + off_g;
+  // 1) [Q|K|V] = x . W_in^T + b_in   (src/attn_dispatch.cpp:63-95)
+  gemm_run(p_in, x, D, true, W_in, D, true, qkv, 3 * D, 1.f, 0.f, b_in, gws, c.status, c.num_sms, s);
+  // 2) per-sequence attention over the head-strided projections (:98-107)
+  for (int b = 0; b < batch; ++b) {
+    const float* base = qkv + (size_t)b * T * 3 * D;
+    attnb_tensor q{base, H, T, Dh, Dh, 3 * D, 1};
+    attnb_tensor k{base + D, H, T, Dh, Dh, 3 * D, 1};
+    attnb_tensor v{base + 2 * D, H, T, Dh, Dh, 3 * D, 1};
+    attnb_mtensor o{ctx + (size_t)b * T * D, H, T, Dh, Dh, D, 1};
+    block_dev(&q, &k, &v, &o, causal, prec, s);
+  }
+  // 3) y = ctx . W_out^T + b_out   (:110-127)
+  const GemmPlan p_out = gemm_plan(rows, D, D, ctx, D, true, W_out, D, true, prec);
+  gemm_run(p_out, ctx, D, true, W_out, D, true, y, D, 1.f, 0.f, b_out, gws, c.status, c.num_sms, s);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* attnb_last_error(void) { return last_error_cstr(); }
+
+const char* attnb_version(void) { return "attnb 0.1 sm_100a"; }
+
+int attnb_stream_status(void* stream) {
+  return guarded([&] {
+    DeviceCtx& c = current_ctx();
+    if (consume_status(c, as_stream(stream)) != ATTNB_OK)
+      fail(ATTNB_ERR_DEVICE_TIMEOUT, "a bounded device wait expired");
+  });
+}
+
+// ------------------------------------------------------------------- SGEMM
+int attnb_sgemm_dev(const float* A, int lda, const float* B, int ldb, float* C, int ldc, int M,
+                    int N, int K, float alpha, float beta, int precision, void* stream) {
+  return guarded([&] {
+    if (M <= 0 || N <= 0 || K <= 0) return;
+    if (!A || !B || !C) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    if (lda < K || ldb < N || ldc < N)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "leading dimension smaller than the row length");
+    const int prec = resolve_precision(precision);
+    DeviceCtx& c = current_ctx();
+    cudaStream_t s = as_stream(stream);
+    const GemmPlan p = gemm_plan(M, N, K, A, lda, true, B, ldb, false, prec);
+    void* ws = dev_scratch(c, p.ws_bytes, s);
+    gemm_run(p, A, lda, true, B, ldb, false, C, ldc, alpha, beta, nullptr, ws, c.status,
+             c.num_sms, s);
+    ATTNB_CUDA(cudaGetLastError());
+  });
+}
+
+int attnb_linear_dev(const float* x, int ldx, const float* W, int ldw, const float* b, float* y,
+                     int ldy, int T, int N, int K, int precision, void* stream) {
+  return guarded([&] {
+    if (T <= 0 || N <= 0 || K <= 0) return;
+    if (!x || !W || !y) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    if (ldx < K || ldw < K || ldy < N)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "leading dimension smaller than the row length");
+    const int prec = resolve_precision(precision);
+    DeviceCtx& c = current_ctx();
+    cudaStream_t s = as_stream(stream);
+    const GemmPlan p = gemm_plan(T, N, K, x, ldx, true, W, ldw, true, prec);
+    void* ws = dev_scratch(c, p.ws_bytes, s);
+    gemm_run(p, x, ldx, true, W, ldw, true, y, ldy, 1.f, 0.f, b, ws, c.status, c.num_sms, s);
+    ATTNB_CUDA(cudaGetLastError());
+  });
+}
+
+static int sgemm_host(const float* A, int M, int K, const float* B, int N, float* C, float alpha,
+                      float beta, int precision) {
+  return guarded([&] {
+    if (M <= 0 || N <= 0 || K <= 0) return;
+    if (!A || !B || !C) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    const int prec = resolve_precision(precision);
+    with_host_ctx([&](DeviceCtx& c) {
+      cudaStream_t s = c.stream;
+      const size_t a = (size_t)M * K, b = (size_t)K * N, cc = (size_t)M * N;
+      const bool read_c = (beta != 0.f);
+      Carver cv;
+      const size_t oa = cv.take(a * 4), ob = cv.take(b * 4), oc = cv.take(cc * 4);
+      const size_t io = cv.take(0);
+      char* base = static_cast<char*>(c.io.ensure(io, s));
+      float* dA = reinterpret_cast<float*>(base + oa);
+      float* dB = reinterpret_cast<float*>(base + ob);
+      float* dC = reinterpret_cast<float*>(base + oc);
+      const GemmPlan p = gemm_plan(M, N, K, dA, K, true, dB, N, false, prec);
+      void* ws = c.scratch_host_path.ensure(p.ws_bytes + 256, s);
+      if (alpha != 0.f) {
+        ATTNB_CUDA(cudaMemcpyAsync(dA, A, a * 4, cudaMemcpyHostToDevice, s));
+        ATTNB_CUDA(cudaMemcpyAsync(dB, B, b * 4, cudaMemcpyHostToDevice, s));
+      }
+      if (read_c) ATTNB_CUDA(cudaMemcpyAsync(dC, C, cc * 4, cudaMemcpyHostToDevice, s));
+      gemm_run(p, dA, K, true, dB, N, false, dC, N, alpha, beta, nullptr, ws, c.status,
+               c.num_sms, s);
+      ATTNB_CUDA(cudaMemcpyAsync(C, dC, cc * 4, cudaMemcpyDeviceToHost, s));
+      finish_host_call(c);
+    });
+  });
+}
+
+int attnb_sgemm(const float* A, int M, int K, const float* B, int N, float* C, float alpha,
+                float beta, int precision) {
+  return sgemm_host(A, M, K, B, N, C, alpha, beta, precision);
+}
+
+int attnb_gemm_jit(const float* A, int M, int K, const float* B, int N, float* C, float alpha,
+                   float beta, int precision) {
+  return sgemm_host(A, M, K, B, N, C, alpha, beta, precision);
+}
+
+// --------------------------------------------------------------- decode step
+int attnb_attn_step_dense_dev(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
+                              attnb_mtensor* O, void* stream) {
+  return guarded([&] {
+    validate_step(Q, K, V, O);
+    DeviceCtx& c = current_ctx();
+    step_dev(Q, K, V, O, c, as_stream(stream), nullptr, 0);
+  });
+}
+
+int attnb_attn_step_dense(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
+                          attnb_mtensor* O) {
+  return guarded([&] {
+    validate_step(Q, K, V, O);
+    with_host_ctx([&](DeviceCtx& c) {
+      cudaStream_t s = c.stream;
+      const Span sq = span_of(Q->H, 1, Q->Dh, Q->strideH, 0, Q->strideDh);
+      const Span sk = span_of(K->H, K->T, K->Dh, K->strideH, K->strideT, K->strideDh);
+      const Span sv = span_of(V->H, V->T, V->Dh, V->strideH, V->strideT, V->strideDh);
+      const Span so = span_of(O->H, 1, O->Dh, O->strideH, 0, O->strideDh);
+      Carver cv;
+      const size_t oq = cv.take(sq.count() * 4), ok = cv.take(sk.count() * 4),
+                   ov = cv.take(sv.count() * 4), oo = cv.take(so.count() * 4);
+      char* base = static_cast<char*>(c.io.ensure(cv.take(0), s));
+      auto put = [&](const float* host, const Span& sp, size_t off) {
+        ATTNB_CUDA(cudaMemcpyAsync(base + off, host + sp.lo, sp.count() * 4,
+                                   cudaMemcpyHostToDevice, s));
+        return reinterpret_cast<float*>(base + off) - sp.lo;
+      };
+      attnb_tensor dq = *Q, dk = *K, dv = *V;
+      attnb_mtensor dO = *O;
+      dq.data = put(Q->data, sq, oq);
+      dk.data = put(K->data, sk, ok);
+      dv.data = put(V->data, sv, ov);
+      // Strided outputs with holes keep the caller's bytes between elements.
+      if (so.count() != (int64_t)O->H * O->Dh) put(O->data, so, oo);
+      dO.data = reinterpret_cast<float*>(base + oo) - so.lo;
+      const View3 q = view(&dq, 1), k = view(&dk, dk.T), v = view(&dv, dv.T);
+      const DecodePlan p = decode_plan(q, k, v, c.num_sms);
+      void* ws = c.scratch_host_path.ensure(decode_workspace_bytes(p, K->H, K->Dh) + 256, s);
+      decode_launch(p, q, k, v, mview(&dO, 1), ws, s);
+      ATTNB_CUDA(cudaMemcpyAsync(O->data + so.lo, base + oo, so.count() * 4,
+                                 cudaMemcpyDeviceToHost, s));
+      finish_host_call(c);
+    });
+  });
+}
+
+// ------------------------------------------------------------------- prefill
+int attnb_attn_block_dense_dev(const attnb_tensor* Q, const attnb_tensor* K,
+                               const attnb_tensor* V, attnb_mtensor* O, int causal, int precision,
+                               void* stream) {
+  return guarded([&] {
+    validate_block(Q, K, V, O, causal);
+    const int prec = resolve_precision(precision);
+    block_dev(Q, K, V, O, causal, prec, as_stream(stream));
+  });
+}
+
+int attnb_attn_block_dense(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
+                           attnb_mtensor* O, int causal, int precision) {
+  return guarded([&] {
+    validate_block(Q, K, V, O, causal);
+    const int prec = resolve_precision(precision);
+    if (Q->T == 0) return;
+    with_host_ctx([&](DeviceCtx& c) {
+      cudaStream_t s = c.stream;
+      const Span sq = span_of(Q->H, Q->T, Q->Dh, Q->strideH, Q->strideT, Q->strideDh);
+      const Span sk = span_of(K->H, K->T, K->Dh, K->strideH, K->strideT, K->strideDh);
+      const Span sv = span_of(V->H, V->T, V->Dh, V->strideH, V->strideT, V->strideDh);
+      const Span so = span_of(O->H, O->T, O->Dh, O->strideH, O->strideT, O->strideDh);
+      Carver cv;
+      const size_t oq = cv.take(sq.count() * 4), ok = cv.take(sk.count() * 4),
+                   ov = cv.take(sv.count() * 4), oo = cv.take(so.count() * 4);
+      char* base = static_cast<char*>(c.io.ensure(cv.take(0), s));
+      auto put = [&](const float* host, const Span& sp, size_t off) {
+        ATTNB_CUDA(cudaMemcpyAsync(base + off, host + sp.lo, sp.count() * 4,
+                                   cudaMemcpyHostToDevice, s));
+        return reinterpret_cast<float*>(base + off) - sp.lo;
+      };
+      attnb_tensor dq = *Q, dk = *K, dv = *V;
+      attnb_mtensor dO = *O;
+      dq.data = put(Q->data, sq, oq);
+      dk.data = put(K->data, sk, ok);
+      dv.data = put(V->data, sv, ov);
+      if (so.count() != (int64_t)O->H * O->T * O->Dh) put(O->data, so, oo);
+      dO.data = reinterpret_cast<float*>(base + oo) - so.lo;
+      block_dev(&dq, &dk, &dv, &dO, causal, prec, s);
+      ATTNB_CUDA(cudaMemcpyAsync(O->data + so.lo, base + oo, so.count() * 4,
+                                 cudaMemcpyDeviceToHost, s));
+      finish_host_call(c);
+    });
+  });
+}
+
+// ------------------------------------------------------------------------ MHA
+int attnb_mha_block_dense_dev(const float* x, int batch, int T, int D, const float* W_in,
+                              const float* b_in, const float* W_out, const float* b_out, int H,
+                              int causal, float* y, int precision, void* stream) {
+  return guarded([&] {
+    validate_mha(x, T, D, W_in, b_in, W_out, b_out, H, y);
+    if (batch < 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "batch must be non-negative");
+    const int prec = resolve_precision(precision);
+    DeviceCtx& c = current_ctx();
+    mha_dev(x, batch, T, D, W_in, b_in, W_out, b_out, H, causal, y, prec, c, as_stream(stream));
+    ATTNB_CUDA(cudaGetLastError());
+  });
+}
+
+int attnb_mha_block_dense(const float* x, int T, int D, const float* W_in, const float* b_in,
+                          const float* W_out, const float* b_out, int H, int causal, float* y,
+                          int precision) {
+  return guarded([&] {
+    validate_mha(x, T, D, W_in, b_in, W_out, b_out, H, y);
+    const int prec = resolve_precision(precision);
+    if (T == 0) return;
+    with_host_ctx([&](DeviceCtx& c) {
+      cudaStream_t s = c.stream;
+      const size_t nx = (size_t)T * D, nwi = (size_t)3 * D * D, nbi = 3 * (size_t)D,
+                   nwo = (size_t)D * D, nbo = D;
+      Carver cv;
+      const size_t ox = cv.take(nx * 4), owi = cv.take(nwi * 4), obi = cv.take(nbi * 4),
+                   owo = cv.take(nwo * 4), obo = cv.take(nbo * 4), oy = cv.take(nx * 4);
+      char* base = static_cast<char*>(c.io.ensure(cv.take(0), s));
+      auto put = [&](const float* host, size_t n, size_t off) {
+        ATTNB_CUDA(cudaMemcpyAsync(base + off, host, n * 4, cudaMemcpyHostToDevice, s));
+        return reinterpret_cast<const float*>(base + off);
+      };
+      const float* dx = put(x, nx, ox);
+      const float* dwi = put(W_in, nwi, owi);
+      const float* dbi = put(b_in, nbi, obi);
+      const float* dwo = put(W_out, nwo, owo);
+      const float* dbo = put(b_out, nbo, obo);
+      float* dy = reinterpret_cast<float*>(base + oy);
+      mha_dev(dx, 1, T, D, dwi, dbi, dwo, dbo, H, causal, dy, prec, c, s);
+      ATTNB_CUDA(cudaMemcpyAsync(y, dy, nx * 4, cudaMemcpyDeviceToHost, s));
+      finish_host_call(c);
+    });
+  });
+}
+
+}  // extern "C"

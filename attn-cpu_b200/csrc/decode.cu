@@ -1,0 +1,309 @@
+// decode.cu -- K4: the M=1 decode step (attn::attn_step_dense) on CUDA cores.
+//
+// Reference: src/attn_dense.cpp:21-73 computes, per head, an exact two-pass
+// softmax over T keys (logits + max, then exp / sum / V-mix / 1/sum).  The same
+// function is computed here as a split-KV online softmax, the running (m, l)
+// update of include/online_softmax.h:8-17:
+//
+//   * the grid is (nsplit, H): each CTA streams one contiguous key range of one
+//     head; each warp takes U keys per step with 128-bit loads (one float4 of
+//     K and of V per lane per key), reduces the U dot products with butterfly
+//     shuffles and folds them into its running max m, sum l and accumulator;
+//   * the warps of a CTA merge (m, l, acc) through shared memory;
+//   * with nsplit > 1 each CTA writes its partial (m, l, acc) to scratch and a
+//     second tiny kernel merges the splits: m = max m_s,
+//     O = sum_s 2^(m_s - m) acc_s / sum_s 2^(m_s - m) l_s.
+//
+// Logits are kept in base-2 units (q is pre-scaled by log2(e)/sqrt(Dh)) so the
+// exponentials are single ex2 instructions.  The path is HBM-bound: it moves
+// K and V once (2*H*T*Dh*4 bytes) plus q and o.
+#include <algorithm>
+#include <cmath>
+#include <cstdlib>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace attnb {
+namespace {
+
+constexpr int kThreads = 256;  // 8 warps per CTA
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Merge the per-warp (m, l, acc[Dh]) of the CTA held in shared memory and
+// write either the final output (nsplit == 1) or the split's partial.
+__device__ void cta_merge_and_store(const float* sm_m, const float* sm_l, const float* sm_acc,
+                                    int nwarps, int Dh, float* out_final, int64_t osD,
+                                    float* part_o, float2* part_ml) {
+  float M = -INFINITY;
+  for (int w = 0; w < nwarps; ++w) M = fmaxf(M, sm_m[w]);
+  float L = 0.f;
+  for (int w = 0; w < nwarps; ++w) L += (sm_m[w] == -INFINITY) ? 0.f : fast_exp2(sm_m[w] - M) * sm_l[w];
+  for (int d = threadIdx.x; d < Dh; d += blockDim.x) {
+    float o = 0.f;
+    for (int w = 0; w < nwarps; ++w)
+      if (sm_m[w] != -INFINITY) o += fast_exp2(sm_m[w] - M) * sm_acc[w * Dh + d];
+    if (out_final) out_final[d * osD] = o / L;
+    else part_o[d] = o;
+  }
+  if (!out_final && threadIdx.x == 0) *part_ml = make_float2(M, L);
+}
+
+// Vector path: NV float4 per lane covers Dh <= 128 * NV; U keys per warp step.
+template <int NV, int U>
+__global__ void __launch_bounds__(kThreads, 2) decode_vec_kernel(
+    const float* __restrict__ Q, int64_t qsH, const float* __restrict__ K, int64_t ksH,
+    int64_t ksT, const float* __restrict__ V, int64_t vsH, int64_t vsT, int T, int Dh,
+    int keys_per_split, float qscale, float* __restrict__ O, int64_t osH, int64_t osD,
+    float* __restrict__ part_o, float2* __restrict__ part_ml) {
+  extern __shared__ float smem[];
+  const int nwarps = kThreads / 32;
+  float* sm_m = smem;
+  float* sm_l = smem + nwarps;
+  float* sm_acc = smem + 2 * nwarps;
+
+  const int split = blockIdx.x, h = blockIdx.y, nsplit = gridDim.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int Dh4 = Dh >> 2;
+  const int t_begin = split * keys_per_split;
+  const int t_end = min(T, t_begin + keys_per_split);
+
+  float4 q[NV];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int i = lane + 32 * v;
+    float4 x = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (i < Dh4) x = *reinterpret_cast<const float4*>(Q + h * qsH + 4 * i);
+    q[v] = make_float4(x.x * qscale, x.y * qscale, x.z * qscale, x.w * qscale);
+  }
+  const float* Kh = K + h * ksH;
+  const float* Vh = V + h * vsH;
+
+  float m = -INFINITY, l = 0.f;
+  float4 acc[NV];
+#pragma unroll
+  for (int v = 0; v < NV; ++v) acc[v] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+  for (int t0 = t_begin + warp * U; t0 < t_end; t0 += nwarps * U) {
+    float4 kr[U][NV], vr[U][NV];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const bool ok = (t0 + u) < t_end;
+      const float* kp = Kh + (int64_t)(t0 + u) * ksT;
+      const float* vp = Vh + (int64_t)(t0 + u) * vsT;
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        const int i = lane + 32 * v;
+        if (ok && i < Dh4) {
+          kr[u][v] = __ldg(reinterpret_cast<const float4*>(kp + 4 * i));
+          vr[u][v] = __ldg(reinterpret_cast<const float4*>(vp + 4 * i));
+        } else {
+          kr[u][v] = make_float4(0.f, 0.f, 0.f, 0.f);
+          vr[u][v] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+    }
+    float s[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      float p = 0.f;
+#pragma unroll
+      for (int v = 0; v < NV; ++v)
+        p += q[v].x * kr[u][v].x + q[v].y * kr[u][v].y + q[v].z * kr[u][v].z + q[v].w * kr[u][v].w;
+      s[u] = warp_sum(p);
+      if (t0 + u >= t_end) s[u] = -INFINITY;
+    }
+    float bm = s[0];
+#pragma unroll
+    for (int u = 1; u < U; ++u) bm = fmaxf(bm, s[u]);
+    const float m_new = fmaxf(m, bm);  // s[0] is a valid key, so m_new is finite
+    const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
+    l *= alpha;
+#pragma unroll
+    for (int v = 0; v < NV; ++v) {
+      acc[v].x *= alpha; acc[v].y *= alpha; acc[v].z *= alpha; acc[v].w *= alpha;
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const float p = (s[u] == -INFINITY) ? 0.f : fast_exp2(s[u] - m_new);
+      l += p;
+#pragma unroll
+      for (int v = 0; v < NV; ++v) {
+        acc[v].x = fmaf(p, vr[u][v].x, acc[v].x);
+        acc[v].y = fmaf(p, vr[u][v].y, acc[v].y);
+        acc[v].z = fmaf(p, vr[u][v].z, acc[v].z);
+        acc[v].w = fmaf(p, vr[u][v].w, acc[v].w);
+      }
+    }
+    m = m_new;
+  }
+
+  if (lane == 0) {
+    sm_m[warp] = m;
+    sm_l[warp] = l;
+  }
+#pragma unroll
+  for (int v = 0; v < NV; ++v) {
+    const int i = lane + 32 * v;
+    if (i < Dh4) *reinterpret_cast<float4*>(sm_acc + warp * Dh + 4 * i) = acc[v];
+  }
+  __syncthreads();
+  const size_t pidx = (size_t)h * nsplit + split;
+  cta_merge_and_store(sm_m, sm_l, sm_acc, nwarps, Dh, nsplit == 1 ? O + h * osH : nullptr, osD,
+                      part_o ? part_o + pidx * Dh : nullptr, part_ml ? part_ml + pidx : nullptr);
+}
+
+// Any strides / head size: scores of the key range go to shared memory, then
+// one exact softmax over the range (this is the reference's two-pass order).
+__global__ void __launch_bounds__(kThreads) decode_generic_kernel(
+    const float* __restrict__ Q, int64_t qsH, int64_t qsD, const float* __restrict__ K,
+    int64_t ksH, int64_t ksT, int64_t ksD, const float* __restrict__ V, int64_t vsH,
+    int64_t vsT, int64_t vsD, int T, int Dh, int keys_per_split, float qscale,
+    float* __restrict__ O, int64_t osH, int64_t osD, float* __restrict__ part_o,
+    float2* __restrict__ part_ml) {
+  extern __shared__ float smem[];
+  float* sc = smem;  // keys_per_split scores
+  __shared__ float red[32];
+  __shared__ float s_max, s_sum;
+
+  const int split = blockIdx.x, h = blockIdx.y, nsplit = gridDim.x;
+  const int t_begin = split * keys_per_split;
+  const int n = min(T, t_begin + keys_per_split) - t_begin;
+  const float* q = Q + h * qsH;
+
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const float* kr = K + h * ksH + (int64_t)(t_begin + j) * ksT;
+    float dot = 0.f;
+    for (int d = 0; d < Dh; ++d) dot = fmaf(q[d * qsD], kr[d * ksD], dot);
+    sc[j] = dot * qscale;
+  }
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) mx = fmaxf(mx, sc[j]);
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = -INFINITY;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v = fmaxf(v, red[w]);
+    s_max = v;
+  }
+  __syncthreads();
+  const float M = s_max;
+  float sum = 0.f;
+  for (int j = threadIdx.x; j < n; j += blockDim.x) {
+    const float p = fast_exp2(sc[j] - M);
+    sc[j] = p;
+    sum += p;
+  }
+  sum = warp_sum(sum);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = sum;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float v = 0.f;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) v += red[w];
+    s_sum = v;
+  }
+  __syncthreads();
+  const float L = s_sum;
+  const size_t pidx = (size_t)h * nsplit + split;
+  for (int d = threadIdx.x; d < Dh; d += blockDim.x) {
+    float o = 0.f;
+    const float* vc = V + h * vsH + (int64_t)t_begin * vsT + d * vsD;
+    for (int j = 0; j < n; ++j) o = fmaf(sc[j], vc[(int64_t)j * vsT], o);
+    if (nsplit == 1) O[h * osH + d * osD] = o / L;
+    else part_o[pidx * Dh + d] = o;
+  }
+  if (nsplit > 1 && threadIdx.x == 0) part_ml[pidx] = make_float2(M, L);
+}
+
+// Merge the nsplit partials of each head.
+__global__ void decode_merge_kernel(const float* __restrict__ part_o,
+                                    const float2* __restrict__ part_ml, int nsplit, int Dh,
+                                    float* __restrict__ O, int64_t osH, int64_t osD) {
+  const int h = blockIdx.x;
+  const float2* ml = part_ml + (size_t)h * nsplit;
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[s].x);
+  float L = 0.f;
+  for (int s = 0; s < nsplit; ++s) L += fast_exp2(ml[s].x - M) * ml[s].y;
+  const float invL = 1.f / L;
+  for (int d = threadIdx.x; d < Dh; d += blockDim.x) {
+    float o = 0.f;
+    for (int s = 0; s < nsplit; ++s)
+      o += fast_exp2(ml[s].x - M) * part_o[((size_t)h * nsplit + s) * Dh + d];
+    O[h * osH + d * osD] = o * invL;
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+DecodePlan decode_plan(const View3& Q, const View3& K, const View3& V, int num_sms) {
+  DecodePlan p{};
+  const int H = K.H, T = K.T, Dh = K.Dh;
+  p.fast = Q.sD == 1 && K.sD == 1 && V.sD == 1 && Dh % 4 == 0 && Dh <= 256 &&
+           aligned16(Q.data) && aligned16(K.data) && aligned16(V.data) && Q.sH % 4 == 0 &&
+           K.sH % 4 == 0 && K.sT % 4 == 0 && V.sH % 4 == 0 && V.sT % 4 == 0;
+  // About eight CTAs per SM over all heads (a few waves of equal ranges); each
+  // split keeps at least 64 keys so the merge stays cheap.
+  int per_sm = 8;
+  if (const char* e = std::getenv("ATTNB_DECODE_CTAS_PER_SM")) per_sm = std::max(1, std::atoi(e));
+  const int slots = std::max(1, num_sms) * per_sm;
+  int ns = std::max(1, slots / std::max(1, H));
+  ns = std::min(ns, std::max(1, (T + 63) / 64));
+  int kps = (T + ns - 1) / ns;
+  if (!p.fast) kps = std::min(kps, 2048);  // generic path keeps a range's scores in smem
+  kps = std::max(kps, 1);
+  p.keys_per_split = kps;
+  p.nsplit = (T + kps - 1) / kps;
+  return p;
+}
+
+size_t decode_workspace_bytes(const DecodePlan& p, int H, int Dh) {
+  if (p.nsplit <= 1) return 0;
+  const size_t n = (size_t)H * p.nsplit;
+  return n * Dh * sizeof(float) + n * sizeof(float2) + 256;
+}
+
+void decode_launch(const DecodePlan& p, const View3& Q, const View3& K, const View3& V,
+                   const MView3& O, void* ws, cudaStream_t stream) {
+  const int H = K.H, T = K.T, Dh = K.Dh;
+  const float qscale = kLog2e / std::sqrt(static_cast<float>(Dh));
+  float* part_o = nullptr;
+  float2* part_ml = nullptr;
+  if (p.nsplit > 1) {
+    part_o = static_cast<float*>(ws);
+    const size_t off = (((size_t)H * p.nsplit * Dh * sizeof(float)) + 255) & ~size_t(255);
+    part_ml = reinterpret_cast<float2*>(static_cast<char*>(ws) + off);
+  }
+  const dim3 grid(p.nsplit, H);
+  if (p.fast) {
+    const size_t sm = (2 * (kThreads / 32) + (kThreads / 32) * Dh) * sizeof(float);
+    if (Dh <= 128)
+      decode_vec_kernel<1, 8><<<grid, kThreads, sm, stream>>>(
+          Q.data, Q.sH, K.data, K.sH, K.sT, V.data, V.sH, V.sT, T, Dh, p.keys_per_split, qscale,
+          O.data, O.sH, O.sD, part_o, part_ml);
+    else
+      decode_vec_kernel<2, 4><<<grid, kThreads, sm, stream>>>(
+          Q.data, Q.sH, K.data, K.sH, K.sT, V.data, V.sH, V.sT, T, Dh, p.keys_per_split, qscale,
+          O.data, O.sH, O.sD, part_o, part_ml);
+  } else {
+    const size_t sm = (size_t)p.keys_per_split * sizeof(float);
+    decode_generic_kernel<<<grid, kThreads, sm, stream>>>(
+        Q.data, Q.sH, Q.sD, K.data, K.sH, K.sT, K.sD, V.data, V.sH, V.sT, V.sD, T, Dh,
+        p.keys_per_split, qscale, O.data, O.sH, O.sD, part_o, part_ml);
+  }
+  if (p.nsplit > 1)
+    decode_merge_kernel<<<H, 128, 0, stream>>>(part_o, part_ml, p.nsplit, Dh, O.data, O.sH, O.sD);
+}
+
+}  // namespace attnb

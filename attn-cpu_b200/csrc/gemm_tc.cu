@@ -1,0 +1,390 @@
+// gemm_tc.cu -- K1: persistent tcgen05 SGEMM (kind::tf32, 1xTF32 or 3xTF32).
+//
+// Computes C[M,N] = alpha * A.B^T' + beta * C (+ bias[n]) where both operands
+// arrive K-major in HBM: A as [M, K] rows, B as [N, K] rows (split.cu packs
+// them, or they are used in place when already K-major and 16-byte aligned).
+// It replaces the reference's FMA micro-kernels: src/gemm.cpp:89-249
+// (8x48 register tiles over KC=768 panels), src/jit_gemm.cpp:256-406 (JIT
+// 8xNR tiles) and include/gemm_16x16.h:7-60 (bias-initialised row GEMM of the
+// MHA projections).  Accumulation is fp32 in tensor memory over the whole K.
+//
+// Structure (one CTA per SM, persistent over 128 x BN output tiles):
+//   warp 0      TMA producer: fills a STAGES-deep shared-memory ring with
+//               128-byte-swizzled 32-wide K slices of A (and B), signalling
+//               `full[s]` with the transaction byte count;
+//   warp 1      allocates 2*BN TMEM columns (two accumulators), then one
+//               lane issues tcgen05.mma (4 K-steps of 8 per slice, x3 terms
+//               in 3xTF32 mode) and tcgen05.commit's the slice back to the
+//               producer (`empty[s]`) and the finished tile to the epilogue;
+//   warps 2-5   epilogue: tcgen05.ld the accumulator (lane = row), apply
+//               alpha / beta / bias, store to C, release the accumulator.
+// Two accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
+#include <algorithm>
+#include <atomic>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "runtime.h"
+
+namespace attnb {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 32;  // fp32 elements per 128-byte swizzle row
+constexpr int kThreads = 192;
+constexpr int GROUP_M = 16;
+
+template <int BN, bool SPLIT3>
+struct GemmCfg {
+  static constexpr int A_BYTES = BM * BK * 4;                 // 16 KB
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int STAGE_BYTES = (SPLIT3 ? 2 : 1) * (A_BYTES + B_BYTES);
+  static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;    // + alignment slack
+  static constexpr int TMEM_COLS = 2 * BN;
+  static_assert(STAGES >= 2, "pipeline needs two stages");
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
+  const int per_group = GROUP_M * tiles_n;
+  const int group = tile / per_group;
+  const int first_m = group * GROUP_M;
+  const int gsize = min(tiles_m - first_m, GROUP_M);
+  const int r = tile % per_group;
+  tm = first_m + r % gsize;
+  tn = r / gsize;
+}
+
+// Wait without the abort short-cut: used to drain copies that are in flight.
+__device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity, int* status) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > ATTNB_WAIT_LIMIT_NS) {
+      raise_timeout(status);
+      return;
+    }
+  }
+}
+
+template <int BN, bool SPLIT3>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA_hi,
+                   const __grid_constant__ CUtensorMap tmA_lo,
+                   const __grid_constant__ CUtensorMap tmB_hi,
+                   const __grid_constant__ CUtensorMap tmB_lo, int M, int N, int Kp,
+                   float* __restrict__ C, int64_t ldc, float alpha, float beta,
+                   const float* __restrict__ bias, int* status) {
+  using Cfg = GemmCfg<BN, SPLIT3>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar[2], tempty_bar[2], final_bar;
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t tiles_base = (smem_addr(smem_raw) + 1023u) & ~1023u;
+  auto sA_hi = [&](int s) { return tiles_base + s * Cfg::STAGE_BYTES; };
+  auto sA_lo = [&](int s) { return tiles_base + s * Cfg::STAGE_BYTES + Cfg::A_BYTES; };
+  auto sB_hi = [&](int s) {
+    return tiles_base + s * Cfg::STAGE_BYTES + (SPLIT3 ? 2 : 1) * Cfg::A_BYTES;
+  };
+  auto sB_lo = [&](int s) {
+    return tiles_base + s * Cfg::STAGE_BYTES + 2 * Cfg::A_BYTES + Cfg::B_BYTES;
+  };
+
+  const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
+  const int num_tiles = tiles_m * tiles_n;
+  const int num_kb = Kp / BK;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_addr(&full_bar[s]), 1);
+      mbar_init(smem_addr(&empty_bar[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_addr(&tfull_bar[b]), 1);
+      mbar_init(smem_addr(&tempty_bar[b]), 4);
+    }
+    mbar_init(smem_addr(&final_bar), 1);
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA_hi);
+    tma_prefetch_desc(&tmB_hi);
+    if (SPLIT3) {
+      tma_prefetch_desc(&tmA_lo);
+      tma_prefetch_desc(&tmB_lo);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(&tmem_base_slot), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = tmem_base_slot;
+  volatile int* abort_p = &abort_flag;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        int tm, tn;
+        tile_coords(tile, tiles_m, tiles_n, tm, tn);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(smem_addr(&empty_bar[stage]), phase ^ 1u, abort_p, status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_addr(&full_bar[stage]);
+          mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
+          tma_load_2d(sA_hi(stage), &tmA_hi, fb, kb * BK, tm * BM);
+          tma_load_2d(sB_hi(stage), &tmB_hi, fb, kb * BK, tn * BN);
+          if (SPLIT3) {
+            tma_load_2d(sA_lo(stage), &tmA_lo, fb, kb * BK, tm * BM);
+            tma_load_2d(sB_lo(stage), &tmB_lo, fb, kb * BK, tn * BN);
+          }
+          issued_mask |= 1u << stage;
+          issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Copies still in flight (only possible after an abort) land before exit.
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_mask & (1u << s))
+          mbar_drain(smem_addr(&full_bar[s]), (issued_parity >> s) & 1u, status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t use = (it >> 1) & 1;
+        if (!mbar_wait(smem_addr(&tempty_bar[buf]), use ^ 1u, abort_p, status)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + buf * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(smem_addr(&full_bar[stage]), phase, abort_p, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            const uint64_t a_hi = sdesc_kmajor_sw128(sA_hi(stage) + kk * 32);
+            const uint64_t b_hi = sdesc_kmajor_sw128(sB_hi(stage) + kk * 32);
+            mma_tf32(d_tmem, a_hi, b_hi, IDESC, (kb | kk) != 0 ? 1u : 0u);
+            if (SPLIT3) {
+              const uint64_t a_lo = sdesc_kmajor_sw128(sA_lo(stage) + kk * 32);
+              const uint64_t b_lo = sdesc_kmajor_sw128(sB_lo(stage) + kk * 32);
+              mma_tf32(d_tmem, a_hi, b_lo, IDESC, 1u);
+              mma_tf32(d_tmem, a_lo, b_hi, IDESC, 1u);
+            }
+          }
+          mma_commit(smem_addr(&empty_bar[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (ok) mma_commit(smem_addr(&tfull_bar[buf]));
+      }
+      // Every MMA issued above has finished before TMEM is released.
+      mma_commit(smem_addr(&final_bar));
+      mbar_drain(smem_addr(&final_bar), 0, status);
+    }
+  } else {
+    // -------------------------------------------------------------- epilogue
+    const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    const bool c_vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      int tm, tn;
+      tile_coords(tile, tiles_m, tiles_n, tm, tn);
+      const int buf = it & 1;
+      const uint32_t use = (it >> 1) & 1;
+      if (!mbar_wait(smem_addr(&tfull_bar[buf]), use, abort_p, status)) break;
+      tc_fence_after();
+      const int row = tm * BM + quarter * 32 + lane;
+      float* crow = C + (int64_t)row * ldc;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN + c * 32, r);
+        const int col0 = tn * BN + c * 32;
+        if (row < M) {
+          float v[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) v[j] = alpha * __uint_as_float(r[j]);
+          if (beta != 0.f) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < N) v[j] = fmaf(beta, crow[col0 + j], v[j]);
+          }
+          if (bias) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < N) v[j] += __ldg(bias + col0 + j);
+          }
+          if (c_vec && col0 + 32 <= N) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4)
+              *reinterpret_cast<float4*>(crow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (col0 + j < N) crow[col0 + j] = v[j];
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&tempty_bar[buf]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// C = beta * C (alpha == 0 path of the reference, src/gemm.cpp:328-336).
+__global__ void scale_c_kernel(float* C, int64_t ldc, int M, int N, float beta) {
+  const int64_t n = (int64_t)M * N;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / N, c = i % N;
+    float* p = C + r * ldc + c;
+    *p = (beta == 0.f) ? 0.f : *p * beta;
+  }
+}
+
+template <int BN, bool SPLIT3>
+void launch_gemm(const GemmPlan& p, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
+                 const CUtensorMap& b_hi, const CUtensorMap& b_lo, float* C, int64_t ldc,
+                 float alpha, float beta, const float* bias, int* status, int num_sms,
+                 cudaStream_t s) {
+  using Cfg = GemmCfg<BN, SPLIT3>;
+  static std::atomic<uint64_t> configured{0};  // one bit per device
+  int dev = 0;
+  ATTNB_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    ATTNB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT3>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    configured.fetch_or(bit);
+  }
+  const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+  const int grid = std::min(tiles, num_sms);
+  gemm_tc_kernel<BN, SPLIT3><<<grid, kThreads, Cfg::SMEM, s>>>(
+      a_hi, a_lo, b_hi, b_lo, p.M, p.N, p.Kp, C, ldc, alpha, beta, bias, status);
+  ATTNB_CUDA(cudaGetLastError());
+}
+
+}  // namespace
+
+int gemm_block_n(int precision) { return precision == ATTNB_PREC_TF32 ? 256 : 128; }
+
+GemmPlan gemm_plan(int M, int N, int K, const float* A, int64_t lda, bool a_kmajor,
+                   const float* B, int64_t ldb, bool b_kmajor, int precision) {
+  GemmPlan p{};
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.Kp = (K + BK - 1) / BK * BK;
+  p.split3 = precision != ATTNB_PREC_TF32;
+  // A 1xTF32 operand that is already K-major with a 16-byte-aligned base and
+  // pitch is read in place (the tensor core reads its tf32 part).
+  auto direct = [&](const float* X, int64_t ld, bool kmajor) {
+    return !p.split3 && kmajor && (reinterpret_cast<uintptr_t>(X) & 15u) == 0 && (ld % 4) == 0;
+  };
+  p.a_direct = direct(A, lda, a_kmajor);
+  p.b_direct = direct(B, ldb, b_kmajor);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  };
+  const size_t a_bytes = (size_t)M * p.Kp * sizeof(float);
+  const size_t b_bytes = (size_t)N * p.Kp * sizeof(float);
+  p.off_a_hi = p.a_direct ? 0 : take(a_bytes);
+  p.off_a_lo = p.split3 ? take(a_bytes) : 0;
+  p.off_b_hi = p.b_direct ? 0 : take(b_bytes);
+  p.off_b_lo = p.split3 ? take(b_bytes) : 0;
+  p.ws_bytes = off;
+  return p;
+}
+
+size_t gemm_workspace_bound(int M, int N, int K, int precision) {
+  const size_t kp = (size_t)(K + BK - 1) / BK * BK;
+  const size_t a = ((size_t)M * kp * sizeof(float) + 255) & ~size_t(255);
+  const size_t b = ((size_t)N * kp * sizeof(float) + 255) & ~size_t(255);
+  return (precision == ATTNB_PREC_TF32 ? 1 : 2) * (a + b);
+}
+
+void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, const float* B,
+              int64_t ldb, bool b_kmajor, float* C, int64_t ldc, float alpha, float beta,
+              const float* bias, void* ws, int* status, int num_sms, cudaStream_t s) {
+  if (p.M <= 0 || p.N <= 0 || p.K <= 0) return;
+  if (alpha == 0.f && bias == nullptr) {
+    if (beta != 1.f) {
+      const int64_t n = (int64_t)p.M * p.N;
+      const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms * 8);
+      scale_c_kernel<<<blocks, 256, 0, s>>>(C, ldc, p.M, p.N, beta);
+    }
+    return;
+  }
+  char* w = static_cast<char*>(ws);
+  const float* a_hi = p.a_direct ? A : reinterpret_cast<float*>(w + p.off_a_hi);
+  const float* b_hi = p.b_direct ? B : reinterpret_cast<float*>(w + p.off_b_hi);
+  float* a_lo = p.split3 ? reinterpret_cast<float*>(w + p.off_a_lo) : nullptr;
+  float* b_lo = p.split3 ? reinterpret_cast<float*>(w + p.off_b_lo) : nullptr;
+  // Operand packing (tf32 rounding / hi-lo split, K-major, K padded to 32).
+  if (!p.a_direct) {
+    if (a_kmajor) pack_rows_launch(A, lda, p.M, p.K, p.Kp, const_cast<float*>(a_hi), a_lo, p.split3, s);
+    else pack_transpose_launch(A, lda, p.K, p.M, p.Kp, const_cast<float*>(a_hi), a_lo, p.split3, s);
+  }
+  if (!p.b_direct) {
+    if (b_kmajor) pack_rows_launch(B, ldb, p.N, p.K, p.Kp, const_cast<float*>(b_hi), b_lo, p.split3, s);
+    else pack_transpose_launch(B, ldb, p.K, p.N, p.Kp, const_cast<float*>(b_hi), b_lo, p.split3, s);
+  }
+  // Tensor maps: a direct operand keeps its own pitch and true K (the copy
+  // engine zero-fills past K); packed operands are [rows, Kp].
+  const int bn = p.split3 ? 128 : 256;
+  const CUtensorMap tA_hi = p.a_direct ? make_tmap_2d(a_hi, p.M, p.K, lda, BM, BK)
+                                       : make_tmap_2d(a_hi, p.M, p.Kp, p.Kp, BM, BK);
+  const CUtensorMap tB_hi = p.b_direct ? make_tmap_2d(b_hi, p.N, p.K, ldb, bn, BK)
+                                       : make_tmap_2d(b_hi, p.N, p.Kp, p.Kp, bn, BK);
+  if (p.split3) {
+    const CUtensorMap tA_lo = make_tmap_2d(a_lo, p.M, p.Kp, p.Kp, BM, BK);
+    const CUtensorMap tB_lo = make_tmap_2d(b_lo, p.N, p.Kp, p.Kp, bn, BK);
+    launch_gemm<128, true>(p, tA_hi, tA_lo, tB_hi, tB_lo, C, ldc, alpha, beta, bias, status,
+                           num_sms, s);
+  } else {
+    launch_gemm<256, false>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias, status,
+                            num_sms, s);
+  }
+}
+
+}  // namespace attnb

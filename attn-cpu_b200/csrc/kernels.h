@@ -1,0 +1,66 @@
+// kernels.h -- host-side launch interface of the device kernels.  Everything
+// here takes device pointers and a stream; validation happens in capi.cu.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace attnb {
+
+// Strided fp32 view [H, T, Dh] (strides in elements).
+struct View3 {
+  const float* data;
+  int H, T, Dh;
+  int64_t sH, sT, sD;
+};
+struct MView3 {
+  float* data;
+  int H, T, Dh;
+  int64_t sH, sT, sD;
+};
+
+// ------------------------------------------------------------ decode (K4)
+// Split-KV plan for one decode step: how many key ranges each head is cut
+// into and how long each range is.
+struct DecodePlan {
+  int nsplit;
+  int keys_per_split;
+  bool fast;  // 128-bit vector path (strideDh == 1, 16-byte aligned rows, Dh % 4 == 0, Dh <= 256)
+};
+DecodePlan decode_plan(const View3& Q, const View3& K, const View3& V, int num_sms);
+// Scratch bytes the plan needs (0 when nsplit == 1).
+size_t decode_workspace_bytes(const DecodePlan& p, int H, int Dh);
+// O[h, :] for every head; `ws` holds decode_workspace_bytes(p, ...) bytes.
+void decode_launch(const DecodePlan& p, const View3& Q, const View3& K, const View3& V,
+                   const MView3& O, void* ws, cudaStream_t stream);
+
+// ------------------------------------------- generic prefill (CUDA cores)
+// O[h,l,:] for any strides and head size; exact fp32 online softmax.
+void attn_block_simt_launch(const View3& Q, const View3& K, const View3& V, const MView3& O,
+                            bool causal, cudaStream_t stream);
+
+// ------------------------------------------------ operand packing (K2)
+// src[rows, cols] (pitch ld) -> hi/lo[rows, kp]; cols..kp-1 zero.
+void pack_rows_launch(const float* src, int64_t ld, int rows, int cols, int kp, float* hi,
+                      float* lo, bool split3, cudaStream_t s);
+// src[K, N] (pitch ld) -> hi/lo[N, kp] (transposed); K..kp-1 zero.
+void pack_transpose_launch(const float* src, int64_t ld, int K, int N, int kp, float* hi,
+                           float* lo, bool split3, cudaStream_t s);
+
+// --------------------------------------------------- tcgen05 GEMM (K1)
+// C[M,N] = alpha * A.B + beta * C (+ bias[n]).  A is [M,K] (a_kmajor: rows of
+// K, pitch lda) or [K,M] (pitch lda); B is [N,K] (b_kmajor) or [K,N].
+struct GemmPlan {
+  int M, N, K, Kp;
+  bool split3, a_direct, b_direct;
+  size_t off_a_hi, off_a_lo, off_b_hi, off_b_lo, ws_bytes;
+};
+GemmPlan gemm_plan(int M, int N, int K, const float* A, int64_t lda, bool a_kmajor,
+                   const float* B, int64_t ldb, bool b_kmajor, int precision);
+// Scratch bytes of any plan of this size (no operand read in place).
+size_t gemm_workspace_bound(int M, int N, int K, int precision);
+void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, const float* B,
+              int64_t ldb, bool b_kmajor, float* C, int64_t ldc, float alpha, float beta,
+              const float* bias, void* ws, int* status, int num_sms, cudaStream_t s);
+
+}  // namespace attnb

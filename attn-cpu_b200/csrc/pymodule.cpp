@@ -1,0 +1,150 @@
+// pymodule.cpp -- the `_attn_cpu` extension module with the reference's
+// Python signatures (src/bindings.cpp:102-124 of the reference): arrays are
+// force-cast to C-contiguous float32, shapes are checked with the same
+// messages (src/bindings.cpp:17-39, 55-61), and a new output array is
+// returned.  It adds attn_step_dense / attn_block_dense, which the
+// reference's tests call (tests/test_attn_step.py:32, python/attn_cpu/mha_np.py:34)
+// but its module never exported, and an optional `precision` argument
+// (-1 default, 0 = 3xTF32, 1 = TF32).  Work runs on the current CUDA device
+// through the C ABI in attnb.h, with the GIL released.
+#include <pybind11/numpy.h>
+#include <pybind11/pybind11.h>
+
+#include <stdexcept>
+#include <string>
+
+#include "../../include/attnb.h"
+
+namespace py = pybind11;
+using farray = py::array_t<float, py::array::c_style | py::array::forcecast>;
+
+namespace {
+
+void rethrow(int rc) {
+  if (rc == ATTNB_OK) return;
+  const std::string msg = attnb_last_error();
+  if (rc == ATTNB_ERR_INVALID_ARGUMENT) throw std::invalid_argument(msg);
+  throw std::runtime_error(msg);
+}
+
+py::array_t<float> mha_block_dense_py(farray x, farray W_in, farray b_in, farray W_out,
+                                      farray b_out, int num_heads, bool causal, int precision) {
+  if (x.ndim() != 2) throw std::invalid_argument("x must be [T,D]");
+  if (W_in.ndim() != 2) throw std::invalid_argument("W_in must be [3D,D]");
+  if (b_in.ndim() != 1) throw std::invalid_argument("b_in must be [3D]");
+  if (W_out.ndim() != 2) throw std::invalid_argument("W_out must be [D,D]");
+  if (b_out.ndim() != 1) throw std::invalid_argument("b_out must be [D]");
+  const int T = (int)x.shape(0), D = (int)x.shape(1);
+  if ((int)W_in.shape(0) != 3 * D || (int)W_in.shape(1) != D)
+    throw std::invalid_argument("W_in shape must be [3D, D]");
+  if ((int)b_in.shape(0) != 3 * D) throw std::invalid_argument("b_in shape must be [3D]");
+  if ((int)W_out.shape(0) != D || (int)W_out.shape(1) != D)
+    throw std::invalid_argument("W_out shape must be [D, D]");
+  if ((int)b_out.shape(0) != D) throw std::invalid_argument("b_out shape must be [D]");
+  if (num_heads <= 0 || (D % num_heads) != 0)
+    throw std::invalid_argument("num_heads must divide D");
+  py::array_t<float> y({T, D});
+  const float *px = x.data(), *pwi = W_in.data(), *pbi = b_in.data(), *pwo = W_out.data(),
+              *pbo = b_out.data();
+  float* py_ = y.mutable_data();
+  int rc;
+  {
+    py::gil_scoped_release nogil;
+    rc = attnb_mha_block_dense(px, T, D, pwi, pbi, pwo, pbo, num_heads, causal ? 1 : 0, py_,
+                               precision);
+  }
+  rethrow(rc);
+  return y;
+}
+
+py::array_t<float> gemm_common(farray A, farray B, float alpha, float beta, int precision,
+                               bool jit) {
+  if (A.ndim() != 2 || B.ndim() != 2)
+    throw std::invalid_argument("A and B must be 2D: A[M,K], B[K,N]");
+  const int M = (int)A.shape(0), K = (int)A.shape(1), KB = (int)B.shape(0),
+            N = (int)B.shape(1);
+  if (K != KB) throw std::invalid_argument("Inner dim mismatch: A[M,K] x B[K,N]");
+  // Zero-initialised, so beta != 0 scales zeros (the reference reads an
+  // uninitialised buffer there, src/bindings.cpp:64-71).
+  py::array_t<float> C({M, N});
+  if ((size_t)M * N) std::fill(C.mutable_data(), C.mutable_data() + (size_t)M * N, 0.f);
+  const float *pa = A.data(), *pb = B.data();
+  float* pc = C.mutable_data();
+  int rc;
+  {
+    py::gil_scoped_release nogil;
+    rc = jit ? attnb_gemm_jit(pa, M, K, pb, N, pc, alpha, beta, precision)
+             : attnb_sgemm(pa, M, K, pb, N, pc, alpha, beta, precision);
+  }
+  rethrow(rc);
+  return C;
+}
+
+py::array_t<float> gemm_py(farray A, farray B, float alpha, float beta, int precision) {
+  return gemm_common(A, B, alpha, beta, precision, false);
+}
+py::array_t<float> gemm_jit_py(farray A, farray B, float alpha, float beta, int precision) {
+  return gemm_common(A, B, alpha, beta, precision, true);
+}
+
+py::array_t<float> attn_step_dense_py(farray Q, farray K, farray V) {
+  if (Q.ndim() != 2) throw std::invalid_argument("Q must be [H,Dh]");
+  if (K.ndim() != 3 || V.ndim() != 3) throw std::invalid_argument("K and V must be [H,T,Dh]");
+  const int H = (int)Q.shape(0), Dh = (int)Q.shape(1);
+  attnb_tensor q{Q.data(), H, 1, Dh, (int64_t)Dh, 0, 1};
+  attnb_tensor k{K.data(), (int)K.shape(0), (int)K.shape(1), (int)K.shape(2),
+                 (int64_t)K.shape(1) * K.shape(2), (int64_t)K.shape(2), 1};
+  attnb_tensor v{V.data(), (int)V.shape(0), (int)V.shape(1), (int)V.shape(2),
+                 (int64_t)V.shape(1) * V.shape(2), (int64_t)V.shape(2), 1};
+  py::array_t<float> O({H, Dh});
+  attnb_mtensor o{O.mutable_data(), H, 1, Dh, (int64_t)Dh, 0, 1};
+  int rc;
+  {
+    py::gil_scoped_release nogil;
+    rc = attnb_attn_step_dense(&q, &k, &v, &o);
+  }
+  rethrow(rc);
+  return O;
+}
+
+py::array_t<float> attn_block_dense_py(farray Q, farray K, farray V, bool causal, int precision) {
+  if (Q.ndim() != 3 || K.ndim() != 3 || V.ndim() != 3)
+    throw std::invalid_argument("Q must be [H,L,Dh], K and V [H,T,Dh]");
+  const int H = (int)Q.shape(0), L = (int)Q.shape(1), Dh = (int)Q.shape(2);
+  attnb_tensor q{Q.data(), H, L, Dh, (int64_t)L * Dh, (int64_t)Dh, 1};
+  attnb_tensor k{K.data(), (int)K.shape(0), (int)K.shape(1), (int)K.shape(2),
+                 (int64_t)K.shape(1) * K.shape(2), (int64_t)K.shape(2), 1};
+  attnb_tensor v{V.data(), (int)V.shape(0), (int)V.shape(1), (int)V.shape(2),
+                 (int64_t)V.shape(1) * V.shape(2), (int64_t)V.shape(2), 1};
+  py::array_t<float> O({H, L, Dh});
+  attnb_mtensor o{O.mutable_data(), H, L, Dh, (int64_t)L * Dh, (int64_t)Dh, 1};
+  int rc;
+  {
+    py::gil_scoped_release nogil;
+    rc = attnb_attn_block_dense(&q, &k, &v, &o, causal ? 1 : 0, precision);
+  }
+  rethrow(rc);
+  return O;
+}
+
+}  // namespace
+
+PYBIND11_MODULE(_attn_cpu, m) {
+  m.doc() = "Dense attention (step + block) and SGEMM on B200 (sm_100a)";
+  m.def("mha_block_dense", &mha_block_dense_py, py::arg("x"), py::arg("W_in"), py::arg("b_in"),
+        py::arg("W_out"), py::arg("b_out"), py::arg("num_heads"), py::arg("causal") = false,
+        py::arg("precision") = -1,
+        "Full MHA block: x:[T,D], W_in:[3D,D], b_in:[3D], W_out:[D,D], b_out:[D] -> y:[T,D]");
+  m.def("gemm", &gemm_py, py::arg("A"), py::arg("B"), py::arg("alpha") = 1.0f,
+        py::arg("beta") = 0.0f, py::arg("precision") = -1,
+        "SGEMM: C = alpha * A@B + beta*C, A:[M,K], B:[K,N] -> C:[M,N]");
+  m.def("gemm_jit", &gemm_jit_py, py::arg("A"), py::arg("B"), py::arg("alpha") = 1.0f,
+        py::arg("beta") = 0.0f, py::arg("precision") = -1,
+        "SGEMM (same kernel as gemm): C = alpha * A@B + beta*C -> C:[M,N]");
+  m.def("attn_step_dense", &attn_step_dense_py, py::arg("Q"), py::arg("K"), py::arg("V"),
+        "Decode step: Q:[H,Dh], K,V:[H,T,Dh] -> O:[H,Dh]");
+  m.def("attn_block_dense", &attn_block_dense_py, py::arg("Q"), py::arg("K"), py::arg("V"),
+        py::arg("causal") = false, py::arg("precision") = -1,
+        "Prefill: Q:[H,L,Dh], K,V:[H,T,Dh] -> O:[H,L,Dh]");
+  m.def("version", &attnb_version);
+}

@@ -1,0 +1,140 @@
+// runtime.cu -- host runtime of libattnb (see runtime.h).
+#include "runtime.h"
+
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <vector>
+
+namespace attnb {
+
+static thread_local std::string t_last_error;
+
+[[noreturn]] void fail(int code, const std::string& msg) { throw Error{code, msg}; }
+
+void check_cuda(cudaError_t e, const char* what, const char* file, int line) {
+  if (e == cudaSuccess) return;
+  fail(ATTNB_ERR_CUDA, std::string(what) + " failed: " + cudaGetErrorString(e) + " (" + file +
+                           ":" + std::to_string(line) + ")");
+}
+
+int set_last_error(int code, const std::string& msg) {
+  t_last_error = msg;
+  return code;
+}
+
+const char* last_error_cstr() { return t_last_error.c_str(); }
+
+void* DeviceBuffer::ensure(size_t need, cudaStream_t stream) {
+  if (need <= bytes && ptr) return ptr;
+  size_t grow = need + need / 4 + 4096;
+  if (ptr) {
+    ATTNB_CUDA(cudaStreamSynchronize(stream));
+    ATTNB_CUDA(cudaFree(ptr));
+    ptr = nullptr;
+    bytes = 0;
+  }
+  ATTNB_CUDA(cudaMalloc(&ptr, grow));
+  bytes = grow;
+  return ptr;
+}
+
+static std::mutex g_ctx_mu;
+static std::map<int, std::unique_ptr<DeviceCtx>> g_ctx;
+
+DeviceCtx& current_ctx() {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    fail(ATTNB_ERR_CUDA, std::string("no CUDA device available: ") + cudaGetErrorString(e));
+  }
+  std::lock_guard<std::mutex> g(g_ctx_mu);
+  auto it = g_ctx.find(dev);
+  if (it != g_ctx.end()) return *it->second;
+  auto c = std::make_unique<DeviceCtx>();
+  c->device = dev;
+  int major = 0, minor = 0;
+  ATTNB_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev));
+  ATTNB_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev));
+  if (major != 10 || minor != 0)
+    fail(ATTNB_ERR_RUNTIME, "libattnb is built for sm_100a (B200); device " + std::to_string(dev) +
+                                " is sm_" + std::to_string(major) + std::to_string(minor));
+  ATTNB_CUDA(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, dev));
+  ATTNB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
+  ATTNB_CUDA(cudaMalloc(&c->status, sizeof(int)));
+  ATTNB_CUDA(cudaMemset(c->status, 0, sizeof(int)));
+  DeviceCtx& ref = *c;
+  g_ctx.emplace(dev, std::move(c));
+  return ref;
+}
+
+void* dev_scratch(DeviceCtx& c, size_t bytes, cudaStream_t stream) {
+  if (bytes == 0) return nullptr;
+  std::lock_guard<std::mutex> g(c.scratch_mu);
+  return c.scratch_dev_path.ensure(bytes, stream);
+}
+
+int resolve_precision(int precision) {
+  if (precision == ATTNB_PREC_3XTF32 || precision == ATTNB_PREC_TF32) return precision;
+  if (precision != ATTNB_PREC_DEFAULT)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "unknown precision " + std::to_string(precision));
+  const char* e = std::getenv("ATTNB_PRECISION");
+  if (e && (std::strcmp(e, "tf32") == 0 || std::strcmp(e, "TF32") == 0)) return ATTNB_PREC_TF32;
+  return ATTNB_PREC_3XTF32;
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                   const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                   CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000,
+                                                     cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p) return (EncodeTiledFn) nullptr;
+    return reinterpret_cast<EncodeTiledFn>(p);
+  }();
+  if (!fn) fail(ATTNB_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  return fn;
+}
+
+CUtensorMap make_tmap_2d(const float* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                         uint32_t box_rows, uint32_t box_cols) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    fail(ATTNB_ERR_RUNTIME, "TMA base address is not 16-byte aligned");
+  if ((ld * sizeof(float)) % 16 != 0) fail(ATTNB_ERR_RUNTIME, "TMA row pitch is not 16-byte aligned");
+  if (box_cols * sizeof(float) > 128 || box_rows > 256 || box_rows == 0 || box_cols == 0)
+    fail(ATTNB_ERR_RUNTIME, "TMA box exceeds the 128-byte swizzle span");
+  CUtensorMap m;
+  std::memset(&m, 0, sizeof(m));
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {ld * sizeof(float)};
+  const cuuint32_t box[2] = {box_cols, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    fail(ATTNB_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return m;
+}
+
+int consume_status(DeviceCtx& c, cudaStream_t stream) {
+  int h = 0;
+  ATTNB_CUDA(cudaMemcpyAsync(&h, c.status, sizeof(int), cudaMemcpyDeviceToHost, stream));
+  ATTNB_CUDA(cudaStreamSynchronize(stream));
+  if (h) {
+    ATTNB_CUDA(cudaMemsetAsync(c.status, 0, sizeof(int), stream));
+    ATTNB_CUDA(cudaStreamSynchronize(stream));
+    return ATTNB_ERR_DEVICE_TIMEOUT;
+  }
+  return ATTNB_OK;
+}
+
+}  // namespace attnb

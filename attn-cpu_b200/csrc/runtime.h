@@ -1,0 +1,68 @@
+// runtime.h -- host runtime of libattnb: errors, per-device context (stream,
+// status word, scratch arenas), TMA descriptor encoding, precision selection.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+#include <mutex>
+#include <string>
+
+#include "../../include/attnb.h"
+
+namespace attnb {
+
+// Internal error type; the C ABI converts it into a status code + message.
+struct Error {
+  int code;
+  std::string msg;
+};
+[[noreturn]] void fail(int code, const std::string& msg);
+void check_cuda(cudaError_t e, const char* what, const char* file, int line);
+#define ATTNB_CUDA(call) ::attnb::check_cuda((call), #call, __FILE__, __LINE__)
+
+// Records `msg` as the calling thread's last error and returns `code`.
+int set_last_error(int code, const std::string& msg);
+
+// Grow-only device buffer.  Growing synchronises `stream` first, so a buffer
+// that earlier work on the same stream still reads is never freed under it.
+struct DeviceBuffer {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+  void* ensure(size_t need, cudaStream_t stream);
+};
+
+struct DeviceCtx {
+  int device = -1;
+  int num_sms = 0;
+  cudaStream_t stream = nullptr;  // used by the host-pointer entry points
+  int* status = nullptr;          // device status word (bit 0: wait time-out)
+  std::mutex mu;                  // serialises host-pointer calls on this device
+  DeviceBuffer io;                // device copies of host inputs/outputs
+  DeviceBuffer scratch_host_path; // kernel scratch for host-pointer calls
+  std::mutex scratch_mu;
+  DeviceBuffer scratch_dev_path;  // kernel scratch for _dev calls (per device)
+};
+
+// Context of the current CUDA device (created on first use).
+DeviceCtx& current_ctx();
+
+// Scratch for a _dev call on `stream`.  Calls on different streams of one
+// device share this buffer, so concurrent _dev calls must use one stream or be
+// ordered by the caller; the returned lock keeps other host threads out while
+// the launch is enqueued.
+void* dev_scratch(DeviceCtx& c, size_t bytes, cudaStream_t stream);
+
+// Resolves ATTNB_PREC_DEFAULT via the ATTNB_PRECISION environment variable.
+int resolve_precision(int precision);
+
+// 2-D fp32 tensor map: rows x cols (cols contiguous, row pitch ld elements),
+// box box_rows x box_cols, 128-byte swizzle, out-of-range elements read as 0.
+CUtensorMap make_tmap_2d(const float* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                         uint32_t box_rows, uint32_t box_cols);
+
+// Reads and clears the device status word of ctx (synchronises `stream`).
+int consume_status(DeviceCtx& c, cudaStream_t stream);
+
+}  // namespace attnb

@@ -1,0 +1,504 @@
+"""bench.py -- throughput of the B200 hot paths, one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload prefill|decode|sgemm|sgemm-large|block] [--precision 3xtf32|tf32]
+
+Default workload (the headline): MHA prefill fp32, batch 1, 8 heads,
+seq_q = seq_kv = 512, head_dim 64, Q/K/V ~ N(0,1), scale 1/sqrt(64), no mask,
+through attn_block_dense.  A step is one pass of that path over one batch.
+At N GPUs (one process per GPU under torchrun) every rank runs its own batch
+(batch x heads partition, no collective on the data path): weak scaling,
+value = all ranks' FLOPs / the slowest rank's time.
+
+Keys beyond the base contract:
+  e2e          the same metric through the public Python API (attn_cpu.*) with
+               pinned host inputs: host->device copies, compute and the
+               device->host read of the result are inside each timed step;
+  roofline     the dominant kernel's algorithmic rate (CUDA events, launching
+               stream) against the measured peak in MEASURED_PEAKS.json;
+  cpu_baseline the reference's own CPU code (oracle/_ref, compiled from its
+               sources) timed on this host on a bounded sample (rank 0, N=1);
+  also         the other measured configs (decode GB/s, SGEMM TFLOP/s,
+               attention block TFLOP/s) with their own rooflines (N=1 only).
+
+`--impl reference` times the reference's CPU implementation of the headline
+path on this host's cores (all threads) and prints its own line.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "attn-cpu_b200"))
+
+# Algorithmic work per call, per workload.
+WORKLOADS = {
+    "prefill": dict(metric="MHA prefill TFLOP/s", unit="TFLOP/s", H=8, L=512, T=512, Dh=64,
+                    desc="MHA prefill fp32 [1,8,512,64] non-causal (attn_block_dense)"),
+    "decode": dict(metric="M=1 decode KV-stream GB/s", unit="GB/s", H=256, T=4096, Dh=128,
+                   desc="MHA decode step fp32 B=8 x H=32, Dh=128, T=4096 (attn_step_dense)"),
+    "sgemm": dict(metric="SGEMM TFLOP/s per GPU", unit="TFLOP/s", M=1024, N=1024, K=1024,
+                  desc="SGEMM fp32 1024^3, U[-1,1], beta=0 (gemm)"),
+    "sgemm-large": dict(metric="SGEMM TFLOP/s per GPU", unit="TFLOP/s", M=16384, N=16384,
+                        K=16384, desc="SGEMM fp32 16384^3, U[-1,1], beta=0 (gemm)"),
+    "block": dict(metric="attention block TFLOP/s", unit="TFLOP/s", B=4, T=2048, D=4096, H=32,
+                  desc="attention block fp32: hidden 4096, 32 heads, Dh 128, batch 4, "
+                       "seq 2048 (mha_block_dense)"),
+}
+
+# DRAM bytes per launch of each dominant kernel from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum); see profiles/.
+NCU_TRAFFIC = {}
+
+
+def flops_of(w: str) -> float:
+    c = WORKLOADS[w]
+    if w == "prefill":
+        return 4.0 * c["H"] * c["L"] * c["T"] * c["Dh"]
+    if w == "decode":
+        return 4.0 * c["H"] * c["T"] * c["Dh"]
+    if w.startswith("sgemm"):
+        return 2.0 * c["M"] * c["N"] * c["K"]
+    if w == "block":
+        B, T, D = c["B"], c["T"], c["D"]
+        return B * (2.0 * T * D * 3 * D + 4.0 * T * T * D + 2.0 * T * D * D)
+    raise KeyError(w)
+
+
+def bytes_of(w: str) -> float:
+    """Algorithmic HBM bytes of the decode step: K + V once, plus q and o."""
+    c = WORKLOADS[w]
+    return 4.0 * (2 * c["H"] * c["T"] * c["Dh"] + 2 * c["H"] * c["Dh"])
+
+
+def load_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as fh:
+            p = json.load(fh)
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "src": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        time.sleep(0.15)
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            time.sleep(0.15)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        mhz, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not mhz:
+            return None
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(mhz)}
+
+
+# ------------------------------------------------------------- helpers
+def dist_setup(n_gpus: int):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+class L2Flusher:
+    """Writes a buffer larger than the 126 MB L2 between timed steps."""
+
+    def __init__(self):
+        import torch
+
+        self.buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+
+    def __call__(self):
+        self.buf.fill_(1.0)
+
+
+def time_device(run, steps: int, warmup: int, world: int, flush: bool):
+    """Per-step CUDA-event times (ms) of `run` on the current stream, L2
+    flushed between steps outside the events; barrier + sync around."""
+    import torch
+
+    fl = L2Flusher() if flush else None
+    for _ in range(warmup):
+        if fl:
+            fl()
+        run()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(steps)]
+    for i in range(steps):
+        if fl:
+            fl()
+        ev[i][0].record()
+        run()
+        ev[i][1].record()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in ev]
+
+
+# --------------------------------------------------------- workloads (ours)
+def setup_workload(w: str, rank: int, precision):
+    """Device inputs (seeded per rank) and (run, e2e_run, h2d, d2h, launches)."""
+    import numpy as np
+    import torch
+
+    import attn_cpu
+    from attn_cpu import capi
+
+    c = WORKLOADS[w]
+    g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+    if w == "prefill":
+        H, L, T, Dh = c["H"], c["L"], c["T"], c["Dh"]
+        Q = torch.randn(H, L, Dh, device="cuda", generator=g)
+        K = torch.randn(H, T, Dh, device="cuda", generator=g)
+        V = torch.randn(H, T, Dh, device="cuda", generator=g)
+        O = torch.empty(H, L, Dh, device="cuda")
+        run = lambda: capi.attn_block_dense_dev(Q, K, V, O, False, precision)
+        hQ, hK, hV = (t.cpu().pin_memory() for t in (Q, K, V))
+        nQ, nK, nV = hQ.numpy(), hK.numpy(), hV.numpy()
+        e2e = lambda: attn_cpu.attn_block_dense(nQ, nK, nV, precision=precision)
+        h2d = 4 * (Q.numel() + K.numel() + V.numel())
+        d2h = 4 * O.numel()
+        return run, e2e, h2d, d2h, 1
+    if w == "decode":
+        H, T, Dh = c["H"], c["T"], c["Dh"]
+        Q = torch.randn(H, Dh, device="cuda", generator=g)
+        K = torch.randn(H, T, Dh, device="cuda", generator=g)
+        V = torch.randn(H, T, Dh, device="cuda", generator=g)
+        O = torch.empty(H, Dh, device="cuda")
+        run = lambda: capi.attn_step_dense_dev(Q, K, V, O)
+        hQ, hK, hV = (t.cpu().pin_memory() for t in (Q, K, V))
+        nQ, nK, nV = hQ.numpy(), hK.numpy(), hV.numpy()
+        e2e = lambda: attn_cpu.attn_step_dense(nQ, nK, nV)
+        return run, e2e, 4 * (Q.numel() + K.numel() + V.numel()), 4 * O.numel(), 2
+    if w.startswith("sgemm"):
+        M, N, K = c["M"], c["N"], c["K"]
+        A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1
+        B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
+        C = torch.empty(M, N, device="cuda")
+        run = lambda: capi.sgemm_dev(A, B, C, precision=precision)
+        hA, hB = A.cpu().pin_memory(), B.cpu().pin_memory()
+        nA, nB = hA.numpy(), hB.numpy()
+        e2e = lambda: attn_cpu.gemm(nA, nB, precision=precision)
+        return run, e2e, 4 * (A.numel() + B.numel()), 4 * C.numel(), 3
+    if w == "block":
+        Bt, T, D, H = c["B"], c["T"], c["D"], c["H"]
+        x = torch.randn(Bt, T, D, device="cuda", generator=g)
+        Wi = torch.randn(3 * D, D, device="cuda", generator=g) * 0.02
+        Wo = torch.randn(D, D, device="cuda", generator=g) * 0.02
+        bi = torch.zeros(3 * D, device="cuda")
+        bo = torch.zeros(D, device="cuda")
+        y = torch.empty_like(x)
+        run = lambda: capi.mha_block_dense_dev(x, Wi, bi, Wo, bo, H, y, False, precision)
+        hx = x.cpu().pin_memory()
+        hw = [t.cpu().pin_memory().numpy() for t in (Wi, bi, Wo, bo)]
+        nx = hx.numpy()
+        e2e = lambda: [attn_cpu.mha_block_dense(nx[b], *hw, H, precision=precision)
+                       for b in range(Bt)]
+        h2d = 4 * (x.numel() + Wi.numel() + bi.numel() + Wo.numel() + bo.numel()) * 1
+        return run, e2e, h2d, 4 * y.numel(), 4 + Bt
+    raise KeyError(w)
+
+
+def roofline_of(w: str, ms: float, peaks: dict, precision) -> dict:
+    traffic = NCU_TRAFFIC.get((w, precision or "3xtf32"))
+    if w == "decode":
+        achieved = bytes_of(w) / (ms * 1e-3) / 1e9
+        peak = peaks["hbm_gbs"]
+        return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "traffic": traffic,
+                "peak_src": f"{peaks['src']} STREAM-style copy"}
+    achieved = flops_of(w) / (ms * 1e-3) / 1e12
+    # tcgen05 kind::tf32 runs at half the bf16 rate; the measured cuBLAS bf16
+    # burst figure / 2 is the TF32 denominator.
+    peak = peaks["bf16_tflops"] / 2
+    r = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1),
+         "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+         "peak_src": f"{peaks['src']} bf16 burst / 2 (TF32 rate)"}
+    if (precision or "3xtf32") == "3xtf32":
+        r["frac_of_3xtf32_cap"] = round(3 * achieved / peak, 4)
+    return r
+
+
+def measure(w: str, rank: int, world: int, steps: int, warmup: int, precision, peaks,
+            with_e2e=True):
+    import torch
+
+    run, e2e, h2d, d2h, launches = setup_workload(w, rank, precision)
+    flush = w in ("prefill", "sgemm")  # the other workloads' inputs exceed L2
+    with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
+        t0 = time.perf_counter()
+        times = time_device(run, steps, warmup, world, flush)
+        wall = time.perf_counter() - t0
+    from attn_cpu import capi
+
+    capi.stream_status()
+    total_ms = max_over_ranks(sum(times), world)
+    ms = total_ms / steps
+    work = flops_of(w) if w != "decode" else bytes_of(w)
+    scale = 1e12 if WORKLOADS[w]["unit"] == "TFLOP/s" else 1e9
+    value = world * work / (ms * 1e-3) / scale
+    res = {"metric": WORKLOADS[w]["metric"], "value": round(value, 3),
+           "unit": WORKLOADS[w]["unit"], "ms_per_step": round(ms, 5),
+           "roofline": roofline_of(w, ms, peaks, precision),
+           "gpu_launches": launches * steps, "l2": "flushed between steps" if flush else
+           "inputs larger than L2", "wall_s": round(wall, 3), "clocks": clk.summary()}
+    if with_e2e:
+        for _ in range(max(1, warmup)):
+            e2e()
+        barrier(world)
+        ts = []
+        for _ in range(steps):
+            t = time.perf_counter()
+            e2e()
+            ts.append(time.perf_counter() - t)
+        e_ms = max_over_ranks(1e3 * sum(ts) / len(ts), world)
+        res["e2e"] = {"value": round(world * work / (e_ms * 1e-3) / scale, 4),
+                      "unit": WORKLOADS[w]["unit"], "ms_per_step": round(e_ms, 4),
+                      "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+    del run, e2e
+    torch.cuda.empty_cache()
+    return res
+
+
+# ----------------------------------------------------- CPU (reference) runs
+def cpu_sample(w: str, budget_s: float):
+    """Time the reference's CPU code (compiled from its sources) on this host,
+    falling back to the float64 restatement when it cannot run here.
+    Returns (value, unit, cores, kind, sample description)."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+
+    kind = "reference" if oracle.ref_available() else "port"
+    cores = os.cpu_count() or 1
+    c = WORKLOADS[w]
+    rng = np.random.default_rng(0)
+    if w == "prefill":
+        Q, K, V = (rng.standard_normal((c["H"], c["L"] if i == 0 else c["T"], c["Dh"]),
+                                       dtype=np.float32) for i in range(3))
+        fn = (lambda: oracle.ref_attn_block(Q, K, V)) if kind == "reference" else \
+            (lambda: oracle.attn_block(Q, K, V))
+        unit_work, desc = flops_of(w), "full [1,8,512,64] problem per call"
+    elif w == "decode":
+        H = 32  # bounded sample: 32 of the 256 heads per call
+        Q = rng.standard_normal((H, c["Dh"]), dtype=np.float32)
+        K = rng.standard_normal((H, c["T"], c["Dh"]), dtype=np.float32)
+        V = rng.standard_normal((H, c["T"], c["Dh"]), dtype=np.float32)
+        fn = (lambda: oracle.ref_attn_step(Q, K, V)) if kind == "reference" else \
+            (lambda: oracle.attn_step(Q, K, V))
+        unit_work = 4.0 * (2 * H * c["T"] * c["Dh"] + 2 * H * c["Dh"])
+        desc = "32 of 256 heads (T=4096, Dh=128) per call; single-threaded reference function"
+        cores = 1
+    elif w.startswith("sgemm"):
+        n = 1024
+        A = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+        B = rng.uniform(-1, 1, (n, n)).astype(np.float32)
+        fn = (lambda: oracle.ref_sgemm(A, B)) if kind == "reference" else \
+            (lambda: oracle.sgemm(A, B))
+        unit_work, desc = 2.0 * n ** 3, "1024^3 SGEMM per call"
+    else:
+        T, D, H = 256, 4096, 32
+        x = rng.standard_normal((T, D), dtype=np.float32)
+        Wi = (0.02 * rng.standard_normal((3 * D, D))).astype(np.float32)
+        Wo = (0.02 * rng.standard_normal((D, D))).astype(np.float32)
+        bi, bo = np.zeros(3 * D, np.float32), np.zeros(D, np.float32)
+        fn = (lambda: oracle.ref_mha_block(x, Wi, bi, Wo, bo, H)) if kind == "reference" else \
+            (lambda: oracle.mha_block(x, Wi, bi, Wo, bo, H))
+        unit_work = 2.0 * T * D * 3 * D + 4.0 * T * T * D + 2.0 * T * D * D
+        desc = "one sequence of T=256 at hidden 4096 / 32 heads per call; single-threaded"
+        cores = 1
+    fn()  # warm (the reference picks its unroll once, src/gemm.cpp:272-316)
+    n_calls, t0 = 0, time.perf_counter()
+    while True:
+        fn()
+        n_calls += 1
+        el = time.perf_counter() - t0
+        if el >= budget_s:
+            break
+    per = el / n_calls
+    scale = 1e12 if WORKLOADS[w]["unit"] == "TFLOP/s" else 1e9
+    return unit_work / per / scale, WORKLOADS[w]["unit"], cores, kind, \
+        f"{desc}; {n_calls} calls in {el:.1f} s"
+
+
+def run_reference_arm(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    w = args.workload
+    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    os.environ.setdefault("OMP_PROC_BIND", "close")
+    per = max(1.0, args.cpu_seconds / max(1, args.steps))
+    vals = []
+    kind = cores = sample = unit = None
+    for i in range(args.warmup + args.steps):
+        v, unit, cores, kind, sample = cpu_sample(w, per if i >= args.warmup else 0.2)
+        if i >= args.warmup:
+            vals.append(v)
+    value = statistics.mean(vals)
+    line = {"impl": "reference", "metric": WORKLOADS[w]["metric"], "value": round(value, 5),
+            "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": WORKLOADS[w]["desc"]},
+            "cpu_baseline": {"value": round(value, 5), "unit": unit, "cores": cores,
+                             "kind": kind, "sample": sample},
+            "e2e": {"value": round(value, 5), "unit": unit, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------- main
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="prefill")
+    ap.add_argument("--precision", choices=["3xtf32", "tf32"], default="3xtf32")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0,
+                    help="CPU time budget of the reference measurement")
+    ap.add_argument("--no-also", action="store_true", help="skip the secondary configs")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be >= 3")
+
+    if args.impl == "reference":
+        run_reference_arm(args)
+        return
+
+    import torch
+
+    rank, world, _ = dist_setup(args.gpus)
+    peaks = load_peaks()
+    prec = args.precision
+    head = measure(args.workload, rank, world, args.steps, args.warmup, prec, peaks)
+    also = []
+    if world == 1 and not args.no_also:
+        for w in ("decode", "sgemm", "sgemm-large", "block"):
+            if w == args.workload:
+                continue
+            steps = args.steps if w in ("decode", "sgemm") else max(3, min(args.steps, 5))
+            r = measure(w, rank, world, steps, 3, prec, peaks,
+                        with_e2e=w in ("decode", "sgemm"))
+            r["config"] = WORKLOADS[w]["desc"]
+            also.append(r)
+    cpu = None
+    if rank == 0 and world == 1:
+        v, unit, cores, kind, sample = cpu_sample(args.workload, args.cpu_seconds)
+        cpu = {"value": round(v, 5), "unit": unit, "cores": cores, "kind": kind,
+               "sample": sample}
+    if rank == 0:
+        line = {"metric": head["metric"], "value": head["value"], "unit": head["unit"],
+                "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                "ms_per_step": head["ms_per_step"], "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+                "precision": prec, "data": "synthetic (seeded N(0,1) / U[-1,1])",
+                "config": {"workload": WORKLOADS[args.workload]["desc"],
+                           "l2": head["l2"], "parallelism": f"batch-x-heads x{world}",
+                           "global_batch": world},
+                "e2e": head.get("e2e"), "roofline": head["roofline"],
+                "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
+                "cpu_baseline": cpu, "also": also}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

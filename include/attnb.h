@@ -1,0 +1,139 @@
+/*
+ * attnb.h -- C ABI of the B200 attention/SGEMM library (libattnb.so).
+ *
+ * Plain pointers, sizes and status codes; no C++ or torch types.  Each entry
+ * point replaces one reference interface, cited beside it.  The C++ headers
+ * attn.h / attn_api.h / gemm.h in this directory keep the reference's own
+ * signatures as thin shims over these calls.
+ *
+ * Host-pointer entry points (no suffix) follow the reference's contract: all
+ * pointers are caller-owned row-major fp32 HOST memory, the call copies inputs
+ * to the current CUDA device, computes there and copies the result back before
+ * returning.  Pinned (page-locked) host buffers make those copies faster but
+ * are not required.
+ *
+ * Device-pointer entry points (suffix _dev) take device pointers and a
+ * cudaStream_t (passed as void*, NULL = legacy default stream); they enqueue
+ * work and return without synchronising.  Kernel-side wait time-outs are
+ * reported by attnb_stream_status().
+ *
+ * Every function returns ATTNB_OK (0) or an error code; attnb_last_error()
+ * returns a message for the calling thread's last failure.
+ */
+#ifndef ATTNB_H
+#define ATTNB_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define ATTNB_API __attribute__((visibility("default")))
+#else
+#define ATTNB_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ATTNB_OK 0
+#define ATTNB_ERR_INVALID_ARGUMENT 1 /* shape/null/stride problems: std::invalid_argument */
+#define ATTNB_ERR_RUNTIME 2          /* unsupported configuration: std::runtime_error */
+#define ATTNB_ERR_CUDA 3             /* a CUDA runtime/driver call failed */
+#define ATTNB_ERR_DEVICE_TIMEOUT 4   /* a bounded in-kernel wait expired */
+
+/* Arithmetic used by the tensor-core contractions (SGEMM, projections,
+ * prefill attention).  Decode is always plain fp32 FMA on CUDA cores.
+ *   ATTNB_PREC_3XTF32: split fp32 operands into tf32 big+small parts and
+ *     accumulate big*big + big*small + small*big in fp32 (fp32-level accuracy,
+ *     max|y-r|/max|r| <= 1e-5 against the reference).
+ *   ATTNB_PREC_TF32: one tf32 pass (<= 2e-3).
+ *   ATTNB_PREC_DEFAULT: ATTNB_PREC_3XTF32 unless the environment variable
+ *     ATTNB_PRECISION is "tf32". */
+#define ATTNB_PREC_DEFAULT (-1)
+#define ATTNB_PREC_3XTF32 0
+#define ATTNB_PREC_TF32 1
+
+/* Non-owning view of a 3-D fp32 tensor [H, T, Dh]; strides in elements.
+ * Mirrors attn::TensorF32 / MutableTensor3F32 (include/attn.h:10-26 of the
+ * reference).  For a 2-D [H, Dh] view set T = 1 and strideT = 0. */
+typedef struct attnb_tensor {
+  const float* data;
+  int H, T, Dh;
+  int64_t strideH, strideT, strideDh;
+} attnb_tensor;
+
+typedef struct attnb_mtensor {
+  float* data;
+  int H, T, Dh;
+  int64_t strideH, strideT, strideDh;
+} attnb_mtensor;
+
+/* ---------------------------------------------------------------- errors */
+ATTNB_API const char* attnb_last_error(void);
+/* Library version string, e.g. "attnb 0.1 sm_100a". */
+ATTNB_API const char* attnb_version(void);
+/* Device status word of `stream`'s device: ATTNB_OK or ATTNB_ERR_DEVICE_TIMEOUT
+ * (and clears it).  Synchronises the stream. */
+ATTNB_API int attnb_stream_status(void* stream);
+
+/* ---------------------------------------------------------------- SGEMM */
+/* C[M,N] = alpha * A[M,K] . B[K,N] + beta * C.
+ * Replaces gemm::sgemm_blocked (include/gemm.h:11-14; src/gemm.cpp:319-415).
+ * M,N,K <= 0 return ATTNB_OK without touching C; alpha == 0 only scales C;
+ * beta == 0 never reads C. */
+ATTNB_API int attnb_sgemm(const float* A, int M, int K, const float* B, int N, float* C,
+                float alpha, float beta, int precision);
+/* Replaces gemm::gemm_blocked_jit (include/gemm.h:17-20; src/jit_gemm.cpp:740-754).
+ * Same function as attnb_sgemm; there is no run-time autotune. */
+ATTNB_API int attnb_gemm_jit(const float* A, int M, int K, const float* B, int N, float* C,
+                   float alpha, float beta, int precision);
+/* Device-pointer SGEMM with leading dimensions (elements): lda >= K, ldb >= N,
+ * ldc >= N. */
+ATTNB_API int attnb_sgemm_dev(const float* A, int lda, const float* B, int ldb, float* C, int ldc,
+                    int M, int N, int K, float alpha, float beta, int precision,
+                    void* stream);
+
+/* y[T,N] = x[T,K] . W[N,K]^T + b[N] on device pointers (b may be NULL).
+ * The projection step of attn::mha_block_dense (src/attn_dispatch.cpp:45-95,
+ * include/gemm_16x16.h:7-60, include/pack_16x16.h:9-25); ldx >= K, ldw >= K,
+ * ldy >= N. */
+ATTNB_API int attnb_linear_dev(const float* x, int ldx, const float* W, int ldw, const float* b,
+                     float* y, int ldy, int T, int N, int K, int precision, void* stream);
+
+/* ------------------------------------------------------------ attention */
+/* Decode step: O[h,:] = softmax(Q[h,:] . K[h]^T / sqrt(Dh)) . V[h].
+ * Q: [H, Dh] (T ignored), K/V: [H, T, Dh], O: [H, Dh].
+ * Replaces attn::attn_step_dense (include/attn.h:35-38; src/attn_dense.cpp:21-73),
+ * with the reference's validate_dense_shapes checks (include/attn.h:54-83). */
+ATTNB_API int attnb_attn_step_dense(const attnb_tensor* Q, const attnb_tensor* K,
+                          const attnb_tensor* V, attnb_mtensor* O);
+ATTNB_API int attnb_attn_step_dense_dev(const attnb_tensor* Q, const attnb_tensor* K,
+                              const attnb_tensor* V, attnb_mtensor* O, void* stream);
+
+/* Prefill with given Q/K/V: Q [H,L,Dh], K/V [H,T,Dh] -> O [H,L,Dh]; causal
+ * needs L == T.  Replaces attn::attn_block_dense (include/attn.h:40-44;
+ * src/attn_block.cpp:104-241). */
+ATTNB_API int attnb_attn_block_dense(const attnb_tensor* Q, const attnb_tensor* K,
+                           const attnb_tensor* V, attnb_mtensor* O, int causal,
+                           int precision);
+ATTNB_API int attnb_attn_block_dense_dev(const attnb_tensor* Q, const attnb_tensor* K,
+                               const attnb_tensor* V, attnb_mtensor* O, int causal,
+                               int precision, void* stream);
+
+/* Full MHA block, x[T,D] -> y[T,D] with W_in[3D,D], b_in[3D], W_out[D,D],
+ * b_out[D] (PyTorch nn.MultiheadAttention packing), H heads.
+ * Replaces attn::mha_block_dense (include/attn_api.h:4-7; src/attn_dispatch.cpp:17-133).
+ * Errors: D % H != 0 or D % 16 != 0 -> ATTNB_ERR_RUNTIME, like the reference. */
+ATTNB_API int attnb_mha_block_dense(const float* x, int T, int D, const float* W_in,
+                          const float* b_in, const float* W_out, const float* b_out, int H,
+                          int causal, float* y, int precision);
+/* Device-pointer MHA block over `batch` independent sequences laid out as
+ * x[batch, T, D] -> y[batch, T, D]. */
+ATTNB_API int attnb_mha_block_dense_dev(const float* x, int batch, int T, int D, const float* W_in,
+                              const float* b_in, const float* W_out, const float* b_out,
+                              int H, int causal, float* y, int precision, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* ATTNB_H */
