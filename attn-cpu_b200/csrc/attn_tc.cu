@@ -1,0 +1,509 @@
+// attn_tc.cu -- K3: tcgen05 prefill attention (attn::attn_block_dense and the
+// attention step of attn::mha_block_dense), 3xTF32 or 1xTF32.
+//
+// Reference: the flash-style online softmax of
+// include/kernels/attn_dhk16_m4_nocausal.h:20-293 (per key block: block max,
+// rescale a = exp(m - m_new), weights exp(s - m_new), masked denominators,
+// V-FMA, stats update, final 1/l) and the causal per-query kernels
+// include/attn_generic_m1.h:7-37 (keys 0..t); exact two-pass form in
+// src/attn_block.cpp:104-241.  The same function, tiled for the tensor cores:
+//
+//   CTA = 128 query rows (one per TMEM lane) of one head, a range of 128-key
+//   tiles.  Warp 0 streams, through a shared-memory ring, 32-wide slices of
+//   Q and K (S phase) and of V^T (PV phase) with TMA.  Warp 1 issues
+//     S  = Q.K^T          into TMEM (3xTF32: big = hi*hi, small = hi*lo + lo*hi)
+//     PV = P.V            with P read straight from TMEM (tcgen05.mma A-from-TMEM)
+//   Warps 2-5 (thread = query row) read S, keep the running max m and sum l,
+//   write P = 2^(s - m) (split hi/lo) over S's TMEM columns, then fold the
+//   finished PV tile into an fp32 register accumulator:
+//     O = O * 2^(m_old - m_new) + PV.
+//   Scores never leave the SM; O is normalised once at the end.  When few
+//   (head, query-tile) pairs exist, the key range is split over CTAs and a
+//   small kernel merges the partial (m, l, O).
+//
+// Operands arrive pre-packed by split.cu: Q scaled by log2(e)/sqrt(Dh), head
+// size zero-padded to a multiple of 32, V transposed per head (K-major for the
+// PV product), each split into tf32 hi + fp32 lo for 3xTF32.
+#include <algorithm>
+#include <atomic>
+#include <cmath>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "runtime.h"
+
+namespace attnb {
+namespace {
+
+constexpr int BM = 128;        // query rows per CTA
+constexpr int BN = 128;        // keys per KV tile
+constexpr int BK = 32;         // fp32 elements per 128-byte swizzle row
+constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <int DHP, bool SPLIT3>
+struct AttnCfg {
+  static constexpr int NKB = DHP / BK;       // K slices of the S product
+  static constexpr int NPART = SPLIT3 ? 2 : 1;
+  static constexpr int QBOX = BM * BK * 4;   // 16 KB
+  static constexpr int KBOX = BN * BK * 4;   // 16 KB
+  static constexpr int VBOX = DHP * BK * 4;  // 32 keys of V^T
+  static constexpr int STAGE = NPART * (QBOX + KBOX);
+  static constexpr int STAGES = SPLIT3 ? 3 : 6;
+  static constexpr int SMEM = STAGES * STAGE + 1024;
+  static constexpr int S_BIG = 0;
+  static constexpr int S_SMALL = BN;
+  static constexpr int PV_BIG = NPART * BN;
+  static constexpr int PV_SMALL = PV_BIG + DHP;
+  static constexpr int TMEM_COLS = SPLIT3 ? 512 : 256;
+  static_assert(DHP % 32 == 0 && DHP <= 128, "head size padded to 32..128");
+  static_assert(NPART * VBOX <= STAGE, "V slice fits a stage");
+  static_assert(PV_BIG + NPART * DHP <= TMEM_COLS, "TMEM budget");
+};
+
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* status) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > ATTNB_WAIT_LIMIT_NS) {
+      raise_timeout(status);
+      return;
+    }
+  }
+}
+
+struct AttnParams {
+  int L, T, H, Dh, causal, nsplit, tiles_per_split;
+  float* O;
+  int64_t osH, osT, osD;
+  float* part_o;    // [nsplit, H, L, DHP] (nsplit > 1)
+  float2* part_ml;  // [nsplit, H, L]
+  int* status;
+};
+
+template <int DHP, bool SPLIT3>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
+                   const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
+                   const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
+                   const AttnParams p) {
+  using Cfg = AttnCfg<DHP, SPLIT3>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr uint32_t IDESC_S = idesc_tf32(BM, BN);
+  constexpr uint32_t IDESC_PV = idesc_tf32(BM, DHP);
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t s_bar, p_bar, pv_bar, final_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qt = blockIdx.x, split = blockIdx.y, h = blockIdx.z;
+  const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
+  auto stage_addr = [&](int s) { return base + s * Cfg::STAGE; };
+
+  // Key tiles of this CTA.
+  int n_kv = (p.T + BN - 1) / BN;
+  if (p.causal) {
+    const int last_row = min(p.L, (qt + 1) * BM) - 1;
+    n_kv = min(n_kv, last_row / BN + 1);
+  }
+  const int j0 = split * p.tiles_per_split;
+  const int j1 = min(n_kv, j0 + p.tiles_per_split);
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_addr(&full_bar[s]), 1);
+      mbar_init(smem_addr(&empty_bar[s]), 1);
+    }
+    mbar_init(smem_addr(&s_bar), 1);
+    mbar_init(smem_addr(&p_bar), 4);
+    mbar_init(smem_addr(&pv_bar), 1);
+    mbar_init(smem_addr(&final_bar), 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(&tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort_p = &abort_flag;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------------------ producer
+      tma_prefetch_desc(&tmQh);
+      tma_prefetch_desc(&tmKh);
+      tma_prefetch_desc(&tmVh);
+      int stage = 0;
+      uint32_t phase = 0, issued_mask = 0, issued_parity = 0;
+      bool ok = true;
+      auto next = [&]() {
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      };
+      for (int j = j0; ok && j < j1; ++j) {
+        for (int kb = 0; kb < Cfg::NKB; ++kb) {
+          if (!mbar_wait(smem_addr(&empty_bar[stage]), phase ^ 1u, abort_p, p.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_addr(&full_bar[stage]), sa = stage_addr(stage);
+          mbar_arrive_expect_tx(fb, Cfg::STAGE);
+          tma_load_3d(sa, &tmQh, fb, kb * BK, qt * BM, h);
+          tma_load_3d(sa + Cfg::QBOX, &tmKh, fb, kb * BK, j * BN, h);
+          if (SPLIT3) {
+            tma_load_3d(sa + Cfg::QBOX + Cfg::KBOX, &tmQl, fb, kb * BK, qt * BM, h);
+            tma_load_3d(sa + 2 * Cfg::QBOX + Cfg::KBOX, &tmKl, fb, kb * BK, j * BN, h);
+          }
+          next();
+        }
+        const int nvb = min(BN / BK, (p.T - j * BN + BK - 1) / BK);
+        for (int vb = 0; ok && vb < nvb; ++vb) {
+          if (!mbar_wait(smem_addr(&empty_bar[stage]), phase ^ 1u, abort_p, p.status)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_addr(&full_bar[stage]), sa = stage_addr(stage);
+          mbar_arrive_expect_tx(fb, Cfg::NPART * Cfg::VBOX);
+          tma_load_3d(sa, &tmVh, fb, j * BN + vb * BK, 0, h);
+          if (SPLIT3) tma_load_3d(sa + Cfg::VBOX, &tmVl, fb, j * BN + vb * BK, 0, h);
+          next();
+        }
+      }
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_mask & (1u << s))
+          drain_wait(smem_addr(&full_bar[s]), (issued_parity >> s) & 1u, p.status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int it = 0;
+      for (int j = j0; ok && j < j1; ++j, ++it) {
+        // S(j) overwrites the TMEM columns PV(j-1) read P from.
+        if (it > 0 && !mbar_wait(smem_addr(&pv_bar), (it - 1) & 1, abort_p, p.status)) break;
+        tc_fence_after();
+        for (int kb = 0; kb < Cfg::NKB; ++kb) {
+          if (!mbar_wait(smem_addr(&full_bar[stage]), phase, abort_p, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = stage_addr(stage);
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
+            const uint64_t qh = sdesc_kmajor_sw128(sa + kk * 32);
+            const uint64_t kh = sdesc_kmajor_sw128(sa + Cfg::QBOX + kk * 32);
+            mma_tf32(tmem + Cfg::S_BIG, qh, kh, IDESC_S, acc);
+            if (SPLIT3) {
+              const uint64_t ql = sdesc_kmajor_sw128(sa + Cfg::QBOX + Cfg::KBOX + kk * 32);
+              const uint64_t kl = sdesc_kmajor_sw128(sa + 2 * Cfg::QBOX + Cfg::KBOX + kk * 32);
+              mma_tf32(tmem + Cfg::S_SMALL, qh, kl, IDESC_S, acc);
+              mma_tf32(tmem + Cfg::S_SMALL, ql, kh, IDESC_S, 1u);
+            }
+          }
+          mma_commit(smem_addr(&empty_bar[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(smem_addr(&s_bar));
+        if (!mbar_wait(smem_addr(&p_bar), it & 1, abort_p, p.status)) break;
+        tc_fence_after();
+        const int nvb = min(BN / BK, (p.T - j * BN + BK - 1) / BK);
+        for (int vb = 0; vb < nvb; ++vb) {
+          if (!mbar_wait(smem_addr(&full_bar[stage]), phase, abort_p, p.status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = stage_addr(stage);
+#pragma unroll
+          for (int kk = 0; kk < BK / 8; ++kk) {
+            const uint32_t acc = (vb | kk) != 0 ? 1u : 0u;
+            const uint32_t key = vb * BK + kk * 8;
+            const uint64_t vh = sdesc_kmajor_sw128(sa + kk * 32);
+            mma_tf32_ts(tmem + Cfg::PV_BIG, tmem + Cfg::S_BIG + key, vh, IDESC_PV, acc);
+            if (SPLIT3) {
+              const uint64_t vl = sdesc_kmajor_sw128(sa + Cfg::VBOX + kk * 32);
+              mma_tf32_ts(tmem + Cfg::PV_SMALL, tmem + Cfg::S_BIG + key, vl, IDESC_PV, acc);
+              mma_tf32_ts(tmem + Cfg::PV_SMALL, tmem + Cfg::S_SMALL + key, vh, IDESC_PV, 1u);
+            }
+          }
+          mma_commit(smem_addr(&empty_bar[stage]));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        mma_commit(smem_addr(&pv_bar));
+      }
+      mma_commit(smem_addr(&final_bar));
+      drain_wait(smem_addr(&final_bar), 0, p.status);
+    }
+  } else {
+    // ----------------------------------------------------- softmax / output
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;
+    const int qrow = qt * BM + r;
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    float m = -INFINITY, l = 0.f;
+    float o[DHP];
+#pragma unroll
+    for (int d = 0; d < DHP; ++d) o[d] = 0.f;
+    bool ok = true;
+    int it = 0;
+    for (int j = j0; j < j1; ++j, ++it) {
+      if (!mbar_wait(smem_addr(&s_bar), it & 1, abort_p, p.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int kbase = j * BN;
+      const int kmax = p.causal ? min(p.T - 1, qrow) : p.T - 1;  // last valid key
+      float tmax = -INFINITY;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t sb[32], ss[32];
+        tmem_ld32(tmem + lane_off + Cfg::S_BIG + c * 32, sb);
+        if (SPLIT3) tmem_ld32(tmem + lane_off + Cfg::S_SMALL + c * 32, ss);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float v = __uint_as_float(sb[i]) + (SPLIT3 ? __uint_as_float(ss[i]) : 0.f);
+          if (kbase + c * 32 + i <= kmax) tmax = fmaxf(tmax, v);
+        }
+      }
+      const float m_new = fmaxf(m, tmax);
+      float lsum = 0.f;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t sb[32], ss[32];
+        tmem_ld32(tmem + lane_off + Cfg::S_BIG + c * 32, sb);
+        if (SPLIT3) tmem_ld32(tmem + lane_off + Cfg::S_SMALL + c * 32, ss);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float v = __uint_as_float(sb[i]) + (SPLIT3 ? __uint_as_float(ss[i]) : 0.f);
+          const float pv = (kbase + c * 32 + i <= kmax) ? fast_exp2(v - m_new) : 0.f;
+          lsum += pv;
+          const float hi = tf32_round(pv);
+          sb[i] = __float_as_uint(hi);
+          ss[i] = __float_as_uint(pv - hi);
+        }
+        tmem_st32(tmem + lane_off + Cfg::S_BIG + c * 32, sb);
+        if (SPLIT3) tmem_st32(tmem + lane_off + Cfg::S_SMALL + c * 32, ss);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&p_bar));
+      const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
+      l = l * alpha + lsum;
+      m = m_new;
+      if (!mbar_wait(smem_addr(&pv_bar), it & 1, abort_p, p.status)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int c = 0; c < DHP / 32; ++c) {
+        uint32_t vb[32], vs[32];
+        tmem_ld32(tmem + lane_off + Cfg::PV_BIG + c * 32, vb);
+        if (SPLIT3) tmem_ld32(tmem + lane_off + Cfg::PV_SMALL + c * 32, vs);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          o[c * 32 + i] = fmaf(o[c * 32 + i], alpha,
+                               __uint_as_float(vb[i]) + (SPLIT3 ? __uint_as_float(vs[i]) : 0.f));
+      }
+      tc_fence_before();
+    }
+    if (ok && qrow < p.L) {
+      if (p.nsplit == 1) {
+        const float inv = 1.f / l;
+        float* orow = p.O + h * p.osH + (int64_t)qrow * p.osT;
+#pragma unroll
+        for (int d = 0; d < DHP; ++d)
+          if (d < p.Dh) orow[d * p.osD] = o[d] * inv;
+      } else {
+        const size_t row = ((size_t)split * p.H + h) * p.L + qrow;
+        float4* dst = reinterpret_cast<float4*>(p.part_o + row * DHP);
+#pragma unroll
+        for (int d = 0; d < DHP; d += 4) dst[d / 4] = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+        p.part_ml[row] = make_float2(m, l);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+// O[h, q, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s.
+__global__ void attn_merge_kernel(const float* __restrict__ part_o,
+                                  const float2* __restrict__ part_ml, int nsplit, int H, int L,
+                                  int Dh, int DHP, float* __restrict__ O, int64_t osH,
+                                  int64_t osT, int64_t osD) {
+  const int64_t n = (int64_t)H * L * Dh;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int d = static_cast<int>(i % Dh);
+    const int64_t hq = i / Dh;
+    const int h = static_cast<int>(hq / L), q = static_cast<int>(hq % L);
+    float M = -INFINITY;
+    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, part_ml[(size_t)s * H * L + hq].x);
+    float num = 0.f, den = 0.f;
+    for (int s = 0; s < nsplit; ++s) {
+      const float2 ml = part_ml[(size_t)s * H * L + hq];
+      if (ml.x == -INFINITY) continue;
+      const float w = fast_exp2(ml.x - M);
+      num += w * part_o[((size_t)s * H * L + hq) * DHP + d];
+      den += w * ml.y;
+    }
+    O[h * osH + (int64_t)q * osT + d * osD] = num / den;
+  }
+}
+
+template <int DHP, bool SPLIT3>
+void launch_attn(const CUtensorMap* maps, const AttnParams& prm, int qtiles, cudaStream_t s) {
+  using Cfg = AttnCfg<DHP, SPLIT3>;
+  static std::atomic<uint64_t> configured{0};
+  int dev = 0;
+  ATTNB_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    ATTNB_CUDA(cudaFuncSetAttribute(attn_tc_kernel<DHP, SPLIT3>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    configured.fetch_or(bit);
+  }
+  const dim3 grid(qtiles, prm.nsplit, prm.H);
+  attn_tc_kernel<DHP, SPLIT3><<<grid, kThreads, Cfg::SMEM, s>>>(maps[0], maps[1], maps[2],
+                                                                maps[3], maps[4], maps[5], prm);
+  ATTNB_CUDA(cudaGetLastError());
+}
+
+template <bool SPLIT3>
+void dispatch_dhp(int dhp, const CUtensorMap* maps, const AttnParams& prm, int qtiles,
+                  cudaStream_t s) {
+  switch (dhp) {
+    case 32: launch_attn<32, SPLIT3>(maps, prm, qtiles, s); break;
+    case 64: launch_attn<64, SPLIT3>(maps, prm, qtiles, s); break;
+    case 96: launch_attn<96, SPLIT3>(maps, prm, qtiles, s); break;
+    case 128: launch_attn<128, SPLIT3>(maps, prm, qtiles, s); break;
+    default: fail(ATTNB_ERR_RUNTIME, "internal: unsupported padded head size");
+  }
+}
+
+}  // namespace
+
+bool attn_tc_supported(int Dh) { return Dh >= 1 && Dh <= 128; }
+
+AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision, int num_sms) {
+  AttnTcPlan p{};
+  p.H = H;
+  p.L = L;
+  p.T = T;
+  p.Dh = Dh;
+  p.dhp = (Dh + 31) / 32 * 32;
+  p.tp = (T + 3) / 4 * 4;
+  p.split3 = precision != ATTNB_PREC_TF32;
+  p.qtiles = (L + BM - 1) / BM;
+  const int n_kv = (T + BN - 1) / BN;
+  // Split the key range when (head, query tile) pairs cannot fill the GPU.
+  const int pairs = H * p.qtiles;
+  int ns = 1;
+  if (!causal && pairs < num_sms) ns = std::min(n_kv, std::max(1, num_sms / pairs));
+  p.tiles_per_split = (n_kv + ns - 1) / ns;
+  p.nsplit = (n_kv + p.tiles_per_split - 1) / p.tiles_per_split;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += (bytes + 255) & ~size_t(255);
+    return o;
+  };
+  const int parts = p.split3 ? 2 : 1;
+  const size_t q = (size_t)H * L * p.dhp * 4, k = (size_t)H * T * p.dhp * 4,
+               v = (size_t)H * p.dhp * p.tp * 4;
+  p.off_q = take(q * parts);
+  p.off_k = take(k * parts);
+  p.off_v = take(v * parts);
+  p.off_po = p.nsplit > 1 ? take((size_t)p.nsplit * H * L * p.dhp * 4) : 0;
+  p.off_pml = p.nsplit > 1 ? take((size_t)p.nsplit * H * L * 8) : 0;
+  p.ws_bytes = off;
+  return p;
+}
+
+void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View3& V,
+                 const MView3& O, bool causal, void* ws, int* status, cudaStream_t s) {
+  char* w = static_cast<char*>(ws);
+  const size_t q = (size_t)p.H * p.L * p.dhp, k = (size_t)p.H * p.T * p.dhp,
+               v = (size_t)p.H * p.dhp * p.tp;
+  float* qh = reinterpret_cast<float*>(w + p.off_q);
+  float* kh = reinterpret_cast<float*>(w + p.off_k);
+  float* vh = reinterpret_cast<float*>(w + p.off_v);
+  float* ql = p.split3 ? qh + q : nullptr;
+  float* kl = p.split3 ? kh + k : nullptr;
+  float* vl = p.split3 ? vh + v : nullptr;
+  const float qscale = kLog2e / std::sqrt(static_cast<float>(p.Dh));
+  pack3_launch(Q.data, Q.sH, Q.sT, Q.sD, p.H, p.L, p.Dh, p.dhp, qscale, qh, ql, p.split3, s);
+  pack3_launch(K.data, K.sH, K.sT, K.sD, p.H, p.T, p.Dh, p.dhp, 1.f, kh, kl, p.split3, s);
+  pack3_transpose_launch(V.data, V.sH, V.sT, V.sD, p.H, p.T, p.Dh, p.tp, p.dhp, vh, vl,
+                         p.split3, s);
+  CUtensorMap maps[6];
+  maps[0] = make_tmap_3d(qh, p.H, p.L, p.dhp, p.dhp, (uint64_t)p.L * p.dhp, BM, BK);
+  maps[2] = make_tmap_3d(kh, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BN, BK);
+  maps[4] = make_tmap_3d(vh, p.H, p.dhp, p.tp, p.tp, (uint64_t)p.dhp * p.tp, p.dhp, BK);
+  if (p.split3) {
+    maps[1] = make_tmap_3d(ql, p.H, p.L, p.dhp, p.dhp, (uint64_t)p.L * p.dhp, BM, BK);
+    maps[3] = make_tmap_3d(kl, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BN, BK);
+    maps[5] = make_tmap_3d(vl, p.H, p.dhp, p.tp, p.tp, (uint64_t)p.dhp * p.tp, p.dhp, BK);
+  } else {
+    maps[1] = maps[0];
+    maps[3] = maps[2];
+    maps[5] = maps[4];
+  }
+  AttnParams prm{};
+  prm.L = p.L;
+  prm.T = p.T;
+  prm.H = p.H;
+  prm.Dh = p.Dh;
+  prm.causal = causal ? 1 : 0;
+  prm.nsplit = p.nsplit;
+  prm.tiles_per_split = p.tiles_per_split;
+  prm.O = O.data;
+  prm.osH = O.sH;
+  prm.osT = O.sT;
+  prm.osD = O.sD;
+  prm.part_o = p.nsplit > 1 ? reinterpret_cast<float*>(w + p.off_po) : nullptr;
+  prm.part_ml = p.nsplit > 1 ? reinterpret_cast<float2*>(w + p.off_pml) : nullptr;
+  prm.status = status;
+  if (p.split3) dispatch_dhp<true>(p.dhp, maps, prm, p.qtiles, s);
+  else dispatch_dhp<false>(p.dhp, maps, prm, p.qtiles, s);
+  if (p.nsplit > 1) {
+    const int64_t n = (int64_t)p.H * p.L * p.Dh;
+    const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 8);
+    attn_merge_kernel<<<blocks, 256, 0, s>>>(prm.part_o, prm.part_ml, p.nsplit, p.H, p.L, p.Dh,
+                                             p.dhp, O.data, O.sH, O.sT, O.sD);
+    ATTNB_CUDA(cudaGetLastError());
+  }
+}
+
+}  // namespace attnb

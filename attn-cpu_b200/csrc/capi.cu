@@ -154,12 +154,26 @@ void step_dev(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* 
 }
 
 // ---------------------------------------------------------------- prefill
+// Head sizes up to 128 take the tcgen05 kernel (any strides: operands are
+// packed first); larger heads the CUDA-core kernel, which needs no scratch.
+size_t block_scratch_bytes(int H, int L, int T, int Dh, bool causal, int prec, int num_sms) {
+  if (L == 0 || !attn_tc_supported(Dh)) return 0;
+  return attn_tc_plan(H, L, T, Dh, causal, prec, num_sms).ws_bytes;
+}
+
 void block_dev(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
-               const attnb_mtensor* O, int causal, int precision, cudaStream_t s) {
-  (void)precision;
+               const attnb_mtensor* O, int causal, int precision, DeviceCtx& c, cudaStream_t s,
+               void* ws) {
   if (Q->T == 0) return;
-  attn_block_simt_launch(view(Q, Q->T), view(K, K->T), view(V, V->T), mview(O, O->T),
-                         causal != 0, s);
+  const View3 q = view(Q, Q->T), k = view(K, K->T), v = view(V, V->T);
+  const MView3 o = mview(O, O->T);
+  if (attn_tc_supported(Q->Dh)) {
+    const AttnTcPlan p =
+        attn_tc_plan(Q->H, Q->T, K->T, Q->Dh, causal != 0, precision, c.num_sms);
+    attn_tc_run(p, q, k, v, o, causal != 0, ws, c.status, s);
+  } else {
+    attn_block_simt_launch(q, k, v, o, causal != 0, s);
+  }
   ATTNB_CUDA(cudaGetLastError());
 }
 
@@ -175,8 +189,11 @@ void mha_dev(const float* x, int batch, int T, int D, const float* W_in, const f
   const size_t off_qkv = cv.take((size_t)rows * 3 * D * sizeof(float));
   const size_t off_ctx = cv.take((size_t)rows * D * sizeof(float));
   const size_t off_g = cv.take(0);
-  // The two projections run one after the other and share the GEMM scratch.
-  const size_t g_bytes = std::max(p_in.ws_bytes, gemm_workspace_bound(rows, D, D, prec));
+  // The projections and the attention run one after the other on the stream
+  // and share one scratch region.
+  const size_t g_bytes =
+      std::max({p_in.ws_bytes, gemm_workspace_bound(rows, D, D, prec),
+                block_scratch_bytes(H, T, T, Dh, causal != 0, prec, c.num_sms)});
   char* w = static_cast<char*>(dev_scratch(c, off_g + g_bytes, s));
   float* qkv = reinterpret_cast<float*>(w + off_qkv);
   float* ctx = reinterpret_cast<float*>(w + off_ctx);
@@ -190,7 +207,7 @@ void mha_dev(const float* x, int batch, int T, int D, const float* W_in, const f
     attnb_tensor k{base + D, H, T, Dh, Dh, 3 * D, 1};
     attnb_tensor v{base + 2 * D, H, T, Dh, Dh, 3 * D, 1};
     attnb_mtensor o{ctx + (size_t)b * T * D, H, T, Dh, Dh, D, 1};
-    block_dev(&q, &k, &v, &o, causal, prec, s);
+    block_dev(&q, &k, &v, &o, causal, prec, c, s, gws);
   }
   // 3) y = ctx . W_out^T + b_out   (:110-127)
   const GemmPlan p_out = gemm_plan(rows, D, D, ctx, D, true, W_out, D, true, prec);
@@ -346,7 +363,11 @@ int attnb_attn_block_dense_dev(const attnb_tensor* Q, const attnb_tensor* K,
   return guarded([&] {
     validate_block(Q, K, V, O, causal);
     const int prec = resolve_precision(precision);
-    block_dev(Q, K, V, O, causal, prec, as_stream(stream));
+    DeviceCtx& c = current_ctx();
+    cudaStream_t s = as_stream(stream);
+    void* ws = dev_scratch(c, block_scratch_bytes(Q->H, Q->T, K->T, Q->Dh, causal != 0, prec,
+                                                  c.num_sms), s);
+    block_dev(Q, K, V, O, causal, prec, c, s, ws);
   });
 }
 
@@ -378,7 +399,9 @@ int attnb_attn_block_dense(const attnb_tensor* Q, const attnb_tensor* K, const a
       dv.data = put(V->data, sv, ov);
       if (so.count() != (int64_t)O->H * O->T * O->Dh) put(O->data, so, oo);
       dO.data = reinterpret_cast<float*>(base + oo) - so.lo;
-      block_dev(&dq, &dk, &dv, &dO, causal, prec, s);
+      void* ws = c.scratch_host_path.ensure(
+          block_scratch_bytes(Q->H, Q->T, K->T, Q->Dh, causal != 0, prec, c.num_sms) + 256, s);
+      block_dev(&dq, &dk, &dv, &dO, causal, prec, c, s, ws);
       ATTNB_CUDA(cudaMemcpyAsync(O->data + so.lo, base + oo, so.count() * 4,
                                  cudaMemcpyDeviceToHost, s));
       finish_host_call(c);

@@ -12,13 +12,18 @@
 //   warp 0      TMA producer: fills a STAGES-deep shared-memory ring with
 //               128-byte-swizzled 32-wide K slices of A (and B), signalling
 //               `full[s]` with the transaction byte count;
-//   warp 1      allocates 2*BN TMEM columns (two accumulators), then one
-//               lane issues tcgen05.mma (4 K-steps of 8 per slice, x3 terms
-//               in 3xTF32 mode) and tcgen05.commit's the slice back to the
-//               producer (`empty[s]`) and the finished tile to the epilogue;
+//   warp 1      allocates all 512 TMEM columns (two accumulator slots), then
+//               one lane issues tcgen05.mma (4 K-steps of 8 per slice) and
+//               tcgen05.commit's each slice back to the producer (`empty[s]`)
+//               and each finished accumulator to the epilogue;
 //   warps 2-5   epilogue: tcgen05.ld the accumulator (lane = row), apply
-//               alpha / beta / bias, store to C, release the accumulator.
-// Two accumulators let the epilogue of tile i overlap the MMAs of tile i+1.
+//               alpha / beta / bias, store to C, release the slot.
+// 1xTF32: one 128x256 accumulator per tile; the two slots let the epilogue of
+// tile i overlap the MMAs of tile i+1.
+// 3xTF32 (128x128 tiles): hi*hi goes to a "big" accumulator and
+// hi*lo + lo*hi to a separate "small" one, and both are drained into fp32
+// registers every 256 K values, alternating slots, so the epilogue's
+// round-to-nearest fp32 sums carry the long-K accumulation.
 #include <algorithm>
 #include <atomic>
 
@@ -41,9 +46,18 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = (SPLIT3 ? 2 : 1) * (A_BYTES + B_BYTES);
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;    // + alignment slack
-  static constexpr int TMEM_COLS = 2 * BN;
+  // Two accumulator slots; in 3xTF32 mode each slot holds a "big" (hi*hi)
+  // and a "small" (hi*lo + lo*hi) accumulator.
+  static constexpr int SLOT_COLS = (SPLIT3 ? 2 : 1) * BN;
+  static constexpr int TMEM_COLS = 2 * SLOT_COLS;
   static_assert(STAGES >= 2, "pipeline needs two stages");
+  static_assert(TMEM_COLS <= 512, "TMEM has 512 columns");
 };
+
+// 3xTF32 drains its TMEM accumulators into fp32 registers every KB_CHUNK
+// K-slices (256 K values): the tensor core's own accumulation truncates, so
+// long K runs inside TMEM would drift by up to ~1e-5 relative at K = 4096.
+constexpr int KB_CHUNK = 8;
 
 __device__ __forceinline__ void tile_coords(int tile, int tiles_m, int tiles_n, int& tm, int& tn) {
   const int per_group = GROUP_M * tiles_n;
@@ -63,6 +77,35 @@ __device__ __forceinline__ void mbar_drain(uint32_t bar, uint32_t parity, int* s
       raise_timeout(status);
       return;
     }
+  }
+}
+
+// Epilogue for 32 consecutive columns of one output row.
+__device__ __forceinline__ void store32(float* crow, int row, int col0, const float* acc, int M,
+                                        int N, float alpha, float beta,
+                                        const float* __restrict__ bias, bool c_vec) {
+  if (row >= M) return;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = alpha * acc[j];
+  if (beta != 0.f) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < N) v[j] = fmaf(beta, crow[col0 + j], v[j]);
+  }
+  if (bias) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < N) v[j] += __ldg(bias + col0 + j);
+  }
+  if (c_vec && col0 + 32 <= N) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4)
+      *reinterpret_cast<float4*>(crow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < N) crow[col0 + j] = v[j];
   }
 }
 
@@ -98,6 +141,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
   const int num_tiles = tiles_m * tiles_n;
   const int num_kb = Kp / BK;
+  // Accumulator hand-offs per tile: one per K chunk (3xTF32) or one per tile.
+  const int nchunks = SPLIT3 ? (num_kb + KB_CHUNK - 1) / KB_CHUNK : 1;
+  const int kb_per_chunk = SPLIT3 ? KB_CHUNK : num_kb;
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
@@ -172,38 +218,47 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      int it = 0;
-      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x, ++it) {
-        const int buf = it & 1;
-        const uint32_t use = (it >> 1) & 1;
-        if (!mbar_wait(smem_addr(&tempty_bar[buf]), use ^ 1u, abort_p, status)) break;
-        tc_fence_after();
-        const uint32_t d_tmem = tmem_base + buf * BN;
-        for (int kb = 0; kb < num_kb; ++kb) {
-          if (!mbar_wait(smem_addr(&full_bar[stage]), phase, abort_p, status)) {
+      int g = 0;  // accumulator hand-offs so far
+      for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
+        for (int c = 0; ok && c < nchunks; ++c, ++g) {
+          const int slot = g & 1;
+          const uint32_t use = (g >> 1) & 1;
+          if (!mbar_wait(smem_addr(&tempty_bar[slot]), use ^ 1u, abort_p, status)) {
             ok = false;
             break;
           }
           tc_fence_after();
+          const uint32_t d_big = tmem_base + slot * Cfg::SLOT_COLS;
+          const uint32_t d_small = d_big + BN;
+          const int kb0 = c * kb_per_chunk;
+          const int kb1 = min(num_kb, kb0 + kb_per_chunk);
+          for (int kb = kb0; kb < kb1; ++kb) {
+            if (!mbar_wait(smem_addr(&full_bar[stage]), phase, abort_p, status)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
 #pragma unroll
-          for (int kk = 0; kk < BK / 8; ++kk) {
-            const uint64_t a_hi = sdesc_kmajor_sw128(sA_hi(stage) + kk * 32);
-            const uint64_t b_hi = sdesc_kmajor_sw128(sB_hi(stage) + kk * 32);
-            mma_tf32(d_tmem, a_hi, b_hi, IDESC, (kb | kk) != 0 ? 1u : 0u);
-            if (SPLIT3) {
-              const uint64_t a_lo = sdesc_kmajor_sw128(sA_lo(stage) + kk * 32);
-              const uint64_t b_lo = sdesc_kmajor_sw128(sB_lo(stage) + kk * 32);
-              mma_tf32(d_tmem, a_hi, b_lo, IDESC, 1u);
-              mma_tf32(d_tmem, a_lo, b_hi, IDESC, 1u);
+            for (int kk = 0; kk < BK / 8; ++kk) {
+              const uint32_t acc = (kb != kb0 || kk != 0) ? 1u : 0u;
+              const uint64_t a_hi = sdesc_kmajor_sw128(sA_hi(stage) + kk * 32);
+              const uint64_t b_hi = sdesc_kmajor_sw128(sB_hi(stage) + kk * 32);
+              mma_tf32(d_big, a_hi, b_hi, IDESC, acc);
+              if (SPLIT3) {
+                const uint64_t a_lo = sdesc_kmajor_sw128(sA_lo(stage) + kk * 32);
+                const uint64_t b_lo = sdesc_kmajor_sw128(sB_lo(stage) + kk * 32);
+                mma_tf32(d_small, a_hi, b_lo, IDESC, acc);
+                mma_tf32(d_small, a_lo, b_hi, IDESC, 1u);
+              }
+            }
+            mma_commit(smem_addr(&empty_bar[stage]));
+            if (++stage == STAGES) {
+              stage = 0;
+              phase ^= 1u;
             }
           }
-          mma_commit(smem_addr(&empty_bar[stage]));
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          if (ok) mma_commit(smem_addr(&tfull_bar[slot]));
         }
-        if (ok) mma_commit(smem_addr(&tfull_bar[buf]));
       }
       // Every MMA issued above has finished before TMEM is released.
       mma_commit(smem_addr(&final_bar));
@@ -212,50 +267,65 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // -------------------------------------------------------------- epilogue
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
+    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const bool c_vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
-    int it = 0;
-    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+    int g = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
       int tm, tn;
       tile_coords(tile, tiles_m, tiles_n, tm, tn);
-      const int buf = it & 1;
-      const uint32_t use = (it >> 1) & 1;
-      if (!mbar_wait(smem_addr(&tfull_bar[buf]), use, abort_p, status)) break;
-      tc_fence_after();
       const int row = tm * BM + quarter * 32 + lane;
       float* crow = C + (int64_t)row * ldc;
+      if constexpr (SPLIT3) {
+        float acc[BN];
+#pragma unroll
+        for (int i = 0; i < BN; ++i) acc[i] = 0.f;
+        for (int c = 0; c < nchunks; ++c, ++g) {
+          const int slot = g & 1;
+          const uint32_t use = (g >> 1) & 1;
+          if (!mbar_wait(smem_addr(&tfull_bar[slot]), use, abort_p, status)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t tb = tmem_base + lane_off + slot * Cfg::SLOT_COLS;
+#pragma unroll
+          for (int j = 0; j < BN / 32; ++j) {
+            uint32_t rb[32], rs[32];
+            tmem_ld32(tb + j * 32, rb);
+            tmem_ld32(tb + BN + j * 32, rs);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              acc[j * 32 + i] += __uint_as_float(rb[i]) + __uint_as_float(rs[i]);
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_addr(&tempty_bar[slot]));
+        }
+        if (!ok) break;
+#pragma unroll
+        for (int j = 0; j < BN / 32; ++j)
+          store32(crow, row, tn * BN + j * 32, &acc[j * 32], M, N, alpha, beta, bias, c_vec);
+      } else {
+        const int slot = g & 1;
+        const uint32_t use = (g >> 1) & 1;
+        if (!mbar_wait(smem_addr(&tfull_bar[slot]), use, abort_p, status)) break;
+        tc_fence_after();
+        const uint32_t tb = tmem_base + lane_off + slot * Cfg::SLOT_COLS;
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem_base + ((uint32_t)(quarter * 32) << 16) + buf * BN + c * 32, r);
-        const int col0 = tn * BN + c * 32;
-        if (row < M) {
+        for (int j = 0; j < BN / 32; ++j) {
+          uint32_t r[32];
+          tmem_ld32(tb + j * 32, r);
           float v[32];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = alpha * __uint_as_float(r[j]);
-          if (beta != 0.f) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < N) v[j] = fmaf(beta, crow[col0 + j], v[j]);
-          }
-          if (bias) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < N) v[j] += __ldg(bias + col0 + j);
-          }
-          if (c_vec && col0 + 32 <= N) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              *reinterpret_cast<float4*>(crow + col0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (col0 + j < N) crow[col0 + j] = v[j];
-          }
+          for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+          store32(crow, row, tn * BN + j * 32, v, M, N, alpha, beta, bias, c_vec);
         }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_addr(&tempty_bar[slot]));
+        ++g;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&tempty_bar[buf]));
     }
   }
 

@@ -39,6 +39,19 @@ void decode_launch(const DecodePlan& p, const View3& Q, const View3& K, const Vi
 void attn_block_simt_launch(const View3& Q, const View3& K, const View3& V, const MView3& O,
                             bool causal, cudaStream_t stream);
 
+// ---------------------------------------- tcgen05 prefill attention (K3)
+struct AttnTcPlan {
+  int H, L, T, Dh, dhp, tp, qtiles, nsplit, tiles_per_split;
+  bool split3;
+  size_t off_q, off_k, off_v, off_po, off_pml, ws_bytes;
+};
+// Head sizes the tensor-core kernel takes (padded to a multiple of 32, <= 128).
+bool attn_tc_supported(int Dh);
+AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision, int num_sms);
+// `ws` holds plan.ws_bytes bytes (packed operands and split partials).
+void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View3& V,
+                 const MView3& O, bool causal, void* ws, int* status, cudaStream_t s);
+
 // ------------------------------------------------ operand packing (K2)
 // src[rows, cols] (pitch ld) -> hi/lo[rows, kp]; cols..kp-1 zero.
 void pack_rows_launch(const float* src, int64_t ld, int rows, int cols, int kp, float* hi,
@@ -46,6 +59,14 @@ void pack_rows_launch(const float* src, int64_t ld, int rows, int cols, int kp, 
 // src[K, N] (pitch ld) -> hi/lo[N, kp] (transposed); K..kp-1 zero.
 void pack_transpose_launch(const float* src, int64_t ld, int K, int N, int kp, float* hi,
                            float* lo, bool split3, cudaStream_t s);
+
+// 3-D strided src[h, r, c] -> hi/lo[h, r, cp] (times `scale`), c >= C zero.
+void pack3_launch(const float* src, int64_t sH, int64_t sR, int64_t sC, int H, int R, int C,
+                  int cp, float scale, float* hi, float* lo, bool split3, cudaStream_t s);
+// 3-D strided src[h, t, d] -> hi/lo[h, d, tp] for d < dp, zero outside [T, D).
+void pack3_transpose_launch(const float* src, int64_t sH, int64_t sT, int64_t sD, int H, int T,
+                            int D, int tp, int dp, float* hi, float* lo, bool split3,
+                            cudaStream_t s);
 
 // --------------------------------------------------- tcgen05 GEMM (K1)
 // C[M,N] = alpha * A.B + beta * C (+ bias[n]).  A is [M,K] (a_kmajor: rows of

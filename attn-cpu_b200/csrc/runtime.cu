@@ -125,6 +125,29 @@ CUtensorMap make_tmap_2d(const float* base, uint64_t rows, uint64_t cols, uint64
   return m;
 }
 
+CUtensorMap make_tmap_3d(const float* base, uint64_t depth, uint64_t rows, uint64_t cols,
+                         uint64_t ld, uint64_t ld_depth, uint32_t box_rows, uint32_t box_cols) {
+  if ((reinterpret_cast<uintptr_t>(base) & 15u) != 0)
+    fail(ATTNB_ERR_RUNTIME, "TMA base address is not 16-byte aligned");
+  if ((ld * sizeof(float)) % 16 != 0 || (ld_depth * sizeof(float)) % 16 != 0)
+    fail(ATTNB_ERR_RUNTIME, "TMA pitch is not 16-byte aligned");
+  if (box_cols * sizeof(float) > 128 || box_rows > 256 || box_rows == 0 || box_cols == 0)
+    fail(ATTNB_ERR_RUNTIME, "TMA box exceeds the 128-byte swizzle span");
+  CUtensorMap m;
+  std::memset(&m, 0, sizeof(m));
+  const cuuint64_t dims[3] = {cols, rows, depth};
+  const cuuint64_t strides[2] = {ld * sizeof(float), ld_depth * sizeof(float)};
+  const cuuint32_t box[3] = {box_cols, box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<float*>(base), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    fail(ATTNB_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (" + std::to_string((int)r) + ")");
+  return m;
+}
+
 int consume_status(DeviceCtx& c, cudaStream_t stream) {
   int h = 0;
   ATTNB_CUDA(cudaMemcpyAsync(&h, c.status, sizeof(int), cudaMemcpyDeviceToHost, stream));

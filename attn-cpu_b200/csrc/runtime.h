@@ -62,6 +62,12 @@ int resolve_precision(int precision);
 CUtensorMap make_tmap_2d(const float* base, uint64_t rows, uint64_t cols, uint64_t ld,
                          uint32_t box_rows, uint32_t box_cols);
 
+// 3-D fp32 tensor map over [depth, rows, cols] (cols contiguous, row pitch
+// ld elements, depth pitch ld_depth elements), box 1 x box_rows x box_cols,
+// 128-byte swizzle; out-of-range elements (per depth slice) read as 0.
+CUtensorMap make_tmap_3d(const float* base, uint64_t depth, uint64_t rows, uint64_t cols,
+                         uint64_t ld, uint64_t ld_depth, uint32_t box_rows, uint32_t box_cols);
+
 // Reads and clears the device status word of ctx (synchronises `stream`).
 int consume_status(DeviceCtx& c, cudaStream_t stream);
 

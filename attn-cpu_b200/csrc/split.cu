@@ -71,7 +71,79 @@ __global__ void pack_transpose_kernel(const float* __restrict__ src, int64_t ld,
   }
 }
 
+// 3-D strided src[h, r, c] (r < R, c < C) -> hi/lo[h, r, cp] scaled by `scale`,
+// columns C..cp-1 zero.  One thread writes 4 output columns.
+__global__ void pack3_kernel(const float* __restrict__ src, int64_t sH, int64_t sR, int64_t sC,
+                             int H, int R, int C, int cp, float scale, float* __restrict__ hi,
+                             float* __restrict__ lo, int split3) {
+  const int cp4 = cp >> 2;
+  const int64_t n = (int64_t)H * R * cp4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t hr = i / cp4;
+    const int c = static_cast<int>(i % cp4) * 4;
+    const int h = static_cast<int>(hr / R), r = static_cast<int>(hr % R);
+    const float* s = src + h * sH + r * sR;
+    float x[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) x[j] = (c + j < C) ? s[(c + j) * sC] * scale : 0.f;
+    float4 h4, l4;
+    split_value(x[0], split3, h4.x, l4.x);
+    split_value(x[1], split3, h4.y, l4.y);
+    split_value(x[2], split3, h4.z, l4.z);
+    split_value(x[3], split3, h4.w, l4.w);
+    reinterpret_cast<float4*>(hi + hr * cp)[c >> 2] = h4;
+    if (split3) reinterpret_cast<float4*>(lo + hr * cp)[c >> 2] = l4;
+  }
+}
+
+// 3-D strided src[h, t, d] (t < T, d < D) -> hi/lo[h, d, tp] for d < dp
+// (transposed per head), zero outside t < T, d < D.  32x32 tiles, block (32, 8).
+__global__ void pack3_transpose_kernel(const float* __restrict__ src, int64_t sH, int64_t sT,
+                                       int64_t sD, int T, int D, int tp, int dp,
+                                       float* __restrict__ hi, float* __restrict__ lo,
+                                       int split3) {
+  __shared__ float tile[32][33];
+  const int h = blockIdx.z;
+  const int d0 = blockIdx.x * 32, t0 = blockIdx.y * 32;
+  const float* s = src + h * sH;
+  for (int j = threadIdx.y; j < 32; j += 8) {
+    const int t = t0 + j, d = d0 + threadIdx.x;
+    tile[j][threadIdx.x] = (t < T && d < D) ? s[t * sT + d * sD] : 0.f;
+  }
+  __syncthreads();
+  float* oh = hi + (int64_t)h * dp * tp;
+  float* ol = split3 ? lo + (int64_t)h * dp * tp : nullptr;
+  for (int j = threadIdx.y; j < 32; j += 8) {
+    const int d = d0 + j, t = t0 + threadIdx.x;
+    if (d < dp && t < tp) {
+      float hv, lv;
+      split_value(tile[threadIdx.x][j], split3, hv, lv);
+      oh[(int64_t)d * tp + t] = hv;
+      if (split3) ol[(int64_t)d * tp + t] = lv;
+    }
+  }
+}
+
 }  // namespace
+
+void pack3_launch(const float* src, int64_t sH, int64_t sR, int64_t sC, int H, int R, int C,
+                  int cp, float scale, float* hi, float* lo, bool split3, cudaStream_t s) {
+  const int64_t n = (int64_t)H * R * (cp / 4);
+  if (n <= 0) return;
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 148 * 16);
+  pack3_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(src, sH, sR, sC, H, R, C, cp, scale,
+                                                              hi, lo, split3 ? 1 : 0);
+}
+
+void pack3_transpose_launch(const float* src, int64_t sH, int64_t sT, int64_t sD, int H, int T,
+                            int D, int tp, int dp, float* hi, float* lo, bool split3,
+                            cudaStream_t s) {
+  if (H <= 0 || tp <= 0 || dp <= 0) return;
+  const dim3 grid((dp + 31) / 32, (tp + 31) / 32, H);
+  pack3_transpose_kernel<<<grid, dim3(32, 8), 0, s>>>(src, sH, sT, sD, T, D, tp, dp, hi, lo,
+                                                      split3 ? 1 : 0);
+}
 
 void pack_rows_launch(const float* src, int64_t ld, int rows, int cols, int kp, float* hi,
                       float* lo, bool split3, cudaStream_t s) {

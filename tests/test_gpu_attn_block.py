@@ -24,6 +24,8 @@ def _qkv(H, L, T, Dh, seed):
     (2, 65, 65, 16, False), (2, 66, 66, 16, True), (3, 100, 37, 32, False),
     (4, 128, 128, 128, False), (4, 200, 200, 128, True), (1, 1, 1, 64, False),
     (2, 33, 300, 96, False), (1, 70, 70, 48, True), (2, 129, 129, 64, True),
+    (32, 256, 256, 128, False), (2, 300, 300, 32, True), (1, 1000, 1000, 64, False),
+    (2, 100, 100, 200, False), (1, 70, 70, 160, True),   # head sizes > 128: CUDA-core kernel
 ])
 def test_block_vs_oracle(cuda, H, L, T, Dh, causal):
     import attn_cpu
