@@ -184,7 +184,7 @@ void mha_dev(const float* x, int batch, int T, int D, const float* W_in, const f
   if (batch <= 0 || T <= 0) return;
   const int Dh = D / H;
   const int rows = batch * T;
-  const GemmPlan p_in = gemm_plan(rows, 3 * D, D, x, D, true, W_in, D, true, prec);
+  const GemmPlan p_in = gemm_plan(rows, 3 * D, D, prec);
   Carver cv;
   const size_t off_qkv = cv.take((size_t)rows * 3 * D * sizeof(float));
   const size_t off_ctx = cv.take((size_t)rows * D * sizeof(float));
@@ -210,7 +210,7 @@ void mha_dev(const float* x, int batch, int T, int D, const float* W_in, const f
     block_dev(&q, &k, &v, &o, causal, prec, c, s, gws);
   }
   // 3) y = ctx . W_out^T + b_out   (:110-127)
-  const GemmPlan p_out = gemm_plan(rows, D, D, ctx, D, true, W_out, D, true, prec);
+  const GemmPlan p_out = gemm_plan(rows, D, D, prec);
   gemm_run(p_out, ctx, D, true, W_out, D, true, y, D, 1.f, 0.f, b_out, gws, c.status, c.num_sms, s);
 }
 
@@ -241,7 +241,7 @@ int attnb_sgemm_dev(const float* A, int lda, const float* B, int ldb, float* C, 
     const int prec = resolve_precision(precision);
     DeviceCtx& c = current_ctx();
     cudaStream_t s = as_stream(stream);
-    const GemmPlan p = gemm_plan(M, N, K, A, lda, true, B, ldb, false, prec);
+    const GemmPlan p = gemm_plan(M, N, K, prec);
     void* ws = dev_scratch(c, p.ws_bytes, s);
     gemm_run(p, A, lda, true, B, ldb, false, C, ldc, alpha, beta, nullptr, ws, c.status,
              c.num_sms, s);
@@ -259,7 +259,7 @@ int attnb_linear_dev(const float* x, int ldx, const float* W, int ldw, const flo
     const int prec = resolve_precision(precision);
     DeviceCtx& c = current_ctx();
     cudaStream_t s = as_stream(stream);
-    const GemmPlan p = gemm_plan(T, N, K, x, ldx, true, W, ldw, true, prec);
+    const GemmPlan p = gemm_plan(T, N, K, prec);
     void* ws = dev_scratch(c, p.ws_bytes, s);
     gemm_run(p, x, ldx, true, W, ldw, true, y, ldy, 1.f, 0.f, b, ws, c.status, c.num_sms, s);
     ATTNB_CUDA(cudaGetLastError());
@@ -283,7 +283,7 @@ static int sgemm_host(const float* A, int M, int K, const float* B, int N, float
       float* dA = reinterpret_cast<float*>(base + oa);
       float* dB = reinterpret_cast<float*>(base + ob);
       float* dC = reinterpret_cast<float*>(base + oc);
-      const GemmPlan p = gemm_plan(M, N, K, dA, K, true, dB, N, false, prec);
+      const GemmPlan p = gemm_plan(M, N, K, prec);
       void* ws = c.scratch_host_path.ensure(p.ws_bytes + 256, s);
       if (alpha != 0.f) {
         ATTNB_CUDA(cudaMemcpyAsync(dA, A, a * 4, cudaMemcpyHostToDevice, s));

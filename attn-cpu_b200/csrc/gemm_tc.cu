@@ -373,23 +373,16 @@ void launch_gemm(const GemmPlan& p, const CUtensorMap& a_hi, const CUtensorMap& 
 
 }  // namespace
 
-int gemm_block_n(int precision) { return precision == ATTNB_PREC_TF32 ? 256 : 128; }
-
-GemmPlan gemm_plan(int M, int N, int K, const float* A, int64_t lda, bool a_kmajor,
-                   const float* B, int64_t ldb, bool b_kmajor, int precision) {
+GemmPlan gemm_plan(int M, int N, int K, int precision) {
   GemmPlan p{};
   p.M = M;
   p.N = N;
   p.K = K;
   p.Kp = (K + BK - 1) / BK * BK;
   p.split3 = precision != ATTNB_PREC_TF32;
-  // A 1xTF32 operand that is already K-major with a 16-byte-aligned base and
-  // pitch is read in place (the tensor core reads its tf32 part).
-  auto direct = [&](const float* X, int64_t ld, bool kmajor) {
-    return !p.split3 && kmajor && (reinterpret_cast<uintptr_t>(X) & 15u) == 0 && (ld % 4) == 0;
-  };
-  p.a_direct = direct(A, lda, a_kmajor);
-  p.b_direct = direct(B, ldb, b_kmajor);
+  // Both operands are always packed: round-to-nearest tf32 (the tensor core
+  // would otherwise truncate an fp32 operand read in place, which doubles and
+  // biases the 1xTF32 error), K-major, K padded to a multiple of 32.
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -398,19 +391,12 @@ GemmPlan gemm_plan(int M, int N, int K, const float* A, int64_t lda, bool a_kmaj
   };
   const size_t a_bytes = (size_t)M * p.Kp * sizeof(float);
   const size_t b_bytes = (size_t)N * p.Kp * sizeof(float);
-  p.off_a_hi = p.a_direct ? 0 : take(a_bytes);
+  p.off_a_hi = take(a_bytes);
   p.off_a_lo = p.split3 ? take(a_bytes) : 0;
-  p.off_b_hi = p.b_direct ? 0 : take(b_bytes);
+  p.off_b_hi = take(b_bytes);
   p.off_b_lo = p.split3 ? take(b_bytes) : 0;
   p.ws_bytes = off;
   return p;
-}
-
-size_t gemm_workspace_bound(int M, int N, int K, int precision) {
-  const size_t kp = (size_t)(K + BK - 1) / BK * BK;
-  const size_t a = ((size_t)M * kp * sizeof(float) + 255) & ~size_t(255);
-  const size_t b = ((size_t)N * kp * sizeof(float) + 255) & ~size_t(255);
-  return (precision == ATTNB_PREC_TF32 ? 1 : 2) * (a + b);
 }
 
 void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, const float* B,
@@ -426,26 +412,17 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
     return;
   }
   char* w = static_cast<char*>(ws);
-  const float* a_hi = p.a_direct ? A : reinterpret_cast<float*>(w + p.off_a_hi);
-  const float* b_hi = p.b_direct ? B : reinterpret_cast<float*>(w + p.off_b_hi);
+  float* a_hi = reinterpret_cast<float*>(w + p.off_a_hi);
+  float* b_hi = reinterpret_cast<float*>(w + p.off_b_hi);
   float* a_lo = p.split3 ? reinterpret_cast<float*>(w + p.off_a_lo) : nullptr;
   float* b_lo = p.split3 ? reinterpret_cast<float*>(w + p.off_b_lo) : nullptr;
-  // Operand packing (tf32 rounding / hi-lo split, K-major, K padded to 32).
-  if (!p.a_direct) {
-    if (a_kmajor) pack_rows_launch(A, lda, p.M, p.K, p.Kp, const_cast<float*>(a_hi), a_lo, p.split3, s);
-    else pack_transpose_launch(A, lda, p.K, p.M, p.Kp, const_cast<float*>(a_hi), a_lo, p.split3, s);
-  }
-  if (!p.b_direct) {
-    if (b_kmajor) pack_rows_launch(B, ldb, p.N, p.K, p.Kp, const_cast<float*>(b_hi), b_lo, p.split3, s);
-    else pack_transpose_launch(B, ldb, p.K, p.N, p.Kp, const_cast<float*>(b_hi), b_lo, p.split3, s);
-  }
-  // Tensor maps: a direct operand keeps its own pitch and true K (the copy
-  // engine zero-fills past K); packed operands are [rows, Kp].
+  if (a_kmajor) pack_rows_launch(A, lda, p.M, p.K, p.Kp, a_hi, a_lo, p.split3, s);
+  else pack_transpose_launch(A, lda, p.K, p.M, p.Kp, a_hi, a_lo, p.split3, s);
+  if (b_kmajor) pack_rows_launch(B, ldb, p.N, p.K, p.Kp, b_hi, b_lo, p.split3, s);
+  else pack_transpose_launch(B, ldb, p.K, p.N, p.Kp, b_hi, b_lo, p.split3, s);
   const int bn = p.split3 ? 128 : 256;
-  const CUtensorMap tA_hi = p.a_direct ? make_tmap_2d(a_hi, p.M, p.K, lda, BM, BK)
-                                       : make_tmap_2d(a_hi, p.M, p.Kp, p.Kp, BM, BK);
-  const CUtensorMap tB_hi = p.b_direct ? make_tmap_2d(b_hi, p.N, p.K, ldb, bn, BK)
-                                       : make_tmap_2d(b_hi, p.N, p.Kp, p.Kp, bn, BK);
+  const CUtensorMap tA_hi = make_tmap_2d(a_hi, p.M, p.Kp, p.Kp, BM, BK);
+  const CUtensorMap tB_hi = make_tmap_2d(b_hi, p.N, p.Kp, p.Kp, bn, BK);
   if (p.split3) {
     const CUtensorMap tA_lo = make_tmap_2d(a_lo, p.M, p.Kp, p.Kp, BM, BK);
     const CUtensorMap tB_lo = make_tmap_2d(b_lo, p.N, p.Kp, p.Kp, bn, BK);
@@ -455,6 +432,10 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
     launch_gemm<256, false>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias, status,
                             num_sms, s);
   }
+}
+
+size_t gemm_workspace_bound(int M, int N, int K, int precision) {
+  return gemm_plan(M, N, K, precision).ws_bytes;
 }
 
 }  // namespace attnb

@@ -73,12 +73,11 @@ void pack3_transpose_launch(const float* src, int64_t sH, int64_t sT, int64_t sD
 // K, pitch lda) or [K,M] (pitch lda); B is [N,K] (b_kmajor) or [K,N].
 struct GemmPlan {
   int M, N, K, Kp;
-  bool split3, a_direct, b_direct;
+  bool split3;
   size_t off_a_hi, off_a_lo, off_b_hi, off_b_lo, ws_bytes;
 };
-GemmPlan gemm_plan(int M, int N, int K, const float* A, int64_t lda, bool a_kmajor,
-                   const float* B, int64_t ldb, bool b_kmajor, int precision);
-// Scratch bytes of any plan of this size (no operand read in place).
+GemmPlan gemm_plan(int M, int N, int K, int precision);
+// Scratch bytes of a plan of this size.
 size_t gemm_workspace_bound(int M, int N, int K, int precision);
 void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, const float* B,
               int64_t ldb, bool b_kmajor, float* C, int64_t ldc, float alpha, float beta,
