@@ -72,11 +72,12 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* s
 }
 
 struct AttnParams {
-  int L, T, H, Dh, causal, nsplit, tiles_per_split;
+  int L, T, H, Dh, causal, nsplit, tiles_per_split, qtiles;
   float* O;
   int64_t osH, osT, osD;
-  float* part_o;    // [nsplit, H, L, DHP] (nsplit > 1)
-  float2* part_ml;  // [nsplit, H, L]
+  float* part_o;       // [nsplit, H, L, DHP] (nsplit > 1)
+  float2* part_ml;     // [nsplit, H, L]
+  unsigned* counters;  // [H, qtiles] finished splits, cleared by the pack kernel
   int* status;
 };
 
@@ -132,6 +133,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
   volatile int* abort_p = &abort_flag;
+  grid_dep_wait();  // packed operands and cleared counters come from the pack kernel
 
   if (warp == 0) {
     if (lane == 0) {
@@ -331,19 +333,63 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
     }
-    if (ok && qrow < p.L) {
-      if (p.nsplit == 1) {
+    if (p.nsplit == 1) {
+      if (ok && qrow < p.L) {
         const float inv = 1.f / l;
         float* orow = p.O + h * p.osH + (int64_t)qrow * p.osT;
 #pragma unroll
         for (int d = 0; d < DHP; ++d)
           if (d < p.Dh) orow[d * p.osD] = o[d] * inv;
-      } else {
+      }
+    } else if (ok) {
+      // Publish this split's (m, l, O); the CTA that finishes a (head, query
+      // tile) last merges all splits:  O = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s.
+      if (qrow < p.L) {
         const size_t row = ((size_t)split * p.H + h) * p.L + qrow;
         float4* dst = reinterpret_cast<float4*>(p.part_o + row * DHP);
 #pragma unroll
         for (int d = 0; d < DHP; d += 4) dst[d / 4] = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
         p.part_ml[row] = make_float2(m, l);
+      }
+      __threadfence();
+      named_bar_sync(1, 128);
+      __shared__ int s_last;
+      unsigned* cnt = p.counters + (size_t)h * p.qtiles + qt;
+      if (r == 0) s_last = (atomicAdd(cnt, 1u) == (unsigned)(p.nsplit - 1));
+      named_bar_sync(1, 128);
+      if (s_last) {
+        __threadfence();
+        if (qrow < p.L) {
+          const size_t hs = (size_t)p.H * p.L, base_row = (size_t)h * p.L + qrow;
+          float M = -INFINITY;
+          for (int sp = 0; sp < p.nsplit; ++sp) M = fmaxf(M, __ldcg(&p.part_ml[sp * hs + base_row]).x);
+          float den = 0.f;
+          for (int sp = 0; sp < p.nsplit; ++sp) {
+            const float2 ml = __ldcg(&p.part_ml[sp * hs + base_row]);
+            if (ml.x != -INFINITY) den += fast_exp2(ml.x - M) * ml.y;
+          }
+          const float inv = 1.f / den;
+          float* orow = p.O + h * p.osH + (int64_t)qrow * p.osT;
+          for (int d = 0; d < p.Dh; d += 4) {
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int sp = 0; sp < p.nsplit; ++sp) {
+              const float2 ml = __ldcg(&p.part_ml[sp * hs + base_row]);
+              if (ml.x == -INFINITY) continue;
+              const float w = fast_exp2(ml.x - M);
+              const float4 v = __ldcg(reinterpret_cast<const float4*>(
+                  p.part_o + (sp * hs + base_row) * DHP + d));
+              acc.x = fmaf(w, v.x, acc.x);
+              acc.y = fmaf(w, v.y, acc.y);
+              acc.z = fmaf(w, v.z, acc.z);
+              acc.w = fmaf(w, v.w, acc.w);
+            }
+            const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              if (d + k < p.Dh) orow[(d + k) * p.osD] = a4[k] * inv;
+          }
+        }
+        if (r == 0) *cnt = 0u;  // cleared again for the next call
       }
     }
   }
@@ -354,31 +400,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, Cfg::TMEM_COLS);
-  }
-}
-
-// O[h, q, :] = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s.
-__global__ void attn_merge_kernel(const float* __restrict__ part_o,
-                                  const float2* __restrict__ part_ml, int nsplit, int H, int L,
-                                  int Dh, int DHP, float* __restrict__ O, int64_t osH,
-                                  int64_t osT, int64_t osD) {
-  const int64_t n = (int64_t)H * L * Dh;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-       i += (int64_t)gridDim.x * blockDim.x) {
-    const int d = static_cast<int>(i % Dh);
-    const int64_t hq = i / Dh;
-    const int h = static_cast<int>(hq / L), q = static_cast<int>(hq % L);
-    float M = -INFINITY;
-    for (int s = 0; s < nsplit; ++s) M = fmaxf(M, part_ml[(size_t)s * H * L + hq].x);
-    float num = 0.f, den = 0.f;
-    for (int s = 0; s < nsplit; ++s) {
-      const float2 ml = part_ml[(size_t)s * H * L + hq];
-      if (ml.x == -INFINITY) continue;
-      const float w = fast_exp2(ml.x - M);
-      num += w * part_o[((size_t)s * H * L + hq) * DHP + d];
-      den += w * ml.y;
-    }
-    O[h * osH + (int64_t)q * osT + d * osD] = num / den;
   }
 }
 
@@ -395,9 +416,8 @@ void launch_attn(const CUtensorMap* maps, const AttnParams& prm, int qtiles, cud
     configured.fetch_or(bit);
   }
   const dim3 grid(qtiles, prm.nsplit, prm.H);
-  attn_tc_kernel<DHP, SPLIT3><<<grid, kThreads, Cfg::SMEM, s>>>(maps[0], maps[1], maps[2],
-                                                                maps[3], maps[4], maps[5], prm);
-  ATTNB_CUDA(cudaGetLastError());
+  ATTNB_CUDA(launch_pdl(attn_tc_kernel<DHP, SPLIT3>, grid, dim3(kThreads), Cfg::SMEM, s, maps[0],
+                        maps[1], maps[2], maps[3], maps[4], maps[5], prm));
 }
 
 template <bool SPLIT3>
@@ -447,12 +467,14 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
   p.off_v = take(v * parts);
   p.off_po = p.nsplit > 1 ? take((size_t)p.nsplit * H * L * p.dhp * 4) : 0;
   p.off_pml = p.nsplit > 1 ? take((size_t)p.nsplit * H * L * 8) : 0;
+  p.off_cnt = p.nsplit > 1 ? take((size_t)H * p.qtiles * sizeof(unsigned)) : 0;
   p.ws_bytes = off;
   return p;
 }
 
 void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View3& V,
-                 const MView3& O, bool causal, void* ws, int* status, cudaStream_t s) {
+                 const MView3& O, bool causal, void* ws, int* status, int num_sms,
+                 cudaStream_t s) {
   char* w = static_cast<char*>(ws);
   const size_t q = (size_t)p.H * p.L * p.dhp, k = (size_t)p.H * p.T * p.dhp,
                v = (size_t)p.H * p.dhp * p.tp;
@@ -463,10 +485,14 @@ void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View
   float* kl = p.split3 ? kh + k : nullptr;
   float* vl = p.split3 ? vh + v : nullptr;
   const float qscale = kLog2e / std::sqrt(static_cast<float>(p.Dh));
-  pack3_launch(Q.data, Q.sH, Q.sT, Q.sD, p.H, p.L, p.Dh, p.dhp, qscale, qh, ql, p.split3, s);
-  pack3_launch(K.data, K.sH, K.sT, K.sD, p.H, p.T, p.Dh, p.dhp, 1.f, kh, kl, p.split3, s);
-  pack3_transpose_launch(V.data, V.sH, V.sT, V.sD, p.H, p.T, p.Dh, p.tp, p.dhp, vh, vl,
-                         p.split3, s);
+  unsigned* counters = p.nsplit > 1 ? reinterpret_cast<unsigned*>(w + p.off_cnt) : nullptr;
+  // Q (scaled by log2(e)/sqrt(Dh)) and K as [H, rows, dhp]; V transposed to
+  // [H, dhp, tp]; all in one launch, which also clears the merge counters.
+  const PackJob jobs[3] = {
+      {Q.data, Q.sH, Q.sT, Q.sD, p.H, p.L, p.Dh, p.L, p.dhp, false, qscale, qh, ql},
+      {K.data, K.sH, K.sT, K.sD, p.H, p.T, p.Dh, p.T, p.dhp, false, 1.f, kh, kl},
+      {V.data, V.sH, V.sT, V.sD, p.H, p.T, p.Dh, p.dhp, p.tp, true, 1.f, vh, vl}};
+  pack_launch(jobs, 3, p.split3, counters, p.H * p.qtiles, num_sms, s);
   CUtensorMap maps[6];
   maps[0] = make_tmap_3d(qh, p.H, p.L, p.dhp, p.dhp, (uint64_t)p.L * p.dhp, BM, BK);
   maps[2] = make_tmap_3d(kh, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BN, BK);
@@ -494,16 +520,11 @@ void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View
   prm.osD = O.sD;
   prm.part_o = p.nsplit > 1 ? reinterpret_cast<float*>(w + p.off_po) : nullptr;
   prm.part_ml = p.nsplit > 1 ? reinterpret_cast<float2*>(w + p.off_pml) : nullptr;
+  prm.counters = counters;
+  prm.qtiles = p.qtiles;
   prm.status = status;
   if (p.split3) dispatch_dhp<true>(p.dhp, maps, prm, p.qtiles, s);
   else dispatch_dhp<false>(p.dhp, maps, prm, p.qtiles, s);
-  if (p.nsplit > 1) {
-    const int64_t n = (int64_t)p.H * p.L * p.Dh;
-    const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 8);
-    attn_merge_kernel<<<blocks, 256, 0, s>>>(prm.part_o, prm.part_ml, p.nsplit, p.H, p.L, p.Dh,
-                                             p.dhp, O.data, O.sH, O.sT, O.sD);
-    ATTNB_CUDA(cudaGetLastError());
-  }
 }
 
 }  // namespace attnb

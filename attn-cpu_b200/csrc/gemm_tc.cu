@@ -175,6 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = tmem_base_slot;
   volatile int* abort_p = &abort_flag;
+  grid_dep_wait();  // the packed operands come from the kernel before this one
 
   if (warp == 0) {
     if (lane == 0) {
@@ -366,9 +367,9 @@ void launch_gemm(const GemmPlan& p, const CUtensorMap& a_hi, const CUtensorMap& 
   }
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = std::min(tiles, num_sms);
-  gemm_tc_kernel<BN, SPLIT3><<<grid, kThreads, Cfg::SMEM, s>>>(
-      a_hi, a_lo, b_hi, b_lo, p.M, p.N, p.Kp, C, ldc, alpha, beta, bias, status);
-  ATTNB_CUDA(cudaGetLastError());
+  ATTNB_CUDA(launch_pdl(gemm_tc_kernel<BN, SPLIT3>, dim3(grid), dim3(kThreads), Cfg::SMEM, s,
+                        a_hi, a_lo, b_hi, b_lo, p.M, p.N, p.Kp, C, ldc, alpha, beta, bias,
+                        status));
 }
 
 }  // namespace
@@ -416,10 +417,13 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
   float* b_hi = reinterpret_cast<float*>(w + p.off_b_hi);
   float* a_lo = p.split3 ? reinterpret_cast<float*>(w + p.off_a_lo) : nullptr;
   float* b_lo = p.split3 ? reinterpret_cast<float*>(w + p.off_b_lo) : nullptr;
-  if (a_kmajor) pack_rows_launch(A, lda, p.M, p.K, p.Kp, a_hi, a_lo, p.split3, s);
-  else pack_transpose_launch(A, lda, p.K, p.M, p.Kp, a_hi, a_lo, p.split3, s);
-  if (b_kmajor) pack_rows_launch(B, ldb, p.N, p.K, p.Kp, b_hi, b_lo, p.split3, s);
-  else pack_transpose_launch(B, ldb, p.K, p.N, p.Kp, b_hi, b_lo, p.split3, s);
+  // A -> [M, Kp] and B -> [N, Kp], K-major, in one launch.
+  PackJob jobs[2];
+  jobs[0] = a_kmajor ? PackJob{A, 0, lda, 1, 1, p.M, p.K, p.M, p.Kp, false, 1.f, a_hi, a_lo}
+                     : PackJob{A, 0, lda, 1, 1, p.K, p.M, p.M, p.Kp, true, 1.f, a_hi, a_lo};
+  jobs[1] = b_kmajor ? PackJob{B, 0, ldb, 1, 1, p.N, p.K, p.N, p.Kp, false, 1.f, b_hi, b_lo}
+                     : PackJob{B, 0, ldb, 1, 1, p.K, p.N, p.N, p.Kp, true, 1.f, b_hi, b_lo};
+  pack_launch(jobs, 2, p.split3, nullptr, 0, num_sms, s);
   const int bn = p.split3 ? 128 : 256;
   const CUtensorMap tA_hi = make_tmap_2d(a_hi, p.M, p.Kp, p.Kp, BM, BK);
   const CUtensorMap tB_hi = make_tmap_2d(b_hi, p.N, p.Kp, p.Kp, bn, BK);

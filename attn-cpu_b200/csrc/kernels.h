@@ -5,6 +5,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace attnb {
 
 // Strided fp32 view [H, T, Dh] (strides in elements).
@@ -43,30 +45,55 @@ void attn_block_simt_launch(const View3& Q, const View3& K, const View3& V, cons
 struct AttnTcPlan {
   int H, L, T, Dh, dhp, tp, qtiles, nsplit, tiles_per_split;
   bool split3;
-  size_t off_q, off_k, off_v, off_po, off_pml, ws_bytes;
+  size_t off_q, off_k, off_v, off_po, off_pml, off_cnt, ws_bytes;
 };
 // Head sizes the tensor-core kernel takes (padded to a multiple of 32, <= 128).
 bool attn_tc_supported(int Dh);
 AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision, int num_sms);
 // `ws` holds plan.ws_bytes bytes (packed operands and split partials).
 void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View3& V,
-                 const MView3& O, bool causal, void* ws, int* status, cudaStream_t s);
+                 const MView3& O, bool causal, void* ws, int* status, int num_sms,
+                 cudaStream_t s);
 
 // ------------------------------------------------ operand packing (K2)
-// src[rows, cols] (pitch ld) -> hi/lo[rows, kp]; cols..kp-1 zero.
-void pack_rows_launch(const float* src, int64_t ld, int rows, int cols, int kp, float* hi,
-                      float* lo, bool split3, cudaStream_t s);
-// src[K, N] (pitch ld) -> hi/lo[N, kp] (transposed); K..kp-1 zero.
-void pack_transpose_launch(const float* src, int64_t ld, int K, int N, int kp, float* hi,
-                           float* lo, bool split3, cudaStream_t s);
+// One packing job: a strided 3-D source src[h][r][c] (r < R, c < C), times
+// `scale`, written to hi (and lo when splitting) either in place as
+// [H][rows_out = R][cols_out] (columns C..cols_out-1 zero) or, with
+// `transpose`, as [H][rows_out][cols_out] holding src[h][r][c] at [h][c][r]
+// (zero outside r < R, c < C).  cols_out % 4 == 0.
+struct PackJob {
+  const float* src;
+  int64_t sH, sR, sC;
+  int H, R, C;
+  int rows_out, cols_out;
+  bool transpose;
+  float scale;
+  float* hi;
+  float* lo;
+};
+constexpr int kMaxPackJobs = 3;
+// Packs up to kMaxPackJobs jobs in one launch and clears `nzero` counters.
+void pack_launch(const PackJob* jobs, int njobs, bool split3, unsigned* zero, int nzero,
+                 int num_sms, cudaStream_t s);
 
-// 3-D strided src[h, r, c] -> hi/lo[h, r, cp] (times `scale`), c >= C zero.
-void pack3_launch(const float* src, int64_t sH, int64_t sR, int64_t sC, int H, int R, int C,
-                  int cp, float scale, float* hi, float* lo, bool split3, cudaStream_t s);
-// 3-D strided src[h, t, d] -> hi/lo[h, d, tp] for d < dp, zero outside [T, D).
-void pack3_transpose_launch(const float* src, int64_t sH, int64_t sT, int64_t sD, int H, int T,
-                            int D, int tp, int dp, float* hi, float* lo, bool split3,
-                            cudaStream_t s);
+// Launches `kernel` with programmatic stream serialisation, so its prologue
+// may overlap the previous kernel on the stream; the kernel must execute
+// griddepcontrol.wait before reading what that kernel wrote.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                       cudaStream_t s, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // --------------------------------------------------- tcgen05 GEMM (K1)
 // C[M,N] = alpha * A.B + beta * C (+ bias[n]).  A is [M,K] (a_kmajor: rows of
