@@ -359,35 +359,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(1, 128);
       if (s_last) {
         __threadfence();
-        if (qrow < p.L) {
-          const size_t hs = (size_t)p.H * p.L, base_row = (size_t)h * p.L + qrow;
-          float M = -INFINITY;
-          for (int sp = 0; sp < p.nsplit; ++sp) M = fmaxf(M, __ldcg(&p.part_ml[sp * hs + base_row]).x);
-          float den = 0.f;
-          for (int sp = 0; sp < p.nsplit; ++sp) {
-            const float2 ml = __ldcg(&p.part_ml[sp * hs + base_row]);
-            if (ml.x != -INFINITY) den += fast_exp2(ml.x - M) * ml.y;
-          }
-          const float inv = 1.f / den;
-          float* orow = p.O + h * p.osH + (int64_t)qrow * p.osT;
-          for (int d = 0; d < p.Dh; d += 4) {
-            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int sp = 0; sp < p.nsplit; ++sp) {
-              const float2 ml = __ldcg(&p.part_ml[sp * hs + base_row]);
-              if (ml.x == -INFINITY) continue;
-              const float w = fast_exp2(ml.x - M);
-              const float4 v = __ldcg(reinterpret_cast<const float4*>(
-                  p.part_o + (sp * hs + base_row) * DHP + d));
-              acc.x = fmaf(w, v.x, acc.x);
-              acc.y = fmaf(w, v.y, acc.y);
-              acc.z = fmaf(w, v.z, acc.z);
-              acc.w = fmaf(w, v.w, acc.w);
-            }
-            const float a4[4] = {acc.x, acc.y, acc.z, acc.w};
+        // Fold the other splits into this CTA's own (m, l, o) with the same
+        // running-max update; each split's row is fetched with all loads in flight.
+        const size_t hs = (size_t)p.H * p.L, base_row = (size_t)h * p.L + min(qrow, p.L - 1);
+        for (int sp = 0; sp < p.nsplit; ++sp) {
+          if (sp == split) continue;
+          const size_t prow = sp * hs + base_row;
+          const float2 ml = __ldcg(&p.part_ml[prow]);
+          const float4* src = reinterpret_cast<const float4*>(p.part_o + prow * DHP);
+          const float m_new = fmaxf(m, ml.x);
+          const float a = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
+          const float b = (ml.x == -INFINITY) ? 0.f : fast_exp2(ml.x - m_new);
+          l = l * a + ml.y * b;
 #pragma unroll
-            for (int k = 0; k < 4; ++k)
-              if (d + k < p.Dh) orow[(d + k) * p.osD] = a4[k] * inv;
+          for (int c = 0; c < DHP / 32; ++c) {
+            float4 v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k) v[k] = __ldcg(src + c * 8 + k);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              float* oc = &o[c * 32 + 4 * k];
+              oc[0] = fmaf(oc[0], a, v[k].x * b);
+              oc[1] = fmaf(oc[1], a, v[k].y * b);
+              oc[2] = fmaf(oc[2], a, v[k].z * b);
+              oc[3] = fmaf(oc[3], a, v[k].w * b);
+            }
           }
+          m = m_new;
+        }
+        if (qrow < p.L) {
+          const float inv = 1.f / l;
+          float* orow = p.O + h * p.osH + (int64_t)qrow * p.osT;
+#pragma unroll
+          for (int d = 0; d < DHP; ++d)
+            if (d < p.Dh) orow[d * p.osD] = o[d] * inv;
         }
         if (r == 0) *cnt = 0u;  // cleared again for the next call
       }
