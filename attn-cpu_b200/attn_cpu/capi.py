@@ -24,7 +24,7 @@ PREC = {None: -1, "default": -1, "3xtf32": 0, "tf32": 1}
 EXPORTED = [
     "attnb_last_error", "attnb_version", "attnb_stream_status",
     "attnb_sgemm", "attnb_gemm_jit", "attnb_sgemm_dev", "attnb_linear_dev",
-    "attnb_attn_step_dense", "attnb_attn_step_dense_dev",
+    "attnb_attn_step_dense", "attnb_attn_step_dense_dev", "attnb_attn_step_dense_noalloc",
     "attnb_attn_block_dense", "attnb_attn_block_dense_dev",
     "attnb_mha_block_dense", "attnb_mha_block_dense_dev",
 ]
@@ -63,6 +63,7 @@ def lib() -> ctypes.CDLL:
         L.attnb_linear_dev.argtypes = [vp, i, vp, i, vp, vp, i, i, i, i, i, vp]
         L.attnb_attn_step_dense.argtypes = [T, T, T, T]
         L.attnb_attn_step_dense_dev.argtypes = [T, T, T, T, vp]
+        L.attnb_attn_step_dense_noalloc.argtypes = [T, T, T, T, vp]
         L.attnb_attn_block_dense.argtypes = [T, T, T, T, i, i]
         L.attnb_attn_block_dense_dev.argtypes = [T, T, T, T, i, i, vp]
         L.attnb_mha_block_dense.argtypes = [vp, i, i, vp, vp, vp, vp, i, i, vp, i]
@@ -117,6 +118,14 @@ def attn_step_dense_dev(Q, K, V, O, stream=None) -> None:
     q, k, v, o = tensor3(Q, True), tensor3(K), tensor3(V), tensor3(O, True)
     check(lib().attnb_attn_step_dense_dev(ctypes.byref(q), ctypes.byref(k), ctypes.byref(v),
                                           ctypes.byref(o), _stream(stream)))
+
+
+def attn_step_dense_noalloc(Q, K, V, O, stream=None) -> None:
+    """Decode step without any device allocation (fixed 2 MiB scratch shared by
+    all calls; see attnb_attn_step_dense_noalloc in include/attnb.h)."""
+    q, k, v, o = tensor3(Q, True), tensor3(K), tensor3(V), tensor3(O, True)
+    check(lib().attnb_attn_step_dense_noalloc(ctypes.byref(q), ctypes.byref(k), ctypes.byref(v),
+                                              ctypes.byref(o), _stream(stream)))
 
 
 def attn_block_dense_dev(Q, K, V, O, causal=False, precision=None, stream=None) -> None:

@@ -307,3 +307,119 @@ void decode_launch(const DecodePlan& p, const View3& Q, const View3& K, const Vi
 }
 
 }  // namespace attnb
+
+// ===================================================================
+// attnb_attn_step_dense_noalloc -- the decode step for callers that may not
+// allocate device memory.
+//
+// Some callers cannot call cudaMalloc at all: code running inside a custom
+// allocator or memory pool that owns the whole device budget, runtimes that
+// forbid allocation on their hot path, and applications that must keep their
+// memory footprint fixed once they start.  For them this entry point computes
+// exactly what attnb_attn_step_dense_dev computes (same plan, same kernels)
+// but keeps the split-KV partials (per head and key range: the running max,
+// the sum and the unnormalised output row) in a fixed, file-scope device array
+// of kNoAllocScratchBytes, which every GPU that loads the library holds until
+// the process exits.  The caller passes device pointers for inputs and output.
+//
+// Limits and rules:
+//   * a call whose decode plan needs more scratch than kNoAllocScratchBytes
+//     (heads x key ranges x head size x 4 bytes + 8 bytes per pair) is
+//     rejected with ATTNB_ERR_INVALID_ARGUMENT before any work is enqueued;
+//   * every call shares the one array, which keeps the previous call's
+//     contents; nothing in it has to start at zero (each partial is written
+//     before it is read), but calls whose work overlaps on the GPU (different
+//     streams, or other host threads) race on it and must be ordered by the
+//     caller;
+//   * the first call on a device looks the array's device address up
+//     (cudaGetSymbolAddress) and caches it, so make that first call before
+//     any stream capture.
+// ===================================================================
+#include <mutex>
+
+#include "runtime.h"
+
+namespace attnb {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(2) << 20;  // 2 MiB
+constexpr int kNoAllocMaxDevices = 64;
+
+static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kNoAllocMaxDevices];
+int g_noalloc_sms[kNoAllocMaxDevices];
+
+// The reference's validate_dense_shapes (include/attn.h:54-83), same messages.
+void noalloc_validate(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
+                      const attnb_mtensor* O) {
+  if (!Q || !K || !V || !O) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null tensor descriptor");
+  if (!Q->data || !K->data || !V->data || !O->data)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+  if (Q->H <= 0 || Q->Dh <= 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "Q has invalid H/Dh");
+  if (K->H != Q->H || V->H != Q->H) fail(ATTNB_ERR_INVALID_ARGUMENT, "K/V H must match Q.H");
+  if (K->Dh != Q->Dh || V->Dh != Q->Dh)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "K/V Dh must match Q.Dh");
+  if (K->T <= 0 || V->T != K->T)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "K/V T must be positive and equal");
+  if (O->H != Q->H || O->Dh != Q->Dh)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "O must be [H, Dh] matching Q");
+  if (Q->strideH == 0 || Q->strideDh == 0 || K->strideH == 0 || K->strideT == 0 ||
+      K->strideDh == 0 || V->strideH == 0 || V->strideT == 0 || V->strideDh == 0 ||
+      O->strideH == 0 || O->strideDh == 0)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "Zero stride encountered");
+}
+
+// Device address of the fixed scratch and the SM count, looked up once per
+// device with that device current.
+void* noalloc_scratch(int dev, int* num_sms) {
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    fail(ATTNB_ERR_RUNTIME, "device index out of range for the fixed decode scratch");
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    ATTNB_CUDA(cudaGetSymbolAddress(&p, g_decode_scratch));
+    int sms = 0;
+    ATTNB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    g_noalloc_sms[dev] = sms;
+    g_noalloc_addr[dev] = p;
+  }
+  *num_sms = g_noalloc_sms[dev];
+  return g_noalloc_addr[dev];
+}
+
+}  // namespace
+}  // namespace attnb
+
+extern "C" ATTNB_API int attnb_attn_step_dense_noalloc(const attnb_tensor* Q,
+                                                       const attnb_tensor* K,
+                                                       const attnb_tensor* V, attnb_mtensor* O,
+                                                       void* stream) {
+  using namespace attnb;
+  try {
+    noalloc_validate(Q, K, V, O);
+    int dev = -1;
+    ATTNB_CUDA(cudaGetDevice(&dev));
+    int num_sms = 0;
+    void* scratch = noalloc_scratch(dev, &num_sms);
+    const View3 q{Q->data, Q->H, 1, Q->Dh, Q->strideH, 0, Q->strideDh};
+    const View3 k{K->data, K->H, K->T, K->Dh, K->strideH, K->strideT, K->strideDh};
+    const View3 v{V->data, V->H, V->T, V->Dh, V->strideH, V->strideT, V->strideDh};
+    const MView3 o{O->data, O->H, 1, O->Dh, O->strideH, 0, O->strideDh};
+    const DecodePlan p = decode_plan(q, k, v, num_sms);
+    const size_t need = decode_workspace_bytes(p, K->H, K->Dh);
+    if (need > kNoAllocScratchBytes)
+      fail(ATTNB_ERR_INVALID_ARGUMENT,
+           "decode step needs " + std::to_string(need) + " bytes of scratch; the fixed scratch of "
+           "attnb_attn_step_dense_noalloc holds " + std::to_string(kNoAllocScratchBytes) +
+           " (use attnb_attn_step_dense_dev)");
+    decode_launch(p, q, k, v, o, scratch, static_cast<cudaStream_t>(stream));
+    ATTNB_CUDA(cudaGetLastError());
+    return ATTNB_OK;
+  } catch (const Error& e) {
+    return set_last_error(e.code, e.msg);
+  } catch (const std::exception& e) {
+    return set_last_error(ATTNB_ERR_RUNTIME, e.what());
+  }
+}

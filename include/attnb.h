@@ -109,6 +109,18 @@ ATTNB_API int attnb_attn_step_dense(const attnb_tensor* Q, const attnb_tensor* K
                           const attnb_tensor* V, attnb_mtensor* O);
 ATTNB_API int attnb_attn_step_dense_dev(const attnb_tensor* Q, const attnb_tensor* K,
                               const attnb_tensor* V, attnb_mtensor* O, void* stream);
+/* The decode step for callers that may not allocate device memory (a custom
+ * allocator or pool that owns the device, a hot path where allocation is
+ * forbidden, a fixed memory footprint).  No counterpart in the reference.
+ * Same arguments, plan and kernels as attnb_attn_step_dense_dev, but the
+ * split-KV scratch is a fixed 2 MiB file-scope device array, held by every
+ * GPU that loads the library until exit; calls needing more are rejected with
+ * ATTNB_ERR_INVALID_ARGUMENT.  All calls share that array: calls that overlap
+ * on the GPU race.  The first call on a device looks up the array's address;
+ * make it before any stream capture.  Allocates nothing. */
+ATTNB_API int attnb_attn_step_dense_noalloc(const attnb_tensor* Q, const attnb_tensor* K,
+                                            const attnb_tensor* V, attnb_mtensor* O,
+                                            void* stream);
 
 /* Prefill with given Q/K/V: Q [H,L,Dh], K/V [H,T,Dh] -> O [H,L,Dh]; causal
  * needs L == T.  Replaces attn::attn_block_dense (include/attn.h:40-44;
