@@ -48,17 +48,41 @@ struct AttnCfg {
   static constexpr int QBOX = BM * BK * 4;   // 16 KB
   static constexpr int KBOX = BN * BK * 4;   // 16 KB
   static constexpr int VBOX = DHP * BK * 4;  // 32 keys of V^T
-  static constexpr int STAGE = NPART * (QBOX + KBOX);
-  static constexpr int STAGES = SPLIT3 ? 3 : 6;
-  static constexpr int SMEM = STAGES * STAGE + 1024;
+  // Two rings: Q+K slices for the S product, V^T slices for the PV product,
+  // so all of a tile's V slices can be in flight while S and the softmax run.
+  static constexpr int S_STAGE = NPART * (QBOX + KBOX);
+  static constexpr int S_STAGES = SPLIT3 ? 2 : 4;
+  static constexpr int V_STAGE = NPART * VBOX;
+  static constexpr int V_STAGES_FIT = (225 * 1024 - S_STAGES * S_STAGE) / V_STAGE;
+  static constexpr int V_STAGES = V_STAGES_FIT < 4 ? V_STAGES_FIT : 4;
+  static constexpr int SMEM = S_STAGES * S_STAGE + V_STAGES * V_STAGE + 1024;
   static constexpr int S_BIG = 0;
   static constexpr int S_SMALL = BN;
   static constexpr int PV_BIG = NPART * BN;
   static constexpr int PV_SMALL = PV_BIG + DHP;
   static constexpr int TMEM_COLS = SPLIT3 ? 512 : 256;
   static_assert(DHP % 32 == 0 && DHP <= 128, "head size padded to 32..128");
-  static_assert(NPART * VBOX <= STAGE, "V slice fits a stage");
+  static_assert(V_STAGES >= 2, "V ring needs two stages");
+  static_assert(BM * (DHP + 1) * 4 <= S_STAGES * S_STAGE, "output staging fits the S ring");
   static_assert(PV_BIG + NPART * DHP <= TMEM_COLS, "TMEM budget");
+};
+
+// Position in a ring of N stages (stage index and the phase parity to wait on).
+template <int N>
+struct Ring {
+  int stage = 0;
+  uint32_t phase = 0;
+  uint32_t issued_mask = 0, issued_parity = 0;
+  __device__ __forceinline__ void note_issue() {
+    issued_mask |= 1u << stage;
+    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+  }
+  __device__ __forceinline__ void advance() {
+    if (++stage == N) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
 };
 
 __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* status) {
@@ -75,8 +99,8 @@ struct AttnParams {
   int L, T, H, Dh, causal, nsplit, tiles_per_split, qtiles;
   float* O;
   int64_t osH, osT, osD;
-  float* part_o;       // [nsplit, H, L, DHP] (nsplit > 1)
-  float2* part_ml;     // [nsplit, H, L]
+  float* part_o;       // [nsplit][H][qtiles][DHP][128] (nsplit > 1)
+  float2* part_ml;     // [nsplit][H][qtiles][128]
   unsigned* counters;  // [H, qtiles] finished splits, cleared by the pack kernel
   int* status;
 };
@@ -88,12 +112,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
                    const AttnParams p) {
   using Cfg = AttnCfg<DHP, SPLIT3>;
-  constexpr int STAGES = Cfg::STAGES;
+  constexpr int SST = Cfg::S_STAGES, VST = Cfg::V_STAGES;
   constexpr uint32_t IDESC_S = idesc_tf32(BM, BN);
   constexpr uint32_t IDESC_PV = idesc_tf32(BM, DHP);
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t sfull[SST], sempty[SST], vfull[VST], vempty[VST];
   __shared__ __align__(8) uint64_t s_bar, p_bar, pv_bar, final_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
@@ -101,7 +125,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, split = blockIdx.y, h = blockIdx.z;
   const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
-  auto stage_addr = [&](int s) { return base + s * Cfg::STAGE; };
+  auto s_addr = [&](int st) { return base + st * Cfg::S_STAGE; };
+  auto v_addr = [&](int st) { return base + SST * Cfg::S_STAGE + st * Cfg::V_STAGE; };
 
   // Key tiles of this CTA.
   int n_kv = (p.T + BN - 1) / BN;
@@ -114,9 +139,13 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(smem_addr(&full_bar[s]), 1);
-      mbar_init(smem_addr(&empty_bar[s]), 1);
+    for (int i = 0; i < SST; ++i) {
+      mbar_init(smem_addr(&sfull[i]), 1);
+      mbar_init(smem_addr(&sempty[i]), 1);
+    }
+    for (int i = 0; i < VST; ++i) {
+      mbar_init(smem_addr(&vfull[i]), 1);
+      mbar_init(smem_addr(&vempty[i]), 1);
     }
     mbar_init(smem_addr(&s_bar), 1);
     mbar_init(smem_addr(&p_bar), 4);
@@ -141,55 +170,53 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmQh);
       tma_prefetch_desc(&tmKh);
       tma_prefetch_desc(&tmVh);
-      int stage = 0;
-      uint32_t phase = 0, issued_mask = 0, issued_parity = 0;
+      Ring<SST> rs;
+      Ring<VST> rv;
       bool ok = true;
-      auto next = [&]() {
-        issued_mask |= 1u << stage;
-        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-        if (++stage == STAGES) {
-          stage = 0;
-          phase ^= 1u;
-        }
-      };
       for (int j = j0; ok && j < j1; ++j) {
         for (int kb = 0; kb < Cfg::NKB; ++kb) {
-          if (!mbar_wait(smem_addr(&empty_bar[stage]), phase ^ 1u, abort_p, p.status)) {
+          if (!mbar_wait(smem_addr(&sempty[rs.stage]), rs.phase ^ 1u, abort_p, p.status)) {
             ok = false;
             break;
           }
-          const uint32_t fb = smem_addr(&full_bar[stage]), sa = stage_addr(stage);
-          mbar_arrive_expect_tx(fb, Cfg::STAGE);
+          const uint32_t fb = smem_addr(&sfull[rs.stage]), sa = s_addr(rs.stage);
+          mbar_arrive_expect_tx(fb, Cfg::S_STAGE);
           tma_load_3d(sa, &tmQh, fb, kb * BK, qt * BM, h);
           tma_load_3d(sa + Cfg::QBOX, &tmKh, fb, kb * BK, j * BN, h);
           if (SPLIT3) {
             tma_load_3d(sa + Cfg::QBOX + Cfg::KBOX, &tmQl, fb, kb * BK, qt * BM, h);
             tma_load_3d(sa + 2 * Cfg::QBOX + Cfg::KBOX, &tmKl, fb, kb * BK, j * BN, h);
           }
-          next();
+          rs.note_issue();
+          rs.advance();
         }
         const int nvb = min(BN / BK, (p.T - j * BN + BK - 1) / BK);
         for (int vb = 0; ok && vb < nvb; ++vb) {
-          if (!mbar_wait(smem_addr(&empty_bar[stage]), phase ^ 1u, abort_p, p.status)) {
+          if (!mbar_wait(smem_addr(&vempty[rv.stage]), rv.phase ^ 1u, abort_p, p.status)) {
             ok = false;
             break;
           }
-          const uint32_t fb = smem_addr(&full_bar[stage]), sa = stage_addr(stage);
-          mbar_arrive_expect_tx(fb, Cfg::NPART * Cfg::VBOX);
-          tma_load_3d(sa, &tmVh, fb, j * BN + vb * BK, 0, h);
-          if (SPLIT3) tma_load_3d(sa + Cfg::VBOX, &tmVl, fb, j * BN + vb * BK, 0, h);
-          next();
+          const uint32_t fb = smem_addr(&vfull[rv.stage]), va = v_addr(rv.stage);
+          mbar_arrive_expect_tx(fb, Cfg::V_STAGE);
+          tma_load_3d(va, &tmVh, fb, j * BN + vb * BK, 0, h);
+          if (SPLIT3) tma_load_3d(va + Cfg::VBOX, &tmVl, fb, j * BN + vb * BK, 0, h);
+          rv.note_issue();
+          rv.advance();
         }
       }
-      for (int s = 0; s < STAGES; ++s)
-        if (issued_mask & (1u << s))
-          drain_wait(smem_addr(&full_bar[s]), (issued_parity >> s) & 1u, p.status);
+      // Copies still in flight (only possible after an abort) land before exit.
+      for (int i = 0; i < SST; ++i)
+        if (rs.issued_mask & (1u << i))
+          drain_wait(smem_addr(&sfull[i]), (rs.issued_parity >> i) & 1u, p.status);
+      for (int i = 0; i < VST; ++i)
+        if (rv.issued_mask & (1u << i))
+          drain_wait(smem_addr(&vfull[i]), (rv.issued_parity >> i) & 1u, p.status);
     }
   } else if (warp == 1) {
     if (lane == 0) {
       // ---------------------------------------------------------- MMA issuer
-      int stage = 0;
-      uint32_t phase = 0;
+      Ring<SST> rs;
+      Ring<VST> rv;
       bool ok = true;
       int it = 0;
       for (int j = j0; ok && j < j1; ++j, ++it) {
@@ -197,12 +224,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (it > 0 && !mbar_wait(smem_addr(&pv_bar), (it - 1) & 1, abort_p, p.status)) break;
         tc_fence_after();
         for (int kb = 0; kb < Cfg::NKB; ++kb) {
-          if (!mbar_wait(smem_addr(&full_bar[stage]), phase, abort_p, p.status)) {
+          if (!mbar_wait(smem_addr(&sfull[rs.stage]), rs.phase, abort_p, p.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = stage_addr(stage);
+          const uint32_t sa = s_addr(rs.stage);
 #pragma unroll
           for (int kk = 0; kk < BK / 8; ++kk) {
             const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
@@ -216,11 +243,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               mma_tf32(tmem + Cfg::S_SMALL, ql, kh, IDESC_S, 1u);
             }
           }
-          mma_commit(smem_addr(&empty_bar[stage]));
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          mma_commit(smem_addr(&sempty[rs.stage]));
+          rs.advance();
         }
         if (!ok) break;
         mma_commit(smem_addr(&s_bar));
@@ -228,12 +252,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         const int nvb = min(BN / BK, (p.T - j * BN + BK - 1) / BK);
         for (int vb = 0; vb < nvb; ++vb) {
-          if (!mbar_wait(smem_addr(&full_bar[stage]), phase, abort_p, p.status)) {
+          if (!mbar_wait(smem_addr(&vfull[rv.stage]), rv.phase, abort_p, p.status)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = stage_addr(stage);
+          const uint32_t sa = v_addr(rv.stage);
 #pragma unroll
           for (int kk = 0; kk < BK / 8; ++kk) {
             const uint32_t acc = (vb | kk) != 0 ? 1u : 0u;
@@ -246,11 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1)
               mma_tf32_ts(tmem + Cfg::PV_SMALL, tmem + Cfg::S_SMALL + key, vh, IDESC_PV, 1u);
             }
           }
-          mma_commit(smem_addr(&empty_bar[stage]));
-          if (++stage == STAGES) {
-            stage = 0;
-            phase ^= 1u;
-          }
+          mma_commit(smem_addr(&vempty[rv.stage]));
+          rv.advance();
         }
         if (!ok) break;
         mma_commit(smem_addr(&pv_bar));
@@ -333,68 +354,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_fence_before();
     }
-    if (p.nsplit == 1) {
-      if (ok && qrow < p.L) {
-        const float inv = 1.f / l;
-        float* orow = p.O + h * p.osH + (int64_t)qrow * p.osT;
+    // Rows are owned one per thread, so global traffic goes through layouts
+    // that keep a warp's accesses contiguous: split partials are stored
+    // column-major per tile ([d][row]), and the final tile is staged in the
+    // (now idle) shared-memory ring and written row by row.
+    const size_t tile_id = (size_t)h * p.qtiles + qt;
+    bool write_out = (p.nsplit == 1) && ok;
+    if (p.nsplit > 1 && ok) {
+      const size_t pbase = ((size_t)split * p.H * p.qtiles + tile_id) * BM;
+      float* po = p.part_o + pbase * DHP;
 #pragma unroll
-        for (int d = 0; d < DHP; ++d)
-          if (d < p.Dh) orow[d * p.osD] = o[d] * inv;
-      }
-    } else if (ok) {
-      // Publish this split's (m, l, O); the CTA that finishes a (head, query
-      // tile) last merges all splits:  O = sum_s 2^(m_s - M) o_s / sum_s 2^(m_s - M) l_s.
-      if (qrow < p.L) {
-        const size_t row = ((size_t)split * p.H + h) * p.L + qrow;
-        float4* dst = reinterpret_cast<float4*>(p.part_o + row * DHP);
-#pragma unroll
-        for (int d = 0; d < DHP; d += 4) dst[d / 4] = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
-        p.part_ml[row] = make_float2(m, l);
-      }
+      for (int d = 0; d < DHP; ++d) po[(size_t)d * BM + r] = o[d];
+      p.part_ml[pbase + r] = make_float2(m, l);
       __threadfence();
       named_bar_sync(1, 128);
       __shared__ int s_last;
-      unsigned* cnt = p.counters + (size_t)h * p.qtiles + qt;
+      unsigned* cnt = p.counters + tile_id;
       if (r == 0) s_last = (atomicAdd(cnt, 1u) == (unsigned)(p.nsplit - 1));
       named_bar_sync(1, 128);
       if (s_last) {
         __threadfence();
         // Fold the other splits into this CTA's own (m, l, o) with the same
-        // running-max update; each split's row is fetched with all loads in flight.
-        const size_t hs = (size_t)p.H * p.L, base_row = (size_t)h * p.L + min(qrow, p.L - 1);
+        // running-max update.
         for (int sp = 0; sp < p.nsplit; ++sp) {
           if (sp == split) continue;
-          const size_t prow = sp * hs + base_row;
-          const float2 ml = __ldcg(&p.part_ml[prow]);
-          const float4* src = reinterpret_cast<const float4*>(p.part_o + prow * DHP);
+          const size_t qb = ((size_t)sp * p.H * p.qtiles + tile_id) * BM;
+          const float2 ml = __ldcg(&p.part_ml[qb + r]);
+          const float* src = p.part_o + qb * DHP + r;
           const float m_new = fmaxf(m, ml.x);
           const float a = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
           const float b = (ml.x == -INFINITY) ? 0.f : fast_exp2(ml.x - m_new);
           l = l * a + ml.y * b;
+          constexpr int CH = DHP < 64 ? DHP : 64;  // loads kept in flight together
 #pragma unroll
-          for (int c = 0; c < DHP / 32; ++c) {
-            float4 v[8];
+          for (int c = 0; c < DHP / CH; ++c) {
+            float v[CH];
 #pragma unroll
-            for (int k = 0; k < 8; ++k) v[k] = __ldcg(src + c * 8 + k);
+            for (int k = 0; k < CH; ++k) v[k] = __ldcg(src + (size_t)(c * CH + k) * BM);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              float* oc = &o[c * 32 + 4 * k];
-              oc[0] = fmaf(oc[0], a, v[k].x * b);
-              oc[1] = fmaf(oc[1], a, v[k].y * b);
-              oc[2] = fmaf(oc[2], a, v[k].z * b);
-              oc[3] = fmaf(oc[3], a, v[k].w * b);
-            }
+            for (int k = 0; k < CH; ++k) o[c * CH + k] = fmaf(o[c * CH + k], a, v[k] * b);
           }
           m = m_new;
         }
-        if (qrow < p.L) {
-          const float inv = 1.f / l;
-          float* orow = p.O + h * p.osH + (int64_t)qrow * p.osT;
-#pragma unroll
-          for (int d = 0; d < DHP; ++d)
-            if (d < p.Dh) orow[d * p.osD] = o[d] * inv;
-        }
         if (r == 0) *cnt = 0u;  // cleared again for the next call
+        write_out = true;
+      }
+    }
+    if (write_out) {
+      // Stage the normalised tile (row stride DHP + 1: conflict-free column
+      // writes), then write each row with the warp's lanes along the row.
+      float* stile = reinterpret_cast<float*>(smem_raw + (base - smem_addr(smem_raw)));
+      const float inv = 1.f / l;
+#pragma unroll
+      for (int d = 0; d < DHP; ++d) stile[r * (DHP + 1) + d] = o[d] * inv;
+      named_bar_sync(1, 128);
+      const int rows = min(BM, p.L - qt * BM);
+      float* obase = p.O + h * p.osH + (int64_t)qt * BM * p.osT;
+#pragma unroll 4
+      for (int rr = quarter; rr < rows; rr += 4) {
+        float* orow = obase + (int64_t)rr * p.osT;
+#pragma unroll
+        for (int dd = 0; dd < DHP; dd += 32)
+          if (dd + lane < p.Dh) orow[(dd + lane) * p.osD] = stile[rr * (DHP + 1) + dd + lane];
       }
     }
   }
@@ -470,8 +491,9 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
   p.off_q = take(q * parts);
   p.off_k = take(k * parts);
   p.off_v = take(v * parts);
-  p.off_po = p.nsplit > 1 ? take((size_t)p.nsplit * H * L * p.dhp * 4) : 0;
-  p.off_pml = p.nsplit > 1 ? take((size_t)p.nsplit * H * L * 8) : 0;
+  const size_t tile_rows = (size_t)p.nsplit * H * p.qtiles * BM;
+  p.off_po = p.nsplit > 1 ? take(tile_rows * p.dhp * 4) : 0;
+  p.off_pml = p.nsplit > 1 ? take(tile_rows * 8) : 0;
   p.off_cnt = p.nsplit > 1 ? take((size_t)H * p.qtiles * sizeof(unsigned)) : 0;
   p.ws_bytes = off;
   return p;
