@@ -1,0 +1,210 @@
+"""parallel -- the hot paths partitioned over the GPUs of one node.
+
+One process per GPU, torch.distributed (NCCL over NVLink / NVSwitch) for the
+collectives.  The reference has no multi-device code at all (its only
+parallelism is OpenMP inside one process, src/gemm.cpp:350); the partitions
+here follow the work's natural independence:
+
+* attention (prefill and decode): whole heads per rank -- no exchange inside
+  the attention itself;
+* the MHA block (attn::mha_block_dense, src/attn_dispatch.cpp:17-133): rank r
+  owns heads [h0, h1): it projects only its heads' Q/K/V rows of W_in
+  (column-parallel QKV), runs their attention, then an all-gather of the
+  per-head context rebuilds ctx [T, D] on every rank, each rank computes the
+  output projection for its own column block of y, and a second all-gather
+  assembles y.  Every output element is summed in the same order as on one
+  GPU;
+* SGEMM (gemm::sgemm_blocked, src/gemm.cpp:319-415): rank r computes a block
+  of C -- a block of rows (A row block x all of B; the all-gather is then
+  contiguous) or, as `shard="cols"`, a block of columns (all of A x a column
+  block of B, read in place through its leading dimension) followed by an
+  all-gather and a permute.
+
+Local compute goes through an `ops` object whose default calls the B200
+kernels in libattnb (attn_cpu.capi); tests substitute a CPU implementation to
+check the partition and collective logic on gloo ranks.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+import torch.distributed as dist
+
+
+def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
+    """Contiguous balanced split of range(n): the first n % world ranks get one more."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError("bad rank/world")
+    base, extra = divmod(n, world)
+    start = rank * base + min(rank, extra)
+    return start, start + base + (1 if rank < extra else 0)
+
+
+class DeviceOps:
+    """Local compute on the current CUDA device through the C ABI."""
+
+    def __init__(self, precision=None):
+        from . import capi
+
+        self.capi = capi
+        self.precision = precision
+
+    def linear(self, x, W, b, y):
+        self.capi.linear_dev(x, W, b, y, precision=self.precision)
+
+    def attention(self, q, k, v, o, causal):
+        self.capi.attn_block_dense_dev(q, k, v, o, causal=causal, precision=self.precision)
+
+    def sgemm(self, A, B, C):
+        self.capi.sgemm_dev(A, B, C, precision=self.precision)
+
+
+def _world(group):
+    if not dist.is_available() or not dist.is_initialized():
+        return 0, 1
+    return dist.get_rank(group), dist.get_world_size(group)
+
+
+def _all_gather_rows(local: torch.Tensor, counts: list[int], group) -> torch.Tensor:
+    """Concatenate every rank's `local` [n_r, ...] along dim 0 (ragged n_r)."""
+    rank, world = _world(group)
+    if world == 1:
+        return local
+    if len(set(counts)) == 1:
+        out = torch.empty((sum(counts),) + tuple(local.shape[1:]), dtype=local.dtype,
+                          device=local.device)
+        dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+        return out
+    # Ragged blocks: pad every rank's block to the largest, gather, then trim.
+    cmax = max(counts)
+    tail = tuple(local.shape[1:])
+    padded = torch.zeros((cmax,) + tail, dtype=local.dtype, device=local.device)
+    padded[:local.shape[0]] = local
+    out = torch.empty((world * cmax,) + tail, dtype=local.dtype, device=local.device)
+    dist.all_gather_into_tensor(out, padded, group=group)
+    return torch.cat([out[r * cmax:r * cmax + c] for r, c in enumerate(counts)], 0)
+
+
+@dataclass
+class _HeadShard:
+    h0: int
+    h1: int
+    W_in: torch.Tensor   # [3 * (h1-h0) * Dh, D]: this rank's Q, K, V rows
+    b_in: torch.Tensor
+    W_out: torch.Tensor  # [c1-c0, D]: this rank's rows of W_out (columns of y)
+    b_out: torch.Tensor
+    c0: int
+    c1: int
+
+
+class ShardedMHA:
+    """mha_block_dense with heads partitioned across the ranks of `group`.
+
+    Weights are sliced once at construction (W_in rows of the local heads,
+    W_out rows of the local output columns); `forward(x)` takes x [T, D] or
+    [B, T, D] (identical on every rank) and returns the full y on every rank.
+    """
+
+    def __init__(self, W_in, b_in, W_out, b_out, num_heads: int, causal: bool = False,
+                 group=None, ops=None):
+        D = W_in.shape[1]
+        if W_in.shape != (3 * D, D) or W_out.shape != (D, D):
+            raise ValueError("W_in must be [3D, D] and W_out [D, D]")
+        if num_heads <= 0 or D % num_heads:
+            raise ValueError("num_heads must divide D")
+        self.D, self.H, self.Dh = D, num_heads, D // num_heads
+        self.causal = causal
+        self.group = group
+        self.ops = ops if ops is not None else DeviceOps()
+        rank, world = _world(group)
+        self.rank, self.world = rank, world
+        h0, h1 = shard_range(num_heads, rank, world)
+        Dh = self.Dh
+        rows = [W_in[p * D + h0 * Dh:p * D + h1 * Dh] for p in range(3)]
+        bias = [b_in[p * D + h0 * Dh:p * D + h1 * Dh] for p in range(3)]
+        c0, c1 = shard_range(D, rank, world)
+        self.shard = _HeadShard(h0, h1, torch.cat(rows, 0).contiguous(),
+                                torch.cat(bias, 0).contiguous(),
+                                W_out[c0:c1].contiguous(), b_out[c0:c1].contiguous(), c0, c1)
+        self.head_counts = [shard_range(num_heads, r, world)[1] - shard_range(num_heads, r, world)[0]
+                            for r in range(world)]
+        self.col_counts = [shard_range(D, r, world)[1] - shard_range(D, r, world)[0]
+                           for r in range(world)]
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        squeeze = x.dim() == 2
+        if squeeze:
+            x = x.unsqueeze(0)
+        B, T, D = x.shape
+        s, Dh = self.shard, self.Dh
+        hl = s.h1 - s.h0
+        rows = B * T
+        x2 = x.reshape(rows, D).contiguous()
+        # 1) local heads' [q | k | v] = x W_in_local^T + b_in_local
+        qkv = torch.empty(rows, 3 * hl * Dh, dtype=x.dtype, device=x.device)
+        if hl:
+            self.ops.linear(x2, s.W_in, s.b_in, qkv)
+        # 2) attention of the local heads, per sequence
+        ctx_local = torch.empty(B, T, hl * Dh, dtype=x.dtype, device=x.device)
+        qkv3 = qkv.view(B, T, 3 * hl * Dh)
+        for b in range(B):
+            if not hl:
+                break
+            def heads(p):
+                return qkv3[b, :, p * hl * Dh:(p + 1) * hl * Dh].reshape(T, hl, Dh).permute(1, 0, 2)
+            o = ctx_local[b].view(T, hl, Dh).permute(1, 0, 2)
+            self.ops.attention(heads(0), heads(1), heads(2), o, self.causal)
+        # 3) all-gather the context: [world][B, T, hl_r * Dh] -> ctx [B, T, D]
+        parts = _all_gather_rows(ctx_local.permute(2, 0, 1).reshape(hl * Dh, rows),
+                                 [c * Dh for c in self.head_counts], self.group)
+        ctx = parts.reshape(D, rows).t().contiguous()
+        # 4) local output columns, then all-gather y's column blocks
+        yl = torch.empty(rows, s.c1 - s.c0, dtype=x.dtype, device=x.device)
+        if s.c1 > s.c0:
+            self.ops.linear(ctx, s.W_out, s.b_out, yl)
+        yc = _all_gather_rows(yl.t().contiguous(), self.col_counts, self.group)  # [D, rows]
+        y = yc.t().reshape(B, T, D)
+        return y[0] if squeeze else y.contiguous()
+
+
+def gemm_sharded(A: torch.Tensor, B: torch.Tensor, group=None, ops=None,
+                 shard: str = "rows") -> torch.Tensor:
+    """C = A @ B with C partitioned across the ranks of `group`; returns the full
+    C on every rank.  shard="rows": rank r computes rows [m0, m1) of C;
+    shard="cols": rank r computes columns [n0, n1) (B's column block is read in
+    place through its leading dimension), then an all-gather and a permute."""
+    ops = ops if ops is not None else DeviceOps()
+    rank, world = _world(group)
+    M, K = A.shape
+    N = B.shape[1]
+    if shard == "rows":
+        m0, m1 = shard_range(M, rank, world)
+        Cl = torch.empty(m1 - m0, N, dtype=A.dtype, device=A.device)
+        if m1 > m0:
+            ops.sgemm(A[m0:m1], B, Cl)
+        counts = [shard_range(M, r, world)[1] - shard_range(M, r, world)[0] for r in range(world)]
+        return _all_gather_rows(Cl, counts, group)
+    if shard == "cols":
+        n0, n1 = shard_range(N, rank, world)
+        Cl = torch.empty(M, n1 - n0, dtype=A.dtype, device=A.device)
+        if n1 > n0:
+            ops.sgemm(A, B[:, n0:n1], Cl)
+        counts = [shard_range(N, r, world)[1] - shard_range(N, r, world)[0] for r in range(world)]
+        Ct = _all_gather_rows(Cl.t().contiguous(), counts, group)  # [N, M]
+        return Ct.t().contiguous()
+    raise ValueError("shard must be 'rows' or 'cols'")
+
+
+def attn_block_sharded(Q, K, V, causal=False, group=None, ops=None) -> torch.Tensor:
+    """attn_block_dense with heads partitioned across ranks; Q/K/V [H, L|T, Dh]
+    identical on every rank, returns the full O [H, L, Dh] on every rank."""
+    ops = ops if ops is not None else DeviceOps()
+    rank, world = _world(group)
+    H, L, Dh = Q.shape
+    h0, h1 = shard_range(H, rank, world)
+    Ol = torch.empty(h1 - h0, L, Dh, dtype=Q.dtype, device=Q.device)
+    if h1 > h0:
+        ops.attention(Q[h0:h1], K[h0:h1], V[h0:h1], Ol, causal)
+    counts = [shard_range(H, r, world)[1] - shard_range(H, r, world)[0] for r in range(world)]
+    return _all_gather_rows(Ol, counts, group)

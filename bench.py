@@ -227,6 +227,36 @@ def time_device(run, steps: int, warmup: int, world: int, flush: bool):
 
 
 # --------------------------------------------------------- workloads (ours)
+def setup_sharded(w: str, precision):
+    """One problem partitioned over all ranks (attn_cpu.parallel) with its
+    NCCL all-gathers: heads for prefill / the attention block, row blocks of
+    C for SGEMM.  Inputs are identical on every rank (same seed)."""
+    import torch
+
+    from attn_cpu import parallel
+
+    c = WORKLOADS[w]
+    ops = parallel.DeviceOps(precision)
+    g = torch.Generator(device="cuda").manual_seed(1000)
+    if w == "prefill":
+        Q, K, V = (torch.randn(c["H"], c["L"], c["Dh"], device="cuda", generator=g)
+                   for _ in range(3))
+        return lambda: parallel.attn_block_sharded(Q, K, V, False, ops=ops)
+    if w.startswith("sgemm"):
+        A = torch.rand(c["M"], c["K"], device="cuda", generator=g) * 2 - 1
+        B = torch.rand(c["K"], c["N"], device="cuda", generator=g) * 2 - 1
+        return lambda: parallel.gemm_sharded(A, B, ops=ops)
+    if w == "block":
+        D, H = c["D"], c["H"]
+        x = torch.randn(c["B"], c["T"], D, device="cuda", generator=g)
+        Wi = torch.randn(3 * D, D, device="cuda", generator=g) * 0.02
+        Wo = torch.randn(D, D, device="cuda", generator=g) * 0.02
+        mha = parallel.ShardedMHA(Wi, torch.zeros(3 * D, device="cuda"), Wo,
+                                  torch.zeros(D, device="cuda"), H, ops=ops)
+        return lambda: mha.forward(x)
+    raise KeyError(f"{w} has no sharded form")
+
+
 def setup_workload(w: str, rank: int, precision):
     """Device inputs (seeded per rank) and (run, e2e_run, h2d, d2h, launches)."""
     import numpy as np
@@ -308,6 +338,22 @@ def roofline_of(w: str, ms: float, peaks: dict, precision) -> dict:
     if (precision or "3xtf32") == "3xtf32":
         r["frac_of_3xtf32_cap"] = round(3 * achieved / peak, 4)
     return r
+
+
+def measure_sharded(w: str, world: int, steps: int, warmup: int, precision, peaks):
+    """Strong scaling: one problem over all ranks, collectives inside the step."""
+    run = setup_sharded(w, precision)
+    times = time_device(run, steps, warmup, world, flush=w in ("prefill", "sgemm"))
+    from attn_cpu import capi
+
+    capi.stream_status()
+    ms = max_over_ranks(sum(times), world) / steps
+    work = flops_of(w)
+    return {"metric": WORKLOADS[w]["metric"] + " (one problem sharded over all GPUs)",
+            "value": round(work / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+            "ms_per_step": round(ms, 5), "scaling": "strong", "config": WORKLOADS[w]["desc"],
+            "parallelism": ("heads" if w in ("prefill", "block") else "C row blocks") +
+                           f" x{world} + NCCL all-gather"}
 
 
 def measure(w: str, rank: int, world: int, steps: int, warmup: int, precision, peaks,
@@ -452,6 +498,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU time budget of the reference measurement")
     ap.add_argument("--no-also", action="store_true", help="skip the secondary configs")
+    ap.add_argument("--sharded", default="",
+                    help="with N>1: also time these workloads (comma list of prefill, sgemm, "
+                         "sgemm-large, block) as one problem partitioned over all GPUs")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -476,6 +525,10 @@ def main():
                         with_e2e=w in ("decode", "sgemm"))
             r["config"] = WORKLOADS[w]["desc"]
             also.append(r)
+    if world > 1 and args.sharded:
+        for w in args.sharded.split(","):
+            also.append(measure_sharded(w.strip(), world, max(3, min(args.steps, 10)), 3, prec,
+                                        peaks))
     cpu = None
     if rank == 0 and world == 1:
         v, unit, cores, kind, sample = cpu_sample(args.workload, args.cpu_seconds)
