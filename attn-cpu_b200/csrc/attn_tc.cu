@@ -385,7 +385,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float a = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
           const float b = (ml.x == -INFINITY) ? 0.f : fast_exp2(ml.x - m_new);
           l = l * a + ml.y * b;
-          constexpr int CH = DHP < 64 ? DHP : 64;  // loads kept in flight together
+          constexpr int CH = (DHP % 64 == 0) ? 64 : 32;  // loads kept in flight together
+          static_assert(DHP % CH == 0, "merge chunks cover the head");
 #pragma unroll
           for (int c = 0; c < DHP / CH; ++c) {
             float v[CH];
