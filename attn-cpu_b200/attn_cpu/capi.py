@@ -23,6 +23,7 @@ PREC = {None: -1, "default": -1, "3xtf32": 0, "tf32": 1}
 # Every symbol include/attnb.h declares.
 EXPORTED = [
     "attnb_last_error", "attnb_version", "attnb_stream_status",
+    "attnb_profile_enable", "attnb_profile_read",
     "attnb_sgemm", "attnb_gemm_jit", "attnb_sgemm_dev", "attnb_linear_dev",
     "attnb_attn_step_dense", "attnb_attn_step_dense_dev", "attnb_attn_step_dense_noalloc",
     "attnb_attn_block_dense", "attnb_attn_block_dense_dev",
@@ -57,6 +58,9 @@ def lib() -> ctypes.CDLL:
         L.attnb_last_error.restype = ctypes.c_char_p
         L.attnb_version.restype = ctypes.c_char_p
         L.attnb_stream_status.argtypes = [vp]
+        L.attnb_profile_enable.argtypes = [i]
+        L.attnb_profile_read.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
+                                         ctypes.POINTER(ctypes.c_int)]
         L.attnb_sgemm.argtypes = [vp, i, i, vp, i, vp, f, f, i]
         L.attnb_gemm_jit.argtypes = [vp, i, i, vp, i, vp, f, f, i]
         L.attnb_sgemm_dev.argtypes = [vp, i, vp, i, vp, i, i, i, i, f, f, i, vp]
@@ -146,6 +150,17 @@ def mha_block_dense_dev(x, W_in, b_in, W_out, b_out, num_heads, y, causal=False,
                                           b_in.data_ptr(), W_out.data_ptr(), b_out.data_ptr(),
                                           num_heads, int(causal), y.data_ptr(), PREC[precision],
                                           _stream(stream)))
+
+
+def profile_enable(on: bool = True) -> None:
+    check(lib().attnb_profile_enable(int(on)))
+
+
+def profile_read(kernel: str) -> tuple[float, int]:
+    """(summed milliseconds, launches) of `kernel` since the last read."""
+    ms, n = ctypes.c_double(), ctypes.c_int()
+    check(lib().attnb_profile_read(kernel.encode(), ctypes.byref(ms), ctypes.byref(n)))
+    return ms.value, n.value
 
 
 def stream_status(stream=None) -> None:

@@ -13,6 +13,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "runtime.h"
 
 namespace attnb {
 namespace {
@@ -109,6 +110,7 @@ void attn_block_simt_launch(const View3& Q, const View3& K, const View3& V, cons
   if ((int64_t)Q.H * Q.T == 0) return;
   const float qscale = kLog2e / std::sqrt(static_cast<float>(Q.Dh));
   const int Dh = Q.Dh;
+  ProfScope prof("attn_simt", stream);
   if (Dh <= 32) launch_rows<1>(Q, K, V, O, causal, qscale, stream);
   else if (Dh <= 64) launch_rows<2>(Q, K, V, O, causal, qscale, stream);
   else if (Dh <= 128) launch_rows<4>(Q, K, V, O, causal, qscale, stream);

@@ -551,6 +551,7 @@ void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View
   prm.counters = counters;
   prm.qtiles = p.qtiles;
   prm.status = status;
+  ProfScope prof("attn_tc", s);
   if (p.split3) dispatch_dhp<true>(p.dhp, maps, prm, p.qtiles, s);
   else dispatch_dhp<false>(p.dhp, maps, prm, p.qtiles, s);
 }

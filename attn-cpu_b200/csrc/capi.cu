@@ -12,6 +12,8 @@
 
 namespace attnb {
 const char* last_error_cstr();
+int profile_enable(int on);
+int profile_read(const char* kernel, double* total_ms, int* launches);
 }
 
 using namespace attnb;
@@ -221,6 +223,12 @@ extern "C" {
 const char* attnb_last_error(void) { return last_error_cstr(); }
 
 const char* attnb_version(void) { return "attnb 0.1 sm_100a"; }
+
+int attnb_profile_enable(int on) { return profile_enable(on); }
+
+int attnb_profile_read(const char* kernel, double* total_ms, int* launches) {
+  return profile_read(kernel, total_ms, launches);
+}
 
 int attnb_stream_status(void* stream) {
   return guarded([&] {

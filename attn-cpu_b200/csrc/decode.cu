@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "runtime.h"
 
 namespace attnb {
 namespace {
@@ -286,6 +287,7 @@ void decode_launch(const DecodePlan& p, const View3& Q, const View3& K, const Vi
     part_ml = reinterpret_cast<float2*>(static_cast<char*>(ws) + off);
   }
   const dim3 grid(p.nsplit, H);
+  ProfScope prof("decode", stream);
   if (p.fast) {
     const size_t sm = (2 * (kThreads / 32) + (kThreads / 32) * Dh) * sizeof(float);
     if (Dh <= 128)

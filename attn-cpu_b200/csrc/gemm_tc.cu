@@ -427,6 +427,7 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
   const int bn = p.split3 ? 128 : 256;
   const CUtensorMap tA_hi = make_tmap_2d(a_hi, p.M, p.Kp, p.Kp, BM, BK);
   const CUtensorMap tB_hi = make_tmap_2d(b_hi, p.N, p.Kp, p.Kp, bn, BK);
+  ProfScope prof("gemm_tc", s);
   if (p.split3) {
     const CUtensorMap tA_lo = make_tmap_2d(a_lo, p.M, p.Kp, p.Kp, BM, BK);
     const CUtensorMap tB_lo = make_tmap_2d(b_lo, p.N, p.Kp, p.Kp, bn, BK);

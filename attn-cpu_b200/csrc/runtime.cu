@@ -3,6 +3,7 @@
 
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <map>
 #include <memory>
 #include <vector>
@@ -146,6 +147,59 @@ CUtensorMap make_tmap_3d(const float* base, uint64_t depth, uint64_t rows, uint6
   if (r != CUDA_SUCCESS)
     fail(ATTNB_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed (" + std::to_string((int)r) + ")");
   return m;
+}
+
+static std::atomic<bool> g_prof_on{false};
+static std::mutex g_prof_mu;
+static std::map<std::string, std::vector<std::pair<cudaEvent_t, cudaEvent_t>>> g_prof;
+
+ProfScope::ProfScope(const char* kernel, cudaStream_t s) : name_(kernel), s_(s) {
+  if (!g_prof_on.load(std::memory_order_relaxed)) return;
+  if (cudaEventCreate(&a_) != cudaSuccess || cudaEventCreate(&b_) != cudaSuccess ||
+      cudaEventRecord(a_, s_) != cudaSuccess) {
+    cudaGetLastError();
+    a_ = b_ = nullptr;
+  }
+}
+
+ProfScope::~ProfScope() {
+  if (!a_) return;
+  if (cudaEventRecord(b_, s_) != cudaSuccess) {
+    cudaGetLastError();
+    return;
+  }
+  std::lock_guard<std::mutex> g(g_prof_mu);
+  g_prof[name_].emplace_back(a_, b_);
+}
+
+int profile_enable(int on) {
+  g_prof_on.store(on != 0);
+  return ATTNB_OK;
+}
+
+int profile_read(const char* kernel, double* total_ms, int* launches) {
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev;
+  {
+    std::lock_guard<std::mutex> g(g_prof_mu);
+    auto it = g_prof.find(kernel ? kernel : "");
+    if (it != g_prof.end()) ev.swap(it->second);
+  }
+  double ms = 0.0;
+  int n = 0;
+  for (auto& e : ev) {
+    float t = 0.f;
+    if (cudaEventSynchronize(e.second) == cudaSuccess &&
+        cudaEventElapsedTime(&t, e.first, e.second) == cudaSuccess) {
+      ms += t;
+      ++n;
+    }
+    cudaEventDestroy(e.first);
+    cudaEventDestroy(e.second);
+  }
+  cudaGetLastError();
+  if (total_ms) *total_ms = ms;
+  if (launches) *launches = n;
+  return ATTNB_OK;
 }
 
 int consume_status(DeviceCtx& c, cudaStream_t stream) {

@@ -68,6 +68,21 @@ CUtensorMap make_tmap_2d(const float* base, uint64_t rows, uint64_t cols, uint64
 CUtensorMap make_tmap_3d(const float* base, uint64_t depth, uint64_t rows, uint64_t cols,
                          uint64_t ld, uint64_t ld_depth, uint32_t box_rows, uint32_t box_cols);
 
+// CUDA-event timing of the dominant kernel of each call (attnb_profile_*):
+// construct before the launch, destroy after it, on the launching stream.
+class ProfScope {
+ public:
+  ProfScope(const char* kernel, cudaStream_t s);
+  ~ProfScope();
+  ProfScope(const ProfScope&) = delete;
+  ProfScope& operator=(const ProfScope&) = delete;
+
+ private:
+  const char* name_;
+  cudaStream_t s_;
+  cudaEvent_t a_ = nullptr, b_ = nullptr;
+};
+
 // Reads and clears the device status word of ctx (synchronises `stream`).
 int consume_status(DeviceCtx& c, cudaStream_t stream);
 

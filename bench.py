@@ -279,7 +279,7 @@ def setup_workload(w: str, rank: int, precision):
         e2e = lambda: attn_cpu.attn_block_dense(nQ, nK, nV, precision=precision)
         h2d = 4 * (Q.numel() + K.numel() + V.numel())
         d2h = 4 * O.numel()
-        return run, e2e, h2d, d2h, 1
+        return run, e2e, h2d, d2h, 2  # pack + attention
     if w == "decode":
         H, T, Dh = c["H"], c["T"], c["Dh"]
         Q = torch.randn(H, Dh, device="cuda", generator=g)
@@ -290,7 +290,7 @@ def setup_workload(w: str, rank: int, precision):
         hQ, hK, hV = (t.cpu().pin_memory() for t in (Q, K, V))
         nQ, nK, nV = hQ.numpy(), hK.numpy(), hV.numpy()
         e2e = lambda: attn_cpu.attn_step_dense(nQ, nK, nV)
-        return run, e2e, 4 * (Q.numel() + K.numel() + V.numel()), 4 * O.numel(), 2
+        return run, e2e, 4 * (Q.numel() + K.numel() + V.numel()), 4 * O.numel(), 2  # + merge
     if w.startswith("sgemm"):
         M, N, K = c["M"], c["N"], c["K"]
         A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1
@@ -300,7 +300,7 @@ def setup_workload(w: str, rank: int, precision):
         hA, hB = A.cpu().pin_memory(), B.cpu().pin_memory()
         nA, nB = hA.numpy(), hB.numpy()
         e2e = lambda: attn_cpu.gemm(nA, nB, precision=precision)
-        return run, e2e, 4 * (A.numel() + B.numel()), 4 * C.numel(), 3
+        return run, e2e, 4 * (A.numel() + B.numel()), 4 * C.numel(), 2  # pack + GEMM
     if w == "block":
         Bt, T, D, H = c["B"], c["T"], c["D"], c["H"]
         x = torch.randn(Bt, T, D, device="cuda", generator=g)
@@ -315,29 +315,76 @@ def setup_workload(w: str, rank: int, precision):
         nx = hx.numpy()
         e2e = lambda: [attn_cpu.mha_block_dense(nx[b], *hw, H, precision=precision)
                        for b in range(Bt)]
-        h2d = 4 * (x.numel() + Wi.numel() + bi.numel() + Wo.numel() + bo.numel()) * 1
-        return run, e2e, h2d, 4 * y.numel(), 4 + Bt
+        # per sequence (e2e calls the host API once per sequence): x_b and all weights
+        h2d = 4 * (x.numel() + Bt * (Wi.numel() + bi.numel() + Wo.numel() + bo.numel()))
+        return run, e2e, h2d, 4 * y.numel(), 4 + 2 * Bt  # 2 x (pack + GEMM), B x (pack + attn)
     raise KeyError(w)
 
 
-def roofline_of(w: str, ms: float, peaks: dict, precision) -> dict:
-    traffic = NCU_TRAFFIC.get((w, precision or "3xtf32"))
+# Dominant kernel of each workload (library profiling name) and its
+# algorithmic work per step.
+def dominant_of(w: str):
+    c = WORKLOADS[w]
+    if w == "prefill":
+        return "attn_tc", flops_of(w)
     if w == "decode":
-        achieved = bytes_of(w) / (ms * 1e-3) / 1e9
+        return "decode", bytes_of(w)
+    if w.startswith("sgemm"):
+        return "gemm_tc", flops_of(w)
+    if w == "block":  # QKV and output projections
+        B, T, D = c["B"], c["T"], c["D"]
+        return "gemm_tc", B * (2.0 * T * D * 3 * D + 2.0 * T * D * D)
+    raise KeyError(w)
+
+
+def roofline_of(w: str, kernel_ms: float, launches: int, peaks: dict, precision) -> dict:
+    """Dominant kernel's algorithmic rate: its work per step over its summed
+    launch durations per step (CUDA events on the launching stream)."""
+    name, work = dominant_of(w)
+    traffic = NCU_TRAFFIC.get((w, precision or "3xtf32"))
+    base = {"kernel": name, "launches_per_step": launches,
+            "kernel_ms_per_step": round(kernel_ms, 5), "traffic": traffic}
+    if w == "decode":
+        achieved = work / (kernel_ms * 1e-3) / 1e9
         peak = peaks["hbm_gbs"]
         return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
-                "frac": round(achieved / peak, 4), "traffic": traffic,
-                "peak_src": f"{peaks['src']} STREAM-style copy"}
-    achieved = flops_of(w) / (ms * 1e-3) / 1e12
-    # tcgen05 kind::tf32 runs at half the bf16 rate; the measured cuBLAS bf16
+                "frac": round(achieved / peak, 4),
+                "peak_src": f"{peaks['src']} STREAM-style copy (MEASURED_PEAKS.json hbm_gbs)",
+                **base}
+    achieved = work / (kernel_ms * 1e-3) / 1e12
+    # tcgen05 kind::tf32 issues at half the bf16 rate: the measured cuBLAS bf16
     # burst figure / 2 is the TF32 denominator.
     peak = peaks["bf16_tflops"] / 2
     r = {"bound": "tensor", "achieved": round(achieved, 2), "peak": round(peak, 1),
-         "unit": "TFLOP/s", "frac": round(achieved / peak, 4), "traffic": traffic,
-         "peak_src": f"{peaks['src']} bf16 burst / 2 (TF32 rate)"}
+         "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+         "peak_src": f"{peaks['src']} bf16 burst / 2 (TF32 rate)", **base}
     if (precision or "3xtf32") == "3xtf32":
+        # 3xTF32 issues three tf32 products per algorithmic one.
         r["frac_of_3xtf32_cap"] = round(3 * achieved / peak, 4)
     return r
+
+
+def kernel_time(run, w: str, steps: int, world: int, flush: bool):
+    """Per-step summed duration (ms) and launch count of the dominant kernel,
+    from the library's CUDA-event hooks over `steps` further steps."""
+    import torch
+
+    from attn_cpu import capi
+
+    name, _ = dominant_of(w)
+    fl = L2Flusher() if flush else None
+    capi.profile_read(name)  # discard anything recorded before
+    capi.profile_enable(True)
+    try:
+        for _ in range(steps):
+            if fl:
+                fl()
+            run()
+        torch.cuda.synchronize()
+    finally:
+        capi.profile_enable(False)
+    ms, n = capi.profile_read(name)
+    return max_over_ranks(ms / steps, world), n // max(1, steps)
 
 
 def measure_sharded(w: str, world: int, steps: int, warmup: int, precision, peaks):
@@ -374,9 +421,10 @@ def measure(w: str, rank: int, world: int, steps: int, warmup: int, precision, p
     work = flops_of(w) if w != "decode" else bytes_of(w)
     scale = 1e12 if WORKLOADS[w]["unit"] == "TFLOP/s" else 1e9
     value = world * work / (ms * 1e-3) / scale
+    k_ms, k_n = kernel_time(run, w, steps, world, flush)
     res = {"metric": WORKLOADS[w]["metric"], "value": round(value, 3),
            "unit": WORKLOADS[w]["unit"], "ms_per_step": round(ms, 5),
-           "roofline": roofline_of(w, ms, peaks, precision),
+           "roofline": roofline_of(w, k_ms, k_n, peaks, precision),
            "gpu_launches": launches * steps, "l2": "flushed between steps" if flush else
            "inputs larger than L2", "wall_s": round(wall, 3), "clocks": clk.summary()}
     if with_e2e:

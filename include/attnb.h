@@ -76,6 +76,15 @@ ATTNB_API const char* attnb_version(void);
  * (and clears it).  Synchronises the stream. */
 ATTNB_API int attnb_stream_status(void* stream);
 
+/* Kernel timing for measurements (no counterpart in the reference).  While
+ * enabled, every call records a CUDA event pair around its dominant kernel on
+ * the launching stream: "attn_tc" (tensor-core prefill), "attn_simt" (CUDA-core
+ * prefill), "gemm_tc" (SGEMM / projections), "decode" (decode step).
+ * attnb_profile_read synchronises the recorded events, returns the summed
+ * milliseconds and launch count for `kernel`, and forgets them. */
+ATTNB_API int attnb_profile_enable(int on);
+ATTNB_API int attnb_profile_read(const char* kernel, double* total_ms, int* launches);
+
 /* ---------------------------------------------------------------- SGEMM */
 /* C[M,N] = alpha * A[M,K] . B[K,N] + beta * C.
  * Replaces gemm::sgemm_blocked (include/gemm.h:11-14; src/gemm.cpp:319-415).
