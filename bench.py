@@ -54,9 +54,16 @@ WORKLOADS = {
                        "seq 2048 (mha_block_dense)"),
 }
 
-# DRAM bytes per launch of each dominant kernel from one ncu capture
-# (dram__bytes_read.sum + dram__bytes_write.sum); see profiles/.
-NCU_TRAFFIC = {}
+# DRAM bytes of each dominant kernel per step (its launches in one step) from
+# one-pass ncu captures of dram__bytes_read.sum + dram__bytes_write.sum on the
+# same problem; commands and figures in profiles/.  Cold-cache captures.
+NCU_TRAFFIC = {
+    ("prefill", "3xtf32"): 6.35e6,     # attn_tc, [1,8,512,64]: packed Q/K/V hi+lo
+    ("decode", "3xtf32"): 1.0798e9,    # decode: K + V once (1.0737e9) + split partials
+    ("decode", "tf32"): 1.0798e9,
+    ("sgemm-large", "3xtf32"): 97.78e9,  # gemm_tc 16384^3: packed operands re-read ~24x
+    ("block", "3xtf32"): 6.93e9,       # gemm_tc QKV (5.11e9) + output (1.82e9) projections
+}
 
 
 def flops_of(w: str) -> float:
