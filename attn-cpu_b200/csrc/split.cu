@@ -41,24 +41,42 @@ __device__ __forceinline__ void split_value(float x, bool split3, float& hi, flo
   lo = split3 ? (x - hi) : 0.f;
 }
 
+// One warp per output row; lanes walk the row four columns at a time, with
+// 16-byte loads when the source row is contiguous and aligned.
 __device__ void pack_rows(const PackJob& j, bool split3, int lb, int nb) {
+  constexpr int kWarps = kThreads / 32;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cp4 = j.cols_out >> 2;
-  const int64_t n = (int64_t)j.H * j.R * cp4;
-  for (int64_t i = (int64_t)lb * kThreads + threadIdx.x; i < n; i += (int64_t)nb * kThreads) {
-    const int64_t hr = i / cp4;
-    const int c = static_cast<int>(i % cp4) * 4;
+  const int64_t nrows = (int64_t)j.H * j.R;
+  const bool vec = j.sC == 1 && (j.sR & 3) == 0 && (j.sH & 3) == 0 &&
+                   (reinterpret_cast<uintptr_t>(j.src) & 15u) == 0;
+  for (int64_t hr = (int64_t)lb * kWarps + warp; hr < nrows; hr += (int64_t)nb * kWarps) {
     const int h = static_cast<int>(hr / j.R), r = static_cast<int>(hr % j.R);
     const float* s = j.src + h * j.sH + r * j.sR;
-    float x[4];
+    float4* oh = reinterpret_cast<float4*>(j.hi + hr * j.cols_out);
+    float4* ol = split3 ? reinterpret_cast<float4*>(j.lo + hr * j.cols_out) : nullptr;
+#pragma unroll 4
+    for (int c4 = lane; c4 < cp4; c4 += 32) {
+      const int c = c4 * 4;
+      float x[4];
+      if (vec && c + 3 < j.C) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(s + c));
+        x[0] = v.x;
+        x[1] = v.y;
+        x[2] = v.z;
+        x[3] = v.w;
+      } else {
 #pragma unroll
-    for (int k = 0; k < 4; ++k) x[k] = (c + k < j.C) ? s[(c + k) * j.sC] * j.scale : 0.f;
-    float4 h4, l4;
-    split_value(x[0], split3, h4.x, l4.x);
-    split_value(x[1], split3, h4.y, l4.y);
-    split_value(x[2], split3, h4.z, l4.z);
-    split_value(x[3], split3, h4.w, l4.w);
-    reinterpret_cast<float4*>(j.hi + hr * j.cols_out)[c >> 2] = h4;
-    if (split3) reinterpret_cast<float4*>(j.lo + hr * j.cols_out)[c >> 2] = l4;
+        for (int k = 0; k < 4; ++k) x[k] = (c + k < j.C) ? s[(int64_t)(c + k) * j.sC] : 0.f;
+      }
+      float4 h4, l4;
+      split_value(x[0] * j.scale, split3, h4.x, l4.x);
+      split_value(x[1] * j.scale, split3, h4.y, l4.y);
+      split_value(x[2] * j.scale, split3, h4.z, l4.z);
+      split_value(x[3] * j.scale, split3, h4.w, l4.w);
+      oh[c4] = h4;
+      if (split3) ol[c4] = l4;
+    }
   }
 }
 
@@ -126,8 +144,7 @@ void pack_launch(const PackJob* jobs, int njobs, bool split3, unsigned* zero, in
     if (j.transpose) {
       blocks = (int64_t)j.H * ((j.rows_out + 31) / 32) * ((j.cols_out + 31) / 32);
     } else {
-      const int64_t n4 = (int64_t)j.H * j.R * (j.cols_out / 4);
-      blocks = (n4 + kThreads - 1) / kThreads;
+      blocks = ((int64_t)j.H * j.R + kThreads / 32 - 1) / (kThreads / 32);  // warp per row
     }
     blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)num_sms * 8));
     total += static_cast<int>(blocks);
