@@ -9,8 +9,8 @@
 // src/attn_block.cpp:104-241.  The same function, tiled for the tensor cores:
 //
 //   CTA = 128 query rows (one per TMEM lane) of one head, a range of 128-key
-//   tiles.  Warp 0 streams, through two shared-memory rings, 32-wide slices
-//   of Q and K (S phase) and 32-key slices of V (PV phase) with TMA.  Warp 1 issues
+//   tiles.  Warp 0 streams, through a shared-memory ring, 32-wide slices of
+//   Q and K (S phase) and of V^T (PV phase) with TMA.  Warp 1 issues
 //     S  = Q.K^T          into TMEM (3xTF32: big = hi*hi, small = hi*lo + lo*hi)
 //     PV = P.V            with P read straight from TMEM (tcgen05.mma A-from-TMEM)
 //   Warps 2-5 (thread = query row) read S, keep the running max m and sum l,
@@ -22,9 +22,8 @@
 //   small kernel merges the partial (m, l, O).
 //
 // Operands arrive pre-packed by split.cu: Q scaled by log2(e)/sqrt(Dh), head
-// size zero-padded to a multiple of 32, each split into tf32 hi + fp32 lo for
-// 3xTF32.  Q and K feed the S product K-major; V feeds the PV product
-// MN-major (head dim contiguous), so no operand is transposed.
+// size zero-padded to a multiple of 32, V transposed per head (K-major for the
+// PV product), each split into tf32 hi + fp32 lo for 3xTF32.
 #include <algorithm>
 #include <atomic>
 #include <cmath>
@@ -48,9 +47,7 @@ struct AttnCfg {
   static constexpr int NPART = SPLIT3 ? 2 : 1;
   static constexpr int QBOX = BM * BK * 4;   // 16 KB
   static constexpr int KBOX = BN * BK * 4;   // 16 KB
-  // 32 keys of V, MN-major: DHP/32 boxes of [32 keys x 32 head dims] (4 KB)
-  static constexpr int VBOX = DHP * BK * 4;
-  static constexpr int VCHUNK = 32 * BK * 4;
+  static constexpr int VBOX = DHP * BK * 4;  // 32 keys of V^T
   // Two rings: Q+K slices for the S product, V^T slices for the PV product,
   // so all of a tile's V slices can be in flight while S and the softmax run.
   static constexpr int S_STAGE = NPART * (QBOX + KBOX);
@@ -117,7 +114,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using Cfg = AttnCfg<DHP, SPLIT3>;
   constexpr int SST = Cfg::S_STAGES, VST = Cfg::V_STAGES;
   constexpr uint32_t IDESC_S = idesc_tf32(BM, BN);
-  constexpr uint32_t IDESC_PV = idesc_tf32(BM, DHP, true);  // V read N(head dim)-contiguous
+  constexpr uint32_t IDESC_PV = idesc_tf32(BM, DHP);
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t sfull[SST], sempty[SST], vfull[VST], vempty[VST];
@@ -201,12 +198,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t fb = smem_addr(&vfull[rv.stage]), va = v_addr(rv.stage);
           mbar_arrive_expect_tx(fb, Cfg::V_STAGE);
-#pragma unroll
-          for (int c = 0; c < DHP / 32; ++c) {
-            tma_load_3d(va + c * Cfg::VCHUNK, &tmVh, fb, c * 32, j * BN + vb * BK, h);
-            if (SPLIT3)
-              tma_load_3d(va + Cfg::VBOX + c * Cfg::VCHUNK, &tmVl, fb, c * 32, j * BN + vb * BK, h);
-          }
+          tma_load_3d(va, &tmVh, fb, j * BN + vb * BK, 0, h);
+          if (SPLIT3) tma_load_3d(va + Cfg::VBOX, &tmVl, fb, j * BN + vb * BK, 0, h);
           rv.note_issue();
           rv.advance();
         }
@@ -269,11 +262,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < BK / 8; ++kk) {
             const uint32_t acc = (vb | kk) != 0 ? 1u : 0u;
             const uint32_t key = vb * BK + kk * 8;
-            const uint64_t vh = sdesc_mnmajor_sw128(sa + kk * 1024, Cfg::VCHUNK, 1024);
+            const uint64_t vh = sdesc_kmajor_sw128(sa + kk * 32);
             mma_tf32_ts(tmem + Cfg::PV_BIG, tmem + Cfg::S_BIG + key, vh, IDESC_PV, acc);
             if (SPLIT3) {
-              const uint64_t vl =
-                  sdesc_mnmajor_sw128(sa + Cfg::VBOX + kk * 1024, Cfg::VCHUNK, 1024);
+              const uint64_t vl = sdesc_kmajor_sw128(sa + Cfg::VBOX + kk * 32);
               mma_tf32_ts(tmem + Cfg::PV_SMALL, tmem + Cfg::S_BIG + key, vl, IDESC_PV, acc);
               mma_tf32_ts(tmem + Cfg::PV_SMALL, tmem + Cfg::S_SMALL + key, vh, IDESC_PV, 1u);
             }
@@ -478,6 +470,7 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
   p.T = T;
   p.Dh = Dh;
   p.dhp = (Dh + 31) / 32 * 32;
+  p.tp = (T + 3) / 4 * 4;
   p.split3 = precision != ATTNB_PREC_TF32;
   p.qtiles = (L + BM - 1) / BM;
   const int n_kv = (T + BN - 1) / BN;
@@ -495,7 +488,7 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
   };
   const int parts = p.split3 ? 2 : 1;
   const size_t q = (size_t)H * L * p.dhp * 4, k = (size_t)H * T * p.dhp * 4,
-               v = (size_t)H * T * p.dhp * 4;
+               v = (size_t)H * p.dhp * p.tp * 4;
   p.off_q = take(q * parts);
   p.off_k = take(k * parts);
   p.off_v = take(v * parts);
@@ -512,7 +505,7 @@ void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View
                  cudaStream_t s) {
   char* w = static_cast<char*>(ws);
   const size_t q = (size_t)p.H * p.L * p.dhp, k = (size_t)p.H * p.T * p.dhp,
-               v = (size_t)p.H * p.T * p.dhp;
+               v = (size_t)p.H * p.dhp * p.tp;
   float* qh = reinterpret_cast<float*>(w + p.off_q);
   float* kh = reinterpret_cast<float*>(w + p.off_k);
   float* vh = reinterpret_cast<float*>(w + p.off_v);
@@ -521,21 +514,21 @@ void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View
   float* vl = p.split3 ? vh + v : nullptr;
   const float qscale = kLog2e / std::sqrt(static_cast<float>(p.Dh));
   unsigned* counters = p.nsplit > 1 ? reinterpret_cast<unsigned*>(w + p.off_cnt) : nullptr;
-  // Q (scaled by log2(e)/sqrt(Dh)), K and V as [H, rows, dhp], all in one
-  // launch, which also clears the merge counters.
+  // Q (scaled by log2(e)/sqrt(Dh)) and K as [H, rows, dhp]; V transposed to
+  // [H, dhp, tp]; all in one launch, which also clears the merge counters.
   const PackJob jobs[3] = {
       {Q.data, Q.sH, Q.sT, Q.sD, p.H, p.L, p.Dh, p.L, p.dhp, false, qscale, qh, ql},
       {K.data, K.sH, K.sT, K.sD, p.H, p.T, p.Dh, p.T, p.dhp, false, 1.f, kh, kl},
-      {V.data, V.sH, V.sT, V.sD, p.H, p.T, p.Dh, p.T, p.dhp, false, 1.f, vh, vl}};
+      {V.data, V.sH, V.sT, V.sD, p.H, p.T, p.Dh, p.dhp, p.tp, true, 1.f, vh, vl}};
   pack_launch(jobs, 3, p.split3, counters, p.H * p.qtiles, num_sms, s);
   CUtensorMap maps[6];
   maps[0] = make_tmap_3d(qh, p.H, p.L, p.dhp, p.dhp, (uint64_t)p.L * p.dhp, BM, BK);
   maps[2] = make_tmap_3d(kh, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BN, BK);
-  maps[4] = make_tmap_3d(vh, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BK, 32);
+  maps[4] = make_tmap_3d(vh, p.H, p.dhp, p.tp, p.tp, (uint64_t)p.dhp * p.tp, p.dhp, BK);
   if (p.split3) {
     maps[1] = make_tmap_3d(ql, p.H, p.L, p.dhp, p.dhp, (uint64_t)p.L * p.dhp, BM, BK);
     maps[3] = make_tmap_3d(kl, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BN, BK);
-    maps[5] = make_tmap_3d(vl, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BK, 32);
+    maps[5] = make_tmap_3d(vl, p.H, p.dhp, p.tp, p.tp, (uint64_t)p.dhp * p.tp, p.dhp, BK);
   } else {
     maps[1] = maps[0];
     maps[3] = maps[2];

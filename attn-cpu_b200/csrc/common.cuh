@@ -206,30 +206,12 @@ __device__ __forceinline__ uint64_t sdesc_kmajor_sw128(uint32_t saddr) {
   return d;
 }
 
-// Shared-memory matrix descriptor for an MN-major operand stored with the
-// 128-byte swizzle: each 1024-byte atom holds 8 K-rows of 32 consecutive
-// MN-elements (128 bytes each); atoms for the next 32 MN-elements are
-// `mn_stride` bytes apart, atoms for the next 8 K-rows `k_stride` bytes
-// apart.  One tf32 MMA (K = 8) reads exactly one atom row band.
-__device__ __forceinline__ uint64_t sdesc_mnmajor_sw128(uint32_t saddr, uint32_t mn_stride,
-                                                        uint32_t k_stride) {
-  uint64_t d = 0;
-  d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);           // start address
-  d |= static_cast<uint64_t>((mn_stride >> 4) & 0x3FFFu) << 16;  // leading byte offset
-  d |= static_cast<uint64_t>((k_stride >> 4) & 0x3FFFu) << 32;   // stride byte offset
-  d |= static_cast<uint64_t>(1) << 46;                           // descriptor version
-  d |= static_cast<uint64_t>(2) << 61;                           // 128-byte swizzle
-  return d;
-}
-
-// Instruction descriptor: tf32 x tf32 -> f32, A K-major, B K-major or
-// (b_mn_major) MN-major, M x N tile (M in {64,128}, N % 16 == 0 for M=128,
-// N <= 256).
-__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N, bool b_mn_major = false) {
+// Instruction descriptor: tf32 x tf32 -> f32, both operands K-major,
+// M x N tile (M in {64,128}, N % 8 == 0 (M=64) or N % 16 == 0 (M=128), N <= 256).
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
   return (1u << 4)                                   // D = f32
          | (2u << 7)                                 // A = tf32
          | (2u << 10)                                // B = tf32
-         | ((b_mn_major ? 1u : 0u) << 16)            // B major-ness
          | (static_cast<uint32_t>(N >> 3) << 17)     // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
 }

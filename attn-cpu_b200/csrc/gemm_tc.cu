@@ -109,7 +109,7 @@ __device__ __forceinline__ void store32(float* crow, int row, int col0, const fl
   }
 }
 
-template <int BN, bool SPLIT3, bool B_MN>
+template <int BN, bool SPLIT3>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                    const __grid_constant__ CUtensorMap tmA_lo,
@@ -119,9 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const float* __restrict__ bias, int* status) {
   using Cfg = GemmCfg<BN, SPLIT3>;
   constexpr int STAGES = Cfg::STAGES;
-  constexpr uint32_t IDESC = idesc_tf32(BM, BN, B_MN);
-  // MN-major B: BN/32 boxes of [32 K-rows x 32 N] (4 KB each) per stage.
-  constexpr uint32_t B_MN_CHUNK = 32 * BK * 4;
+  constexpr uint32_t IDESC = idesc_tf32(BM, BN);
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
@@ -197,23 +195,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t fb = smem_addr(&full_bar[stage]);
           mbar_arrive_expect_tx(fb, Cfg::STAGE_BYTES);
           tma_load_2d(sA_hi(stage), &tmA_hi, fb, kb * BK, tm * BM);
-          if (B_MN) {
-#pragma unroll
-            for (int c = 0; c < BN / 32; ++c)
-              tma_load_2d(sB_hi(stage) + c * B_MN_CHUNK, &tmB_hi, fb, tn * BN + c * 32, kb * BK);
-          } else {
-            tma_load_2d(sB_hi(stage), &tmB_hi, fb, kb * BK, tn * BN);
-          }
+          tma_load_2d(sB_hi(stage), &tmB_hi, fb, kb * BK, tn * BN);
           if (SPLIT3) {
             tma_load_2d(sA_lo(stage), &tmA_lo, fb, kb * BK, tm * BM);
-            if (B_MN) {
-#pragma unroll
-              for (int c = 0; c < BN / 32; ++c)
-                tma_load_2d(sB_lo(stage) + c * B_MN_CHUNK, &tmB_lo, fb, tn * BN + c * 32,
-                            kb * BK);
-            } else {
-              tma_load_2d(sB_lo(stage), &tmB_lo, fb, kb * BK, tn * BN);
-            }
+            tma_load_2d(sB_lo(stage), &tmB_lo, fb, kb * BK, tn * BN);
           }
           issued_mask |= 1u << stage;
           issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
@@ -258,15 +243,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int kk = 0; kk < BK / 8; ++kk) {
               const uint32_t acc = (kb != kb0 || kk != 0) ? 1u : 0u;
               const uint64_t a_hi = sdesc_kmajor_sw128(sA_hi(stage) + kk * 32);
-              const uint64_t b_hi =
-                  B_MN ? sdesc_mnmajor_sw128(sB_hi(stage) + kk * 1024, B_MN_CHUNK, 1024)
-                       : sdesc_kmajor_sw128(sB_hi(stage) + kk * 32);
+              const uint64_t b_hi = sdesc_kmajor_sw128(sB_hi(stage) + kk * 32);
               mma_tf32(d_big, a_hi, b_hi, IDESC, acc);
               if (SPLIT3) {
                 const uint64_t a_lo = sdesc_kmajor_sw128(sA_lo(stage) + kk * 32);
-                const uint64_t b_lo =
-                    B_MN ? sdesc_mnmajor_sw128(sB_lo(stage) + kk * 1024, B_MN_CHUNK, 1024)
-                         : sdesc_kmajor_sw128(sB_lo(stage) + kk * 32);
+                const uint64_t b_lo = sdesc_kmajor_sw128(sB_lo(stage) + kk * 32);
                 mma_tf32(d_small, a_hi, b_lo, IDESC, acc);
                 mma_tf32(d_small, a_lo, b_hi, IDESC, 1u);
               }
@@ -369,7 +350,7 @@ __global__ void scale_c_kernel(float* C, int64_t ldc, int M, int N, float beta) 
   }
 }
 
-template <int BN, bool SPLIT3, bool B_MN>
+template <int BN, bool SPLIT3>
 void launch_gemm(const GemmPlan& p, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
                  const CUtensorMap& b_hi, const CUtensorMap& b_lo, float* C, int64_t ldc,
                  float alpha, float beta, const float* bias, int* status, int num_sms,
@@ -380,13 +361,13 @@ void launch_gemm(const GemmPlan& p, const CUtensorMap& a_hi, const CUtensorMap& 
   ATTNB_CUDA(cudaGetDevice(&dev));
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
-    ATTNB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT3, B_MN>,
+    ATTNB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT3>,
                                     cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
     configured.fetch_or(bit);
   }
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = std::min(tiles, num_sms);
-  ATTNB_CUDA(launch_pdl(gemm_tc_kernel<BN, SPLIT3, B_MN>, dim3(grid), dim3(kThreads), Cfg::SMEM, s,
+  ATTNB_CUDA(launch_pdl(gemm_tc_kernel<BN, SPLIT3>, dim3(grid), dim3(kThreads), Cfg::SMEM, s,
                         a_hi, a_lo, b_hi, b_lo, p.M, p.N, p.Kp, C, ldc, alpha, beta, bias,
                         status));
 }
@@ -410,10 +391,7 @@ GemmPlan gemm_plan(int M, int N, int K, int precision) {
     return o;
   };
   const size_t a_bytes = (size_t)M * p.Kp * sizeof(float);
-  // B is packed K-major [N, Kp] or, from a row-major [K, N] source, MN-major
-  // [K, Np] with Np = N rounded up to 4 (16-byte rows); room for either.
-  p.Np = (N + 3) / 4 * 4;
-  const size_t b_bytes = std::max((size_t)N * p.Kp, (size_t)K * p.Np) * sizeof(float);
+  const size_t b_bytes = (size_t)N * p.Kp * sizeof(float);
   p.off_a_hi = take(a_bytes);
   p.off_a_lo = p.split3 ? take(a_bytes) : 0;
   p.off_b_hi = take(b_bytes);
@@ -443,37 +421,21 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
   PackJob jobs[2];
   jobs[0] = a_kmajor ? PackJob{A, 0, lda, 1, 1, p.M, p.K, p.M, p.Kp, false, 1.f, a_hi, a_lo}
                      : PackJob{A, 0, lda, 1, 1, p.K, p.M, p.M, p.Kp, true, 1.f, a_hi, a_lo};
-  // B [N, K] stays K-major; B [K, N] is split in place as MN-major [K, Np]
-  // (the MMA reads it N-contiguous, so no transpose is needed).
   jobs[1] = b_kmajor ? PackJob{B, 0, ldb, 1, 1, p.N, p.K, p.N, p.Kp, false, 1.f, b_hi, b_lo}
-                     : PackJob{B, 0, ldb, 1, 1, p.K, p.N, p.K, p.Np, false, 1.f, b_hi, b_lo};
+                     : PackJob{B, 0, ldb, 1, 1, p.K, p.N, p.N, p.Kp, true, 1.f, b_hi, b_lo};
   pack_launch(jobs, 2, p.split3, nullptr, 0, num_sms, s);
   const int bn = p.split3 ? 128 : 256;
-  // K-major B: boxes of [bn rows x 32 K]; MN-major B: boxes of [32 K-rows x 32 N]
-  // over a map with K rows (rows past K read as zero).
-  auto b_map = [&](const float* b) {
-    return b_kmajor ? make_tmap_2d(b, p.N, p.Kp, p.Kp, bn, BK)
-                    : make_tmap_2d(b, p.K, p.Np, p.Np, BK, 32);
-  };
   const CUtensorMap tA_hi = make_tmap_2d(a_hi, p.M, p.Kp, p.Kp, BM, BK);
-  const CUtensorMap tB_hi = b_map(b_hi);
+  const CUtensorMap tB_hi = make_tmap_2d(b_hi, p.N, p.Kp, p.Kp, bn, BK);
   ProfScope prof("gemm_tc", s);
   if (p.split3) {
     const CUtensorMap tA_lo = make_tmap_2d(a_lo, p.M, p.Kp, p.Kp, BM, BK);
-    const CUtensorMap tB_lo = b_map(b_lo);
-    if (b_kmajor)
-      launch_gemm<128, true, false>(p, tA_hi, tA_lo, tB_hi, tB_lo, C, ldc, alpha, beta, bias,
-                                    status, num_sms, s);
-    else
-      launch_gemm<128, true, true>(p, tA_hi, tA_lo, tB_hi, tB_lo, C, ldc, alpha, beta, bias,
-                                   status, num_sms, s);
+    const CUtensorMap tB_lo = make_tmap_2d(b_lo, p.N, p.Kp, p.Kp, bn, BK);
+    launch_gemm<128, true>(p, tA_hi, tA_lo, tB_hi, tB_lo, C, ldc, alpha, beta, bias, status,
+                           num_sms, s);
   } else {
-    if (b_kmajor)
-      launch_gemm<256, false, false>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias,
-                                     status, num_sms, s);
-    else
-      launch_gemm<256, false, true>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias,
-                                    status, num_sms, s);
+    launch_gemm<256, false>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias, status,
+                            num_sms, s);
   }
 }
 

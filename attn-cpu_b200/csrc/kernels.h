@@ -43,7 +43,7 @@ void attn_block_simt_launch(const View3& Q, const View3& K, const View3& V, cons
 
 // ---------------------------------------- tcgen05 prefill attention (K3)
 struct AttnTcPlan {
-  int H, L, T, Dh, dhp, qtiles, nsplit, tiles_per_split;
+  int H, L, T, Dh, dhp, tp, qtiles, nsplit, tiles_per_split;
   bool split3;
   size_t off_q, off_k, off_v, off_po, off_pml, off_cnt, ws_bytes;
 };
@@ -99,7 +99,7 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
 // C[M,N] = alpha * A.B + beta * C (+ bias[n]).  A is [M,K] (a_kmajor: rows of
 // K, pitch lda) or [K,M] (pitch lda); B is [N,K] (b_kmajor) or [K,N].
 struct GemmPlan {
-  int M, N, K, Kp, Np;
+  int M, N, K, Kp;
   bool split3;
   size_t off_a_hi, off_a_lo, off_b_hi, off_b_lo, ws_bytes;
 };
