@@ -22,7 +22,7 @@ PREC = {None: -1, "default": -1, "3xtf32": 0, "tf32": 1}
 
 # Every symbol include/attnb.h declares.
 EXPORTED = [
-    "attnb_last_error", "attnb_version", "attnb_stream_status",
+    "attnb_last_error", "attnb_version", "attnb_stream_status", "attnb_selftest_wait_timeout",
     "attnb_profile_enable", "attnb_profile_read",
     "attnb_sgemm", "attnb_gemm_jit", "attnb_sgemm_dev", "attnb_linear_dev",
     "attnb_attn_step_dense", "attnb_attn_step_dense_dev", "attnb_attn_step_dense_noalloc",
@@ -58,6 +58,7 @@ def lib() -> ctypes.CDLL:
         L.attnb_last_error.restype = ctypes.c_char_p
         L.attnb_version.restype = ctypes.c_char_p
         L.attnb_stream_status.argtypes = [vp]
+        L.attnb_selftest_wait_timeout.argtypes = [i, vp]
         L.attnb_profile_enable.argtypes = [i]
         L.attnb_profile_read.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
                                          ctypes.POINTER(ctypes.c_int)]

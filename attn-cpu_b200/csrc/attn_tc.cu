@@ -55,7 +55,13 @@ struct AttnCfg {
   static constexpr int V_STAGE = NPART * VBOX;
   static constexpr int V_STAGES_FIT = (225 * 1024 - S_STAGES * S_STAGE) / V_STAGE;
   static constexpr int V_STAGES = V_STAGES_FIT < 4 ? V_STAGES_FIT : 4;
-  static constexpr int SMEM = S_STAGES * S_STAGE + V_STAGES * V_STAGE + 1024;
+  static constexpr int RING_BYTES = S_STAGES * S_STAGE + V_STAGES * V_STAGE;
+  static constexpr int SMEM = RING_BYTES + 1024;
+  // Split merge: another split's partial tile ([DHP][128] floats) and its
+  // (m, l) row pairs, bulk-copied into the idle rings.
+  static constexpr int PART_TILE = DHP * BM * 4;
+  static constexpr int PART_ML = BM * 8;
+  static constexpr int MAX_MERGE = RING_BYTES / (PART_TILE + PART_ML);
   static constexpr int S_BIG = 0;
   static constexpr int S_SMALL = BN;
   static constexpr int PV_BIG = NPART * BN;
@@ -64,6 +70,7 @@ struct AttnCfg {
   static_assert(DHP % 32 == 0 && DHP <= 128, "head size padded to 32..128");
   static_assert(V_STAGES >= 2, "V ring needs two stages");
   static_assert(BM * (DHP + 1) * 4 <= S_STAGES * S_STAGE, "output staging fits the S ring");
+  static_assert(MAX_MERGE >= 1, "merge buffers fit the rings");
   static_assert(PV_BIG + NPART * DHP <= TMEM_COLS, "TMEM budget");
 };
 
@@ -97,6 +104,7 @@ __device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* s
 
 struct AttnParams {
   int L, T, H, Dh, causal, nsplit, tiles_per_split, qtiles;
+  int o_tma;  // the output tile leaves through the tmO tensor map
   float* O;
   int64_t osH, osT, osD;
   float* part_o;       // [nsplit][H][qtiles][DHP][128] (nsplit > 1)
@@ -110,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
                    const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
                    const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
-                   const AttnParams p) {
+                   const __grid_constant__ CUtensorMap tmO, const AttnParams p) {
   using Cfg = AttnCfg<DHP, SPLIT3>;
   constexpr int SST = Cfg::S_STAGES, VST = Cfg::V_STAGES;
   constexpr uint32_t IDESC_S = idesc_tf32(BM, BN);
@@ -118,9 +126,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t sfull[SST], sempty[SST], vfull[VST], vempty[VST];
-  __shared__ __align__(8) uint64_t s_bar, p_bar, pv_bar, final_bar;
+  __shared__ __align__(8) uint64_t s_bar, p_bar, pv_bar, final_bar, merge_bar;
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
+  __shared__ int softmax_failed;  // any softmax thread saw a wait fail
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, split = blockIdx.y, h = blockIdx.z;
@@ -139,6 +148,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 0) {
     abort_flag = 0;
+    softmax_failed = 0;
     for (int i = 0; i < SST; ++i) {
       mbar_init(smem_addr(&sfull[i]), 1);
       mbar_init(smem_addr(&sempty[i]), 1);
@@ -151,6 +161,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_addr(&p_bar), 4);
     mbar_init(smem_addr(&pv_bar), 1);
     mbar_init(smem_addr(&final_bar), 1);
+    mbar_init(smem_addr(&merge_bar), 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -356,9 +367,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // Rows are owned one per thread, so global traffic goes through layouts
     // that keep a warp's accesses contiguous: split partials are stored
-    // column-major per tile ([d][row]), and the final tile is staged in the
-    // (now idle) shared-memory ring and written row by row.
+    // column-major per tile ([d][row]) and read back with bulk copies, and the
+    // final tile is staged in the (now idle) shared-memory rings and written
+    // with TMA stores (or row by row when the output view does not allow TMA).
     const size_t tile_id = (size_t)h * p.qtiles + qt;
+    uint8_t* ring = smem_raw + (base - smem_addr(smem_raw));
+    // Wait results can differ between threads after an abort; every branch
+    // below that holds a barrier of the four softmax warps is taken on a
+    // decision they share.
+    auto all_ok = [&](bool mine) {
+      if (!mine) softmax_failed = 1;
+      named_bar_sync(1, 128);
+      return softmax_failed == 0;
+    };
+    ok = all_ok(ok);
     bool write_out = (p.nsplit == 1) && ok;
     if (p.nsplit > 1 && ok) {
       const size_t pbase = ((size_t)split * p.H * p.qtiles + tile_id) * BM;
@@ -373,50 +395,88 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (r == 0) s_last = (atomicAdd(cnt, 1u) == (unsigned)(p.nsplit - 1));
       named_bar_sync(1, 128);
       if (s_last) {
-        __threadfence();
-        // Fold the other splits into this CTA's own (m, l, o) with the same
-        // running-max update.
-        for (int sp = 0; sp < p.nsplit; ++sp) {
-          if (sp == split) continue;
-          const size_t qb = ((size_t)sp * p.H * p.qtiles + tile_id) * BM;
-          const float2 ml = __ldcg(&p.part_ml[qb + r]);
-          const float* src = p.part_o + qb * DHP + r;
-          const float m_new = fmaxf(m, ml.x);
-          const float a = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
-          const float b = (ml.x == -INFINITY) ? 0.f : fast_exp2(ml.x - m_new);
-          l = l * a + ml.y * b;
-          constexpr int CH = (DHP % 64 == 0) ? 64 : 32;  // loads kept in flight together
-          static_assert(DHP % CH == 0, "merge chunks cover the head");
-#pragma unroll
-          for (int c = 0; c < DHP / CH; ++c) {
-            float v[CH];
-#pragma unroll
-            for (int k = 0; k < CH; ++k) v[k] = __ldcg(src + (size_t)(c * CH + k) * BM);
-#pragma unroll
-            for (int k = 0; k < CH; ++k) o[c * CH + k] = fmaf(o[c * CH + k], a, v[k] * b);
+        // Fetch every other split's partial tile and (m, l) pairs at once.
+        const int nother = p.nsplit - 1;  // <= Cfg::MAX_MERGE (host plan)
+        if (r == 0) {
+          __threadfence();
+          fence_proxy_async_global();
+          const uint32_t mb = smem_addr(&merge_bar);
+          mbar_arrive_expect_tx(mb, nother * (Cfg::PART_TILE + Cfg::PART_ML));
+          int k = 0;
+          for (int sp = 0; sp < p.nsplit; ++sp) {
+            if (sp == split) continue;
+            const size_t qb = ((size_t)sp * p.H * p.qtiles + tile_id) * BM;
+            bulk_load(base + k * Cfg::PART_TILE, p.part_o + qb * DHP, Cfg::PART_TILE, mb);
+            bulk_load(base + nother * Cfg::PART_TILE + k * Cfg::PART_ML, p.part_ml + qb,
+                      Cfg::PART_ML, mb);
+            ++k;
           }
-          m = m_new;
         }
-        if (r == 0) *cnt = 0u;  // cleared again for the next call
-        write_out = true;
+        const bool got = all_ok(mbar_wait(smem_addr(&merge_bar), 0, abort_p, p.status));
+        if (got) {
+          // Fold them into this CTA's own (m, l, o) with the running-max update.
+          const float* tiles = reinterpret_cast<const float*>(ring);
+          const float2* mls =
+              reinterpret_cast<const float2*>(ring + nother * Cfg::PART_TILE);
+          for (int k = 0; k < nother; ++k) {
+            const float2 ml = mls[k * BM + r];
+            const float m_new = fmaxf(m, ml.x);
+            const float a = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
+            const float b2 = (ml.x == -INFINITY) ? 0.f : fast_exp2(ml.x - m_new);
+            l = l * a + ml.y * b2;
+            const float* t = tiles + (size_t)k * DHP * BM + r;
+#pragma unroll
+            for (int d = 0; d < DHP; ++d) o[d] = fmaf(o[d], a, t[d * BM] * b2);
+            m = m_new;
+          }
+          if (r == 0) *cnt = 0u;  // cleared again for the next call
+          write_out = true;
+        }
+        // Copies that never landed (only after an abort) finish before exit.
+        if (!got && r == 0) drain_wait(smem_addr(&merge_bar), 0, p.status);
+        named_bar_sync(1, 128);  // merge buffers are read before staging reuses them
       }
     }
     if (write_out) {
-      // Stage the normalised tile (row stride DHP + 1: conflict-free column
-      // writes), then write each row with the warp's lanes along the row.
-      float* stile = reinterpret_cast<float*>(smem_raw + (base - smem_addr(smem_raw)));
       const float inv = 1.f / l;
+      if (p.o_tma) {
+        // DHP/32 boxes of [128 rows x 32 columns], 128-byte swizzled, each
+        // thread writing its row as eight 16-byte chunks.
 #pragma unroll
-      for (int d = 0; d < DHP; ++d) stile[r * (DHP + 1) + d] = o[d] * inv;
-      named_bar_sync(1, 128);
-      const int rows = min(BM, p.L - qt * BM);
-      float* obase = p.O + h * p.osH + (int64_t)qt * BM * p.osT;
+        for (int bx = 0; bx < DHP / 32; ++bx) {
+          uint8_t* box = ring + bx * (BM * 128);
+#pragma unroll
+          for (int c = 0; c < 8; ++c) {
+            const int d = bx * 32 + c * 4;
+            *reinterpret_cast<float4*>(box + r * 128 + ((c ^ (r & 7)) << 4)) =
+                make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
+          }
+        }
+        fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (r == 0) {
+#pragma unroll
+          for (int bx = 0; bx < DHP / 32; ++bx)
+            tma_store_3d(&tmO, base + bx * (BM * 128), bx * 32, qt * BM, h);
+          bulk_commit_group();
+          bulk_wait_read_all();
+        }
+      } else {
+        // Stage the normalised tile (row stride DHP + 1: conflict-free column
+        // writes), then write each row with the warp's lanes along the row.
+        float* stile = reinterpret_cast<float*>(ring);
+#pragma unroll
+        for (int d = 0; d < DHP; ++d) stile[r * (DHP + 1) + d] = o[d] * inv;
+        named_bar_sync(1, 128);
+        const int rows = min(BM, p.L - qt * BM);
+        float* obase = p.O + h * p.osH + (int64_t)qt * BM * p.osT;
 #pragma unroll 4
-      for (int rr = quarter; rr < rows; rr += 4) {
-        float* orow = obase + (int64_t)rr * p.osT;
+        for (int rr = quarter; rr < rows; rr += 4) {
+          float* orow = obase + (int64_t)rr * p.osT;
 #pragma unroll
-        for (int dd = 0; dd < DHP; dd += 32)
-          if (dd + lane < p.Dh) orow[(dd + lane) * p.osD] = stile[rr * (DHP + 1) + dd + lane];
+          for (int dd = 0; dd < DHP; dd += 32)
+            if (dd + lane < p.Dh) orow[(dd + lane) * p.osD] = stile[rr * (DHP + 1) + dd + lane];
+        }
       }
     }
   }
@@ -444,7 +504,16 @@ void launch_attn(const CUtensorMap* maps, const AttnParams& prm, int qtiles, cud
   }
   const dim3 grid(qtiles, prm.nsplit, prm.H);
   ATTNB_CUDA(launch_pdl(attn_tc_kernel<DHP, SPLIT3>, grid, dim3(kThreads), Cfg::SMEM, s, maps[0],
-                        maps[1], maps[2], maps[3], maps[4], maps[5], prm));
+                        maps[1], maps[2], maps[3], maps[4], maps[5], maps[6], prm));
+}
+
+int max_merge(int dhp, bool split3) {
+  switch (dhp) {
+    case 32: return split3 ? AttnCfg<32, true>::MAX_MERGE : AttnCfg<32, false>::MAX_MERGE;
+    case 64: return split3 ? AttnCfg<64, true>::MAX_MERGE : AttnCfg<64, false>::MAX_MERGE;
+    case 96: return split3 ? AttnCfg<96, true>::MAX_MERGE : AttnCfg<96, false>::MAX_MERGE;
+    default: return split3 ? AttnCfg<128, true>::MAX_MERGE : AttnCfg<128, false>::MAX_MERGE;
+  }
 }
 
 template <bool SPLIT3>
@@ -478,6 +547,8 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
   const int pairs = H * p.qtiles;
   int ns = 1;
   if (!causal && pairs < num_sms) ns = std::min(n_kv, std::max(1, num_sms / pairs));
+  // The last CTA of a tile pulls every other split into shared memory at once.
+  ns = std::min(ns, 1 + max_merge(p.dhp, p.split3));
   p.tiles_per_split = (n_kv + ns - 1) / ns;
   p.nsplit = (n_kv + p.tiles_per_split - 1) / p.tiles_per_split;
   size_t off = 0;
@@ -521,7 +592,7 @@ void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View
       {K.data, K.sH, K.sT, K.sD, p.H, p.T, p.Dh, p.T, p.dhp, false, 1.f, kh, kl},
       {V.data, V.sH, V.sT, V.sD, p.H, p.T, p.Dh, p.dhp, p.tp, true, 1.f, vh, vl}};
   pack_launch(jobs, 3, p.split3, counters, p.H * p.qtiles, num_sms, s);
-  CUtensorMap maps[6];
+  CUtensorMap maps[7];
   maps[0] = make_tmap_3d(qh, p.H, p.L, p.dhp, p.dhp, (uint64_t)p.L * p.dhp, BM, BK);
   maps[2] = make_tmap_3d(kh, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BN, BK);
   maps[4] = make_tmap_3d(vh, p.H, p.dhp, p.tp, p.tp, (uint64_t)p.dhp * p.tp, p.dhp, BK);
@@ -534,6 +605,11 @@ void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View
     maps[3] = maps[2];
     maps[5] = maps[4];
   }
+  // The output leaves through TMA stores when its view allows a tensor map
+  // (unit column stride, 16-byte aligned base and row / head pitches).
+  const bool o_tma = O.sD == 1 && (reinterpret_cast<uintptr_t>(O.data) & 15u) == 0 &&
+                     (O.sT % 4) == 0 && (O.sH % 4) == 0 && O.sT > 0 && O.sH > 0;
+  maps[6] = o_tma ? make_tmap_3d(O.data, p.H, p.L, p.Dh, O.sT, O.sH, BM, 32) : maps[0];
   AttnParams prm{};
   prm.L = p.L;
   prm.T = p.T;
@@ -549,6 +625,7 @@ void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View
   prm.part_o = p.nsplit > 1 ? reinterpret_cast<float*>(w + p.off_po) : nullptr;
   prm.part_ml = p.nsplit > 1 ? reinterpret_cast<float2*>(w + p.off_pml) : nullptr;
   prm.counters = counters;
+  prm.o_tma = o_tma ? 1 : 0;
   prm.qtiles = p.qtiles;
   prm.status = status;
   ProfScope prof("attn_tc", s);

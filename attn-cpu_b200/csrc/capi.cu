@@ -226,6 +226,14 @@ const char* attnb_version(void) { return "attnb 0.1 sm_100a"; }
 
 int attnb_profile_enable(int on) { return profile_enable(on); }
 
+int attnb_selftest_wait_timeout(int limit_us, void* stream) {
+  return guarded([&] {
+    if (limit_us <= 0 || limit_us > 10000000)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "limit_us must be in (0, 1e7]");
+    selftest_wait_timeout(current_ctx(), limit_us, as_stream(stream));
+  });
+}
+
 int attnb_profile_read(const char* kernel, double* total_ms, int* launches) {
   return profile_read(kernel, total_ms, launches);
 }

@@ -1,6 +1,8 @@
 // runtime.cu -- host runtime of libattnb (see runtime.h).
 #include "runtime.h"
 
+#include "common.cuh"
+
 #include <cstdlib>
 #include <cstring>
 #include <atomic>
@@ -200,6 +202,25 @@ int profile_read(const char* kernel, double* total_ms, int* launches) {
   if (total_ms) *total_ms = ms;
   if (launches) *launches = n;
   return ATTNB_OK;
+}
+
+// Self-test of the bounded-wait machinery: one thread waits on an mbarrier
+// that nothing arrives on; after `limit_ns` it raises the status word and the
+// kernel returns normally (the context stays usable).
+__global__ void wait_timeout_selftest_kernel(int* status, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    mbar_init(smem_addr(&bar), 1);
+    fence_barrier_init();
+    mbar_wait_limit(smem_addr(&bar), 0, &abort_flag, status, limit_ns);
+  }
+}
+
+void selftest_wait_timeout(DeviceCtx& c, int limit_us, cudaStream_t s) {
+  wait_timeout_selftest_kernel<<<1, 32, 0, s>>>(c.status, (uint64_t)limit_us * 1000ull);
+  ATTNB_CUDA(cudaGetLastError());
 }
 
 int consume_status(DeviceCtx& c, cudaStream_t stream) {

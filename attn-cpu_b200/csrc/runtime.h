@@ -83,6 +83,9 @@ class ProfScope {
   cudaEvent_t a_ = nullptr, b_ = nullptr;
 };
 
+// Launches a kernel whose bounded wait expires after limit_us (see attnb.h).
+void selftest_wait_timeout(DeviceCtx& c, int limit_us, cudaStream_t s);
+
 // Reads and clears the device status word of ctx (synchronises `stream`).
 int consume_status(DeviceCtx& c, cudaStream_t stream);
 

@@ -41,22 +41,30 @@ __device__ __forceinline__ void split_value(float x, bool split3, float& hi, flo
   lo = split3 ? (x - hi) : 0.f;
 }
 
-// One warp per output row; lanes walk the row four columns at a time, with
-// 16-byte loads when the source row is contiguous and aligned.
+// Rows are spread over the lanes of a warp: `lpr` lanes per row (32 for long
+// rows, fewer for short ones so no lane idles), each lane four columns at a
+// time, with 16-byte loads when the source row is contiguous and aligned.
+__device__ __forceinline__ int lanes_per_row(int cp4) {
+  return cp4 >= 32 ? 32 : cp4 >= 16 ? 16 : cp4 >= 8 ? 8 : 4;
+}
+
 __device__ void pack_rows(const PackJob& j, bool split3, int lb, int nb) {
   constexpr int kWarps = kThreads / 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int cp4 = j.cols_out >> 2;
+  const int lpr = lanes_per_row(cp4), rpw = 32 / lpr;
+  const int sub = lane / lpr, sl = lane % lpr;
   const int64_t nrows = (int64_t)j.H * j.R;
   const bool vec = j.sC == 1 && (j.sR & 3) == 0 && (j.sH & 3) == 0 &&
                    (reinterpret_cast<uintptr_t>(j.src) & 15u) == 0;
-  for (int64_t hr = (int64_t)lb * kWarps + warp; hr < nrows; hr += (int64_t)nb * kWarps) {
+  for (int64_t hr = ((int64_t)lb * kWarps + warp) * rpw + sub; hr < nrows;
+       hr += (int64_t)nb * kWarps * rpw) {
     const int h = static_cast<int>(hr / j.R), r = static_cast<int>(hr % j.R);
     const float* s = j.src + h * j.sH + r * j.sR;
     float4* oh = reinterpret_cast<float4*>(j.hi + hr * j.cols_out);
     float4* ol = split3 ? reinterpret_cast<float4*>(j.lo + hr * j.cols_out) : nullptr;
 #pragma unroll 4
-    for (int c4 = lane; c4 < cp4; c4 += 32) {
+    for (int c4 = sl; c4 < cp4; c4 += lpr) {
       const int c = c4 * 4;
       float x[4];
       if (vec && c + 3 < j.C) {
@@ -144,7 +152,10 @@ void pack_launch(const PackJob* jobs, int njobs, bool split3, unsigned* zero, in
     if (j.transpose) {
       blocks = (int64_t)j.H * ((j.rows_out + 31) / 32) * ((j.cols_out + 31) / 32);
     } else {
-      blocks = ((int64_t)j.H * j.R + kThreads / 32 - 1) / (kThreads / 32);  // warp per row
+      const int cp4 = j.cols_out / 4;
+      const int rpw = 32 / (cp4 >= 32 ? 32 : cp4 >= 16 ? 16 : cp4 >= 8 ? 8 : 4);
+      const int64_t rows_per_block = (int64_t)(kThreads / 32) * rpw;
+      blocks = ((int64_t)j.H * j.R + rows_per_block - 1) / rows_per_block;
     }
     blocks = std::max<int64_t>(1, std::min<int64_t>(blocks, (int64_t)num_sms * 8));
     total += static_cast<int>(blocks);

@@ -75,6 +75,12 @@ ATTNB_API const char* attnb_version(void);
 /* Device status word of `stream`'s device: ATTNB_OK or ATTNB_ERR_DEVICE_TIMEOUT
  * (and clears it).  Synchronises the stream. */
 ATTNB_API int attnb_stream_status(void* stream);
+/* Self-test of the failure path (no counterpart in the reference): enqueues a
+ * kernel whose bounded wait on a barrier that nothing arrives on expires after
+ * limit_us microseconds (0 < limit_us <= 1e7).  The kernel then returns
+ * normally, so a following attnb_stream_status() reports
+ * ATTNB_ERR_DEVICE_TIMEOUT and the context stays usable. */
+ATTNB_API int attnb_selftest_wait_timeout(int limit_us, void* stream);
 
 /* Kernel timing for measurements (no counterpart in the reference).  While
  * enabled, every call records a CUDA event pair around its dominant kernel on
