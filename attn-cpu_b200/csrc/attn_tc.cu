@@ -23,7 +23,10 @@
 //
 // Operands arrive pre-packed by split.cu: Q scaled by log2(e)/sqrt(Dh), head
 // size zero-padded to a multiple of 32, V transposed per head (K-major for the
-// PV product), each split into tf32 hi + fp32 lo for 3xTF32.
+// PV product), each split into tf32 hi + fp32 lo for 3xTF32.  When every CTA
+// holds a single key tile and dhp <= 64 (short sequences, where the packing
+// launch would cost as much as the attention), four extra warps do that
+// conversion from the raw fp32 tensors straight into shared memory instead.
 #include <algorithm>
 #include <atomic>
 #include <cmath>
@@ -39,6 +42,7 @@ constexpr int BM = 128;        // query rows per CTA
 constexpr int BN = 128;        // keys per KV tile
 constexpr int BK = 32;         // fp32 elements per 128-byte swizzle row
 constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
+constexpr int kThreadsFused = 320;  // + warps 6-9 converting raw fp32 operands
 constexpr float kLog2e = 1.4426950408889634f;
 
 template <int DHP, bool SPLIT3>
@@ -57,6 +61,8 @@ struct AttnCfg {
   static constexpr int V_STAGES = V_STAGES_FIT < 4 ? V_STAGES_FIT : 4;
   static constexpr int RING_BYTES = S_STAGES * S_STAGE + V_STAGES * V_STAGE;
   static constexpr int SMEM = RING_BYTES + 1024;
+  // Fused form: raw V rows of the tile's key slices staged past the rings.
+  static constexpr int SMEM_FUSED = RING_BYTES + (BN / BK) * VBOX + 1024;
   // Split merge: another split's partial tile ([DHP][128] floats) and its
   // (m, l) row pairs, bulk-copied into the idle rings.
   static constexpr int PART_TILE = DHP * BM * 4;
@@ -107,26 +113,44 @@ struct AttnParams {
   int o_tma;  // the output tile leaves through the tmO tensor map
   float* O;
   int64_t osH, osT, osD;
+  // Raw operands for the fused form (the kernel splits them itself).
+  const float* q;
+  const float* k;
+  const float* v;
+  int64_t qsH, qsT, qsD, ksH, ksT, ksD, vsH, vsT, vsD;
+  float qscale;
   float* part_o;       // [nsplit][H][qtiles][DHP][128] (nsplit > 1)
   float2* part_ml;     // [nsplit][H][qtiles][128]
-  unsigned* counters;  // [H, qtiles] finished splits, cleared by the pack kernel
+  unsigned* counters;  // [H * qtiles] arrival tickets, zero between calls
   int* status;
 };
 
-template <int DHP, bool SPLIT3>
-__global__ void __launch_bounds__(kThreads, 1)
+__device__ __forceinline__ void split4(float4 x, float s, float4& hi, float4& lo) {
+  hi = make_float4(tf32_round(x.x * s), tf32_round(x.y * s), tf32_round(x.z * s),
+                   tf32_round(x.w * s));
+  lo = make_float4(x.x * s - hi.x, x.y * s - hi.y, x.z * s - hi.z, x.w * s - hi.w);
+}
+
+// FUSED: every CTA owns one key tile; warps 6-9 read the raw fp32 Q, K, V
+// rows, split them and write the swizzled shared-memory tiles themselves (no
+// packing pass, no TMA loads).  Otherwise warp 0 streams pre-packed tiles.
+template <int DHP, bool SPLIT3, bool FUSED>
+__global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
                    const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
                    const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
                    const __grid_constant__ CUtensorMap tmO, const AttnParams p) {
   using Cfg = AttnCfg<DHP, SPLIT3>;
   constexpr int SST = Cfg::S_STAGES, VST = Cfg::V_STAGES;
+  static_assert(!FUSED || (Cfg::NKB <= SST && BN / BK <= VST && Cfg::SMEM_FUSED <= 227 * 1024),
+                "fused form: one stage per slice of the single key tile");
   constexpr uint32_t IDESC_S = idesc_tf32(BM, BN);
   constexpr uint32_t IDESC_PV = idesc_tf32(BM, DHP);
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t sfull[SST], sempty[SST], vfull[VST], vempty[VST];
   __shared__ __align__(8) uint64_t s_bar, p_bar, pv_bar, final_bar, merge_bar;
+  __shared__ __align__(8) uint64_t rbar[FUSED ? 8 : 1];  // fused: raw Q/K (per slice), V slices
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   __shared__ int softmax_failed;  // any softmax thread saw a wait fail
@@ -149,12 +173,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     abort_flag = 0;
     softmax_failed = 0;
+    // Full barriers: one TMA arrival with a byte count, or one arrival per
+    // converter warp in the fused form (whose stages are each filled once).
     for (int i = 0; i < SST; ++i) {
-      mbar_init(smem_addr(&sfull[i]), 1);
+      mbar_init(smem_addr(&sfull[i]), FUSED ? 4 : 1);
       mbar_init(smem_addr(&sempty[i]), 1);
     }
     for (int i = 0; i < VST; ++i) {
-      mbar_init(smem_addr(&vfull[i]), 1);
+      mbar_init(smem_addr(&vfull[i]), FUSED ? 4 : 1);
       mbar_init(smem_addr(&vempty[i]), 1);
     }
     mbar_init(smem_addr(&s_bar), 1);
@@ -162,6 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_addr(&pv_bar), 1);
     mbar_init(smem_addr(&final_bar), 1);
     mbar_init(smem_addr(&merge_bar), 1);
+    if (FUSED)
+      for (int i = 0; i < 8; ++i) mbar_init(smem_addr(&rbar[i]), 1);
     fence_barrier_init();
   }
   if (warp == 1) {
@@ -173,10 +201,32 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
   volatile int* abort_p = &abort_flag;
-  grid_dep_wait();  // packed operands and cleared counters come from the pack kernel
+  grid_dep_wait();  // packed operands (or, fused, the raw ones) come from earlier kernels
 
   if (warp == 0) {
-    if (lane == 0) {
+    if (FUSED && lane == 0 && j0 < j1) {
+      // ----------------------------------------------- raw loads (fused form)
+      // The only key tile's Q/K slices into the S stages' hi slots, its V
+      // rows (32 keys x 32 columns per box) into the staging area.
+      const int j = j0;
+      const int nvb = min(BN / BK, (p.T - j * BN + BK - 1) / BK);
+      for (int kb = 0; kb < Cfg::NKB; ++kb) {
+        const uint32_t rb = smem_addr(&rbar[kb]), sa = s_addr(kb);
+        mbar_arrive_expect_tx(rb, Cfg::QBOX + Cfg::KBOX);
+        tma_load_3d(sa, &tmQh, rb, kb * BK, qt * BM, h);
+        tma_load_3d(sa + Cfg::QBOX, &tmKh, rb, kb * BK, j * BN, h);
+      }
+      for (int vb = 0; vb < nvb; ++vb) {
+        const uint32_t rb = smem_addr(&rbar[Cfg::NKB + vb]);
+        const uint32_t va = base + Cfg::RING_BYTES + vb * Cfg::VBOX;
+        mbar_arrive_expect_tx(rb, Cfg::VBOX);
+        for (int bx = 0; bx < DHP / 32; ++bx)
+          tma_load_3d(va + bx * 4096, &tmVh, rb, bx * 32, j * BN + vb * BK, h);
+      }
+      // Every copy lands before the CTA can exit (they are never cancelled).
+      for (int i = 0; i < Cfg::NKB + nvb; ++i) drain_wait(smem_addr(&rbar[i]), 0, p.status);
+    }
+    if (!FUSED && lane == 0) {
       // ------------------------------------------------------------ producer
       tma_prefetch_desc(&tmQh);
       tma_prefetch_desc(&tmKh);
@@ -290,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(smem_addr(&final_bar));
       drain_wait(smem_addr(&final_bar), 0, p.status);
     }
-  } else {
+  } else if (warp < 6) {
     // ----------------------------------------------------- softmax / output
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;
@@ -392,7 +442,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       named_bar_sync(1, 128);
       __shared__ int s_last;
       unsigned* cnt = p.counters + tile_id;
-      if (r == 0) s_last = (atomicAdd(cnt, 1u) == (unsigned)(p.nsplit - 1));
+      // The ticket wraps to 0 on the last arrival, ready for the next call.
+      if (r == 0) s_last = (atomicInc(cnt, (unsigned)(p.nsplit - 1)) == (unsigned)(p.nsplit - 1));
       named_bar_sync(1, 128);
       if (s_last) {
         // Fetch every other split's partial tile and (m, l) pairs at once.
@@ -429,7 +480,6 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int d = 0; d < DHP; ++d) o[d] = fmaf(o[d], a, t[d * BM] * b2);
             m = m_new;
           }
-          if (r == 0) *cnt = 0u;  // cleared again for the next call
           write_out = true;
         }
         // Copies that never landed (only after an abort) finish before exit.
@@ -479,6 +529,66 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
+  } else if (FUSED) {
+    // ---------------------------------------------------- operand converters
+    // Raw fp32 slices land by TMA: Q and K straight into their hi slots, V
+    // rows into a staging area.  Each is split in place (Q also scaled) and V
+    // transposed into its K-major V^T slots, then handed to the MMA warp.
+    const int ct = threadIdx.x - 192;  // 0..127
+    const int cw = ct >> 5;            // converter warp 0..3
+    uint8_t* sm = smem_raw + (base - smem_addr(smem_raw));
+    bool ok = j0 < j1;
+    for (int kb = 0; ok && kb < Cfg::NKB; ++kb) {
+      if (!mbar_wait(smem_addr(&rbar[kb]), 0, abort_p, p.status)) {
+        ok = false;
+        break;
+      }
+      uint8_t* st = sm + kb * Cfg::S_STAGE;
+#pragma unroll 4
+      for (int i = ct; i < Cfg::QBOX / 16; i += 128) {
+        float4 hi, lo;
+        float4* qv = reinterpret_cast<float4*>(st + i * 16);
+        float4* kv = reinterpret_cast<float4*>(st + Cfg::QBOX + i * 16);
+        split4(*qv, p.qscale, hi, lo);
+        *qv = hi;
+        if (SPLIT3) *reinterpret_cast<float4*>(st + Cfg::QBOX + Cfg::KBOX + i * 16) = lo;
+        split4(*kv, 1.f, hi, lo);
+        *kv = hi;
+        if (SPLIT3) *reinterpret_cast<float4*>(st + 2 * Cfg::QBOX + Cfg::KBOX + i * 16) = lo;
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&sfull[kb]));
+    }
+    // V: staging slice vb holds keys vb*32.. as DHP/32 boxes of [32 keys x 32
+    // columns] (128-byte swizzle).  Lane = key: a 16-byte read of four
+    // columns of its row, four 4-byte writes down the V^T columns.
+    const int nvb = ok ? min(BN / BK, (p.T - j0 * BN + BK - 1) / BK) : 0;
+    for (int vb = 0; vb < nvb; ++vb) {
+      if (!mbar_wait(smem_addr(&rbar[Cfg::NKB + vb]), 0, abort_p, p.status)) break;
+      const uint8_t* raw = sm + Cfg::RING_BYTES + vb * Cfg::VBOX;
+      uint8_t* st = sm + SST * Cfg::S_STAGE + vb * Cfg::V_STAGE;
+#pragma unroll
+      for (int g = cw; g < DHP / 4; g += 4) {
+        const int bx = g >> 3, c = g & 7;
+        const float4 x = *reinterpret_cast<const float4*>(raw + bx * 4096 + lane * 128 +
+                                                          ((c ^ (lane & 7)) << 4));
+        float4 hi, lo;
+        split4(x, 1.f, hi, lo);
+        const float hv[4] = {hi.x, hi.y, hi.z, hi.w};
+        const float lv[4] = {lo.x, lo.y, lo.z, lo.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int d = g * 4 + i;
+          const uint32_t off = d * 128 + (((lane >> 2) ^ (d & 7)) << 4) + (lane & 3) * 4;
+          *reinterpret_cast<float*>(st + off) = hv[i];
+          if (SPLIT3) *reinterpret_cast<float*>(st + Cfg::VBOX + off) = lv[i];
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_addr(&vfull[vb]));
+    }
   }
 
   tc_fence_before();
@@ -490,7 +600,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <int DHP, bool SPLIT3>
+template <int DHP, bool SPLIT3, bool FUSED>
 void launch_attn(const CUtensorMap* maps, const AttnParams& prm, int qtiles, cudaStream_t s) {
   using Cfg = AttnCfg<DHP, SPLIT3>;
   static std::atomic<uint64_t> configured{0};
@@ -498,13 +608,16 @@ void launch_attn(const CUtensorMap* maps, const AttnParams& prm, int qtiles, cud
   ATTNB_CUDA(cudaGetDevice(&dev));
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
-    ATTNB_CUDA(cudaFuncSetAttribute(attn_tc_kernel<DHP, SPLIT3>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    ATTNB_CUDA(cudaFuncSetAttribute(attn_tc_kernel<DHP, SPLIT3, FUSED>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                    FUSED ? Cfg::SMEM_FUSED : Cfg::SMEM));
     configured.fetch_or(bit);
   }
+  constexpr int smem = FUSED ? Cfg::SMEM_FUSED : Cfg::SMEM;
   const dim3 grid(qtiles, prm.nsplit, prm.H);
-  ATTNB_CUDA(launch_pdl(attn_tc_kernel<DHP, SPLIT3>, grid, dim3(kThreads), Cfg::SMEM, s, maps[0],
-                        maps[1], maps[2], maps[3], maps[4], maps[5], maps[6], prm));
+  ATTNB_CUDA(launch_pdl(attn_tc_kernel<DHP, SPLIT3, FUSED>, grid,
+                        dim3(FUSED ? kThreadsFused : kThreads), smem, s, maps[0], maps[1],
+                        maps[2], maps[3], maps[4], maps[5], maps[6], prm));
 }
 
 int max_merge(int dhp, bool split3) {
@@ -517,13 +630,21 @@ int max_merge(int dhp, bool split3) {
 }
 
 template <bool SPLIT3>
-void dispatch_dhp(int dhp, const CUtensorMap* maps, const AttnParams& prm, int qtiles,
-                  cudaStream_t s) {
+void dispatch_dhp(int dhp, bool fused, const CUtensorMap* maps, const AttnParams& prm,
+                  int qtiles, cudaStream_t s) {
+  if (fused) {
+    switch (dhp) {
+      case 32: launch_attn<32, SPLIT3, true>(maps, prm, qtiles, s); break;
+      case 64: launch_attn<64, SPLIT3, true>(maps, prm, qtiles, s); break;
+      default: fail(ATTNB_ERR_RUNTIME, "internal: fused form needs dhp <= 64");
+    }
+    return;
+  }
   switch (dhp) {
-    case 32: launch_attn<32, SPLIT3>(maps, prm, qtiles, s); break;
-    case 64: launch_attn<64, SPLIT3>(maps, prm, qtiles, s); break;
-    case 96: launch_attn<96, SPLIT3>(maps, prm, qtiles, s); break;
-    case 128: launch_attn<128, SPLIT3>(maps, prm, qtiles, s); break;
+    case 32: launch_attn<32, SPLIT3, false>(maps, prm, qtiles, s); break;
+    case 64: launch_attn<64, SPLIT3, false>(maps, prm, qtiles, s); break;
+    case 96: launch_attn<96, SPLIT3, false>(maps, prm, qtiles, s); break;
+    case 128: launch_attn<128, SPLIT3, false>(maps, prm, qtiles, s); break;
     default: fail(ATTNB_ERR_RUNTIME, "internal: unsupported padded head size");
   }
 }
@@ -546,11 +667,13 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
   // Split the key range when (head, query tile) pairs cannot fill the GPU.
   const int pairs = H * p.qtiles;
   int ns = 1;
-  if (!causal && pairs < num_sms) ns = std::min(n_kv, std::max(1, num_sms / pairs));
+  if (!causal && pairs < num_sms && pairs <= kMergeCounters)
+    ns = std::min(n_kv, std::max(1, num_sms / pairs));
   // The last CTA of a tile pulls every other split into shared memory at once.
   ns = std::min(ns, 1 + max_merge(p.dhp, p.split3));
   p.tiles_per_split = (n_kv + ns - 1) / ns;
   p.nsplit = (n_kv + p.tiles_per_split - 1) / p.tiles_per_split;
+  p.fusable = p.tiles_per_split == 1 && p.dhp <= 64;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -560,56 +683,72 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
   const int parts = p.split3 ? 2 : 1;
   const size_t q = (size_t)H * L * p.dhp * 4, k = (size_t)H * T * p.dhp * 4,
                v = (size_t)H * p.dhp * p.tp * 4;
+  // Packed copies (unused when the call takes the fused form; small then).
   p.off_q = take(q * parts);
   p.off_k = take(k * parts);
   p.off_v = take(v * parts);
   const size_t tile_rows = (size_t)p.nsplit * H * p.qtiles * BM;
   p.off_po = p.nsplit > 1 ? take(tile_rows * p.dhp * 4) : 0;
   p.off_pml = p.nsplit > 1 ? take(tile_rows * 8) : 0;
-  p.off_cnt = p.nsplit > 1 ? take((size_t)H * p.qtiles * sizeof(unsigned)) : 0;
   p.ws_bytes = off;
   return p;
 }
 
 void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View3& V,
-                 const MView3& O, bool causal, void* ws, int* status, int num_sms,
-                 cudaStream_t s) {
+                 const MView3& O, bool causal, void* ws, unsigned* counters, int* status,
+                 int num_sms, cudaStream_t s) {
   char* w = static_cast<char*>(ws);
-  const size_t q = (size_t)p.H * p.L * p.dhp, k = (size_t)p.H * p.T * p.dhp,
-               v = (size_t)p.H * p.dhp * p.tp;
-  float* qh = reinterpret_cast<float*>(w + p.off_q);
-  float* kh = reinterpret_cast<float*>(w + p.off_k);
-  float* vh = reinterpret_cast<float*>(w + p.off_v);
-  float* ql = p.split3 ? qh + q : nullptr;
-  float* kl = p.split3 ? kh + k : nullptr;
-  float* vl = p.split3 ? vh + v : nullptr;
   const float qscale = kLog2e / std::sqrt(static_cast<float>(p.Dh));
-  unsigned* counters = p.nsplit > 1 ? reinterpret_cast<unsigned*>(w + p.off_cnt) : nullptr;
-  // Q (scaled by log2(e)/sqrt(Dh)) and K as [H, rows, dhp]; V transposed to
-  // [H, dhp, tp]; all in one launch, which also clears the merge counters.
-  const PackJob jobs[3] = {
-      {Q.data, Q.sH, Q.sT, Q.sD, p.H, p.L, p.Dh, p.L, p.dhp, false, qscale, qh, ql},
-      {K.data, K.sH, K.sT, K.sD, p.H, p.T, p.Dh, p.T, p.dhp, false, 1.f, kh, kl},
-      {V.data, V.sH, V.sT, V.sD, p.H, p.T, p.Dh, p.dhp, p.tp, true, 1.f, vh, vl}};
-  pack_launch(jobs, 3, p.split3, counters, p.H * p.qtiles, num_sms, s);
-  CUtensorMap maps[7];
-  maps[0] = make_tmap_3d(qh, p.H, p.L, p.dhp, p.dhp, (uint64_t)p.L * p.dhp, BM, BK);
-  maps[2] = make_tmap_3d(kh, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BN, BK);
-  maps[4] = make_tmap_3d(vh, p.H, p.dhp, p.tp, p.tp, (uint64_t)p.dhp * p.tp, p.dhp, BK);
-  if (p.split3) {
-    maps[1] = make_tmap_3d(ql, p.H, p.L, p.dhp, p.dhp, (uint64_t)p.L * p.dhp, BM, BK);
-    maps[3] = make_tmap_3d(kl, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BN, BK);
-    maps[5] = make_tmap_3d(vl, p.H, p.dhp, p.tp, p.tp, (uint64_t)p.dhp * p.tp, p.dhp, BK);
-  } else {
+  CUtensorMap maps[7] = {};
+  // Fused form: the raw views are read by TMA, so each needs a unit column
+  // stride and 16-byte aligned base, row and head pitches.
+  auto tma_view = [](const View3& x) {
+    return x.sD == 1 && (reinterpret_cast<uintptr_t>(x.data) & 15u) == 0 && x.sT > 0 &&
+           x.sT % 4 == 0 && (x.H == 1 || (x.sH > 0 && x.sH % 4 == 0));
+  };
+  const bool fused = p.fusable && tma_view(Q) && tma_view(K) && tma_view(V);
+  if (fused) {
+    auto pitch = [](const View3& x, int rows) { return x.H == 1 ? (int64_t)rows * x.sT : x.sH; };
+    maps[0] = make_tmap_3d(Q.data, p.H, p.L, p.Dh, Q.sT, pitch(Q, p.L), BM, BK);
+    maps[2] = make_tmap_3d(K.data, p.H, p.T, p.Dh, K.sT, pitch(K, p.T), BN, BK);
+    maps[4] = make_tmap_3d(V.data, p.H, p.T, p.Dh, V.sT, pitch(V, p.T), BK, 32);
     maps[1] = maps[0];
     maps[3] = maps[2];
     maps[5] = maps[4];
+  } else {
+    const size_t q = (size_t)p.H * p.L * p.dhp, k = (size_t)p.H * p.T * p.dhp,
+                 v = (size_t)p.H * p.dhp * p.tp;
+    float* qh = reinterpret_cast<float*>(w + p.off_q);
+    float* kh = reinterpret_cast<float*>(w + p.off_k);
+    float* vh = reinterpret_cast<float*>(w + p.off_v);
+    float* ql = p.split3 ? qh + q : nullptr;
+    float* kl = p.split3 ? kh + k : nullptr;
+    float* vl = p.split3 ? vh + v : nullptr;
+    // Q (scaled by log2(e)/sqrt(Dh)) and K as [H, rows, dhp]; V transposed to
+    // [H, dhp, tp]; all in one launch.
+    const PackJob jobs[3] = {
+        {Q.data, Q.sH, Q.sT, Q.sD, p.H, p.L, p.Dh, p.L, p.dhp, false, qscale, qh, ql},
+        {K.data, K.sH, K.sT, K.sD, p.H, p.T, p.Dh, p.T, p.dhp, false, 1.f, kh, kl},
+        {V.data, V.sH, V.sT, V.sD, p.H, p.T, p.Dh, p.dhp, p.tp, true, 1.f, vh, vl}};
+    pack_launch(jobs, 3, p.split3, num_sms, s);
+    maps[0] = make_tmap_3d(qh, p.H, p.L, p.dhp, p.dhp, (uint64_t)p.L * p.dhp, BM, BK);
+    maps[2] = make_tmap_3d(kh, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BN, BK);
+    maps[4] = make_tmap_3d(vh, p.H, p.dhp, p.tp, p.tp, (uint64_t)p.dhp * p.tp, p.dhp, BK);
+    if (p.split3) {
+      maps[1] = make_tmap_3d(ql, p.H, p.L, p.dhp, p.dhp, (uint64_t)p.L * p.dhp, BM, BK);
+      maps[3] = make_tmap_3d(kl, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BN, BK);
+      maps[5] = make_tmap_3d(vl, p.H, p.dhp, p.tp, p.tp, (uint64_t)p.dhp * p.tp, p.dhp, BK);
+    } else {
+      maps[1] = maps[0];
+      maps[3] = maps[2];
+      maps[5] = maps[4];
+    }
   }
   // The output leaves through TMA stores when its view allows a tensor map
   // (unit column stride, 16-byte aligned base and row / head pitches).
   const bool o_tma = O.sD == 1 && (reinterpret_cast<uintptr_t>(O.data) & 15u) == 0 &&
                      (O.sT % 4) == 0 && (O.sH % 4) == 0 && O.sT > 0 && O.sH > 0;
-  maps[6] = o_tma ? make_tmap_3d(O.data, p.H, p.L, p.Dh, O.sT, O.sH, BM, 32) : maps[0];
+  if (o_tma) maps[6] = make_tmap_3d(O.data, p.H, p.L, p.Dh, O.sT, O.sH, BM, 32);
   AttnParams prm{};
   prm.L = p.L;
   prm.T = p.T;
@@ -618,19 +757,32 @@ void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View
   prm.causal = causal ? 1 : 0;
   prm.nsplit = p.nsplit;
   prm.tiles_per_split = p.tiles_per_split;
+  prm.qtiles = p.qtiles;
+  prm.o_tma = o_tma ? 1 : 0;
   prm.O = O.data;
   prm.osH = O.sH;
   prm.osT = O.sT;
   prm.osD = O.sD;
+  prm.q = Q.data;
+  prm.k = K.data;
+  prm.v = V.data;
+  prm.qsH = Q.sH;
+  prm.qsT = Q.sT;
+  prm.qsD = Q.sD;
+  prm.ksH = K.sH;
+  prm.ksT = K.sT;
+  prm.ksD = K.sD;
+  prm.vsH = V.sH;
+  prm.vsT = V.sT;
+  prm.vsD = V.sD;
+  prm.qscale = qscale;
   prm.part_o = p.nsplit > 1 ? reinterpret_cast<float*>(w + p.off_po) : nullptr;
   prm.part_ml = p.nsplit > 1 ? reinterpret_cast<float2*>(w + p.off_pml) : nullptr;
   prm.counters = counters;
-  prm.o_tma = o_tma ? 1 : 0;
-  prm.qtiles = p.qtiles;
   prm.status = status;
   ProfScope prof("attn_tc", s);
-  if (p.split3) dispatch_dhp<true>(p.dhp, maps, prm, p.qtiles, s);
-  else dispatch_dhp<false>(p.dhp, maps, prm, p.qtiles, s);
+  if (p.split3) dispatch_dhp<true>(p.dhp, fused, maps, prm, p.qtiles, s);
+  else dispatch_dhp<false>(p.dhp, fused, maps, prm, p.qtiles, s);
 }
 
 }  // namespace attnb

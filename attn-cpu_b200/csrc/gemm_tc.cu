@@ -423,7 +423,7 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
                      : PackJob{A, 0, lda, 1, 1, p.K, p.M, p.M, p.Kp, true, 1.f, a_hi, a_lo};
   jobs[1] = b_kmajor ? PackJob{B, 0, ldb, 1, 1, p.N, p.K, p.N, p.Kp, false, 1.f, b_hi, b_lo}
                      : PackJob{B, 0, ldb, 1, 1, p.K, p.N, p.N, p.Kp, true, 1.f, b_hi, b_lo};
-  pack_launch(jobs, 2, p.split3, nullptr, 0, num_sms, s);
+  pack_launch(jobs, 2, p.split3, num_sms, s);
   const int bn = p.split3 ? 128 : 256;
   const CUtensorMap tA_hi = make_tmap_2d(a_hi, p.M, p.Kp, p.Kp, BM, BK);
   const CUtensorMap tB_hi = make_tmap_2d(b_hi, p.N, p.Kp, p.Kp, bn, BK);

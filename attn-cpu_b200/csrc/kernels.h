@@ -45,15 +45,19 @@ void attn_block_simt_launch(const View3& Q, const View3& K, const View3& V, cons
 struct AttnTcPlan {
   int H, L, T, Dh, dhp, tp, qtiles, nsplit, tiles_per_split;
   bool split3;
-  size_t off_q, off_k, off_v, off_po, off_pml, off_cnt, ws_bytes;
+  // One key tile per CTA and dhp <= 64: when the views allow TMA reads, the
+  // kernel loads and splits the raw operands itself (no packing launch).
+  bool fusable;
+  size_t off_q, off_k, off_v, off_po, off_pml, ws_bytes;
 };
 // Head sizes the tensor-core kernel takes (padded to a multiple of 32, <= 128).
 bool attn_tc_supported(int Dh);
 AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision, int num_sms);
-// `ws` holds plan.ws_bytes bytes (packed operands and split partials).
+// `ws` holds plan.ws_bytes bytes (packed operands and split partials);
+// `counters` kMergeCounters zeroed merge tickets (left zeroed on success).
 void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View3& V,
-                 const MView3& O, bool causal, void* ws, int* status, int num_sms,
-                 cudaStream_t s);
+                 const MView3& O, bool causal, void* ws, unsigned* counters, int* status,
+                 int num_sms, cudaStream_t s);
 
 // ------------------------------------------------ operand packing (K2)
 // One packing job: a strided 3-D source src[h][r][c] (r < R, c < C), times
@@ -72,9 +76,8 @@ struct PackJob {
   float* lo;
 };
 constexpr int kMaxPackJobs = 3;
-// Packs up to kMaxPackJobs jobs in one launch and clears `nzero` counters.
-void pack_launch(const PackJob* jobs, int njobs, bool split3, unsigned* zero, int nzero,
-                 int num_sms, cudaStream_t s);
+// Packs up to kMaxPackJobs jobs in one launch.
+void pack_launch(const PackJob* jobs, int njobs, bool split3, int num_sms, cudaStream_t s);
 
 // Launches `kernel` with programmatic stream serialisation, so its prologue
 // may overlap the previous kernel on the stream; the kernel must execute

@@ -68,9 +68,15 @@ DeviceCtx& current_ctx() {
   ATTNB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   ATTNB_CUDA(cudaMalloc(&c->status, sizeof(int)));
   ATTNB_CUDA(cudaMemset(c->status, 0, sizeof(int)));
+  ATTNB_CUDA(cudaMalloc(&c->merge_counters, 2 * kMergeCounters * sizeof(unsigned)));
+  ATTNB_CUDA(cudaMemset(c->merge_counters, 0, 2 * kMergeCounters * sizeof(unsigned)));
   DeviceCtx& ref = *c;
   g_ctx.emplace(dev, std::move(c));
   return ref;
+}
+
+unsigned* merge_counters(DeviceCtx& c, cudaStream_t stream) {
+  return c.merge_counters + (stream == c.stream ? 0 : kMergeCounters);
 }
 
 void* dev_scratch(DeviceCtx& c, size_t bytes, cudaStream_t stream) {
@@ -228,6 +234,8 @@ int consume_status(DeviceCtx& c, cudaStream_t stream) {
   ATTNB_CUDA(cudaMemcpyAsync(&h, c.status, sizeof(int), cudaMemcpyDeviceToHost, stream));
   ATTNB_CUDA(cudaStreamSynchronize(stream));
   if (h) {
+    // An aborted kernel may have left merge tickets part-way.
+    ATTNB_CUDA(cudaMemsetAsync(c.merge_counters, 0, 2 * kMergeCounters * sizeof(unsigned), stream));
     ATTNB_CUDA(cudaMemsetAsync(c.status, 0, sizeof(int), stream));
     ATTNB_CUDA(cudaStreamSynchronize(stream));
     return ATTNB_ERR_DEVICE_TIMEOUT;

@@ -13,8 +13,7 @@
 // One launch packs every operand of a contraction (up to three jobs: e.g. Q,
 // K and V^T of an attention call), each job a strided 3-D source written
 // either in place ([h][r][c], columns padded) or transposed per head
-// ([h][c][r]).  It also clears the attention kernel's merge counters, and
-// releases the dependent kernel early (programmatic dependent launch) so that
+// ([h][c][r]).  It releases the dependent kernel early (programmatic dependent launch) so that
 // kernel's prologue overlaps the packing.  HBM-bound streaming pass.
 #include <algorithm>
 
@@ -32,8 +31,6 @@ struct PackArgs {
   int start[kMaxPackJobs + 1];  // first block of each job
   int njobs;
   int split3;
-  unsigned* zero;  // counters to clear (may be null)
-  int nzero;
 };
 
 __device__ __forceinline__ void split_value(float x, bool split3, float& hi, float& lo) {
@@ -124,8 +121,6 @@ __global__ void __launch_bounds__(kThreads) pack_kernel(const __grid_constant__ 
   // (griddepcontrol.wait) for this grid's writes before reading them.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const int b = blockIdx.x;
-  if (b == 0)
-    for (int i = threadIdx.x; i < a.nzero; i += kThreads) a.zero[i] = 0u;
   int j = 0;
   while (j + 1 < a.njobs && b >= a.start[j + 1]) ++j;
   const int lb = b - a.start[j], nb = a.start[j + 1] - a.start[j];
@@ -135,14 +130,11 @@ __global__ void __launch_bounds__(kThreads) pack_kernel(const __grid_constant__ 
 
 }  // namespace
 
-void pack_launch(const PackJob* jobs, int njobs, bool split3, unsigned* zero, int nzero,
-                 int num_sms, cudaStream_t s) {
+void pack_launch(const PackJob* jobs, int njobs, bool split3, int num_sms, cudaStream_t s) {
   if (njobs < 1 || njobs > kMaxPackJobs) fail(ATTNB_ERR_RUNTIME, "internal: bad pack job count");
   PackArgs a{};
   a.njobs = njobs;
   a.split3 = split3 ? 1 : 0;
-  a.zero = zero;
-  a.nzero = zero ? nzero : 0;
   int total = 0;
   for (int i = 0; i < njobs; ++i) {
     const PackJob& j = jobs[i];

@@ -58,7 +58,7 @@ WORKLOADS = {
 # one-pass ncu captures of dram__bytes_read.sum + dram__bytes_write.sum on the
 # same problem; commands and figures in profiles/.  Cold-cache captures.
 NCU_TRAFFIC = {
-    ("prefill", "3xtf32"): 6.35e6,     # attn_tc, [1,8,512,64]: packed Q/K/V hi+lo
+    ("prefill", "3xtf32"): None,       # attn_tc, [1,8,512,64]: raw Q/K/V (re-capture pending)
     ("decode", "3xtf32"): 1.0798e9,    # decode: K + V once (1.0737e9) + split partials
     ("decode", "tf32"): 1.0798e9,
     ("sgemm-large", "3xtf32"): 97.78e9,  # gemm_tc 16384^3: packed operands re-read ~24x
@@ -286,7 +286,9 @@ def setup_workload(w: str, rank: int, precision):
         e2e = lambda: attn_cpu.attn_block_dense(nQ, nK, nV, precision=precision)
         h2d = 4 * (Q.numel() + K.numel() + V.numel())
         d2h = 4 * O.numel()
-        return run, e2e, h2d, d2h, 2  # pack + attention
+        # One launch: each CTA holds one key tile and loads and splits the raw
+        # operands itself (no packing pass).
+        return run, e2e, h2d, d2h, 1
     if w == "decode":
         H, T, Dh = c["H"], c["T"], c["Dh"]
         Q = torch.randn(H, Dh, device="cuda", generator=g)

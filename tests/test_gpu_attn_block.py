@@ -66,6 +66,36 @@ def test_block_head_strided_dev(cuda):
     assert rel_err(Ov.cpu().numpy(), ref) < TOL_3XTF32
 
 
+@pytest.mark.parametrize("layout", ["head_strided", "column_strided", "unaligned"])
+@pytest.mark.parametrize("T,Dh", [(512, 64), (100, 40), (384, 17)])
+def test_block_views_single_tile_dev(cuda, layout, T, Dh):
+    """Non-causal calls whose CTAs each hold one key tile (the kernel converts
+    the raw operands itself) over views its vector loads cannot take."""
+    import torch
+    from attn_cpu import capi
+
+    H = 4
+    g = torch.Generator(device="cuda").manual_seed(T + Dh)
+    if layout == "head_strided":      # [T, 3, H, Dh] buffer, rows 3*H*Dh apart
+        qkv = torch.randn(T, 3, H, Dh, device="cuda", generator=g)
+        Q, K, V = (qkv[:, i].permute(1, 0, 2) for i in range(3))
+    elif layout == "column_strided":  # [H, Dh, T] storage: unit stride along T
+        Q, K, V = (torch.randn(H, Dh, T, device="cuda", generator=g).transpose(1, 2)
+                   for _ in range(3))
+    else:                             # contiguous but 4 bytes off a 16-byte boundary
+        flat = torch.randn(3 * H * T * Dh + 1, device="cuda", generator=g)
+        Q, K, V = (flat[1 + i * H * T * Dh:1 + (i + 1) * H * T * Dh].view(H, T, Dh)
+                   for i in range(3))
+    O = torch.empty(H, T, Dh, device="cuda")
+    host = [np.ascontiguousarray(t.cpu().numpy()) for t in (Q, K, V)]
+    ref = oracle.attn_block(*host, False)
+    for prec, tol in (("3xtf32", TOL_3XTF32), ("tf32", TOL_TF32)):
+        O.fill_(float("nan"))
+        capi.attn_block_dense_dev(Q, K, V, O, False, prec)
+        capi.stream_status()
+        assert rel_err(O.cpu().numpy(), ref) < tol, prec
+
+
 def test_mha_np_driver_runs(cuda):
     """The reference's NumPy driver (python/attn_cpu/mha_np.py) now has its binding."""
     from attn_cpu.mha_np import mha_forward_dense
