@@ -55,6 +55,11 @@ struct AttnCfg {
   // Two rings: Q+K slices for the S product, V^T slices for the PV product,
   // so all of a tile's V slices can be in flight while S and the softmax run.
   static constexpr int S_STAGE = NPART * (QBOX + KBOX);
+  // S stage: Q hi | K hi | K lo | Q lo, so that K hi and K lo form one
+  // 256-row B operand ([Qh.Kh | Qh.Kl] in a single N = 256 MMA).
+  static constexpr int OFF_KH = QBOX;
+  static constexpr int OFF_KL = QBOX + KBOX;
+  static constexpr int OFF_QL = QBOX + 2 * KBOX;
   static constexpr int S_STAGES = SPLIT3 ? 2 : 4;
   static constexpr int V_STAGE = NPART * VBOX;
   static constexpr int V_STAGES_FIT = (225 * 1024 - S_STAGES * S_STAGE) / V_STAGE;
@@ -131,9 +136,40 @@ __device__ __forceinline__ void split4(float4 x, float s, float4& hi, float4& lo
   lo = make_float4(x.x * s - hi.x, x.y * s - hi.y, x.z * s - hi.z, x.w * s - hi.w);
 }
 
-// FUSED: every CTA owns one key tile; warps 6-9 read the raw fp32 Q, K, V
-// rows, split them and write the swizzled shared-memory tiles themselves (no
-// packing pass, no TMA loads).  Otherwise warp 0 streams pre-packed tiles.
+// Fused form, S operands: waits for the raw Q and K slices of each S stage
+// (TMA-loaded into the hi slots), splits them in place (Q also scaled) and
+// releases the stage to the MMA warp.  Run by the 256 threads of warps 2-9,
+// `t` = 0..255.  Returns false when a wait gave up.
+template <int DHP, bool SPLIT3>
+__device__ __forceinline__ bool fused_split_qk(uint8_t* ring, const uint64_t* rbar,
+                                               uint64_t* sfull, int t, float qscale,
+                                               volatile int* abort_p, int* status) {
+  using Cfg = AttnCfg<DHP, SPLIT3>;
+  for (int kb = 0; kb < Cfg::NKB; ++kb) {
+    if (!mbar_wait(smem_addr(&rbar[kb]), 0, abort_p, status)) return false;
+    uint8_t* st = ring + kb * Cfg::S_STAGE;
+#pragma unroll
+    for (int i = t; i < Cfg::QBOX / 16; i += 256) {
+      float4 hi, lo;
+      float4* qv = reinterpret_cast<float4*>(st + i * 16);
+      float4* kv = reinterpret_cast<float4*>(st + Cfg::OFF_KH + i * 16);
+      split4(*qv, qscale, hi, lo);
+      *qv = hi;
+      if (SPLIT3) *reinterpret_cast<float4*>(st + Cfg::OFF_QL + i * 16) = lo;
+      split4(*kv, 1.f, hi, lo);
+      *kv = hi;
+      if (SPLIT3) *reinterpret_cast<float4*>(st + Cfg::OFF_KL + i * 16) = lo;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if ((t & 31) == 0) mbar_arrive(smem_addr(&sfull[kb]));
+  }
+  return true;
+}
+
+// FUSED: every CTA owns one key tile, loaded raw by TMA and split in shared
+// memory by warps 2-9 (Q, K) and 6-9 (V).  Otherwise warp 0 streams
+// pre-packed tiles.
 template <int DHP, bool SPLIT3, bool FUSED>
 __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
@@ -144,8 +180,16 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
   constexpr int SST = Cfg::S_STAGES, VST = Cfg::V_STAGES;
   static_assert(!FUSED || (Cfg::NKB <= SST && BN / BK <= VST && Cfg::SMEM_FUSED <= 227 * 1024),
                 "fused form: one stage per slice of the single key tile");
+  // 3xTF32 issues two MMAs per K step where three products are needed: the
+  // hi.hi and hi.lo products share one MMA of twice the width (their B
+  // operands sit next to each other in shared memory, their accumulators next
+  // to each other in TMEM), the lo.hi product takes a second one.
   constexpr uint32_t IDESC_S = idesc_tf32(BM, BN);
+  constexpr uint32_t IDESC_S2 = idesc_tf32(BM, 2 * BN);
   constexpr uint32_t IDESC_PV = idesc_tf32(BM, DHP);
+  constexpr uint32_t IDESC_PV2 = idesc_tf32(BM, 2 * DHP);
+  static_assert(Cfg::S_SMALL == Cfg::S_BIG + BN && Cfg::PV_SMALL == Cfg::PV_BIG + DHP,
+                "small accumulators follow the big ones");
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t sfull[SST], sempty[SST], vfull[VST], vempty[VST];
@@ -173,10 +217,10 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
   if (threadIdx.x == 0) {
     abort_flag = 0;
     softmax_failed = 0;
-    // Full barriers: one TMA arrival with a byte count, or one arrival per
-    // converter warp in the fused form (whose stages are each filled once).
+    // Full barriers: one TMA arrival with a byte count, or in the fused form
+    // (whose stages are each filled once) one arrival per splitting warp.
     for (int i = 0; i < SST; ++i) {
-      mbar_init(smem_addr(&sfull[i]), FUSED ? 4 : 1);
+      mbar_init(smem_addr(&sfull[i]), FUSED ? 8 : 1);
       mbar_init(smem_addr(&sempty[i]), 1);
     }
     for (int i = 0; i < VST; ++i) {
@@ -214,7 +258,7 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
         const uint32_t rb = smem_addr(&rbar[kb]), sa = s_addr(kb);
         mbar_arrive_expect_tx(rb, Cfg::QBOX + Cfg::KBOX);
         tma_load_3d(sa, &tmQh, rb, kb * BK, qt * BM, h);
-        tma_load_3d(sa + Cfg::QBOX, &tmKh, rb, kb * BK, j * BN, h);
+        tma_load_3d(sa + Cfg::OFF_KH, &tmKh, rb, kb * BK, j * BN, h);
       }
       for (int vb = 0; vb < nvb; ++vb) {
         const uint32_t rb = smem_addr(&rbar[Cfg::NKB + vb]);
@@ -243,10 +287,10 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
           const uint32_t fb = smem_addr(&sfull[rs.stage]), sa = s_addr(rs.stage);
           mbar_arrive_expect_tx(fb, Cfg::S_STAGE);
           tma_load_3d(sa, &tmQh, fb, kb * BK, qt * BM, h);
-          tma_load_3d(sa + Cfg::QBOX, &tmKh, fb, kb * BK, j * BN, h);
+          tma_load_3d(sa + Cfg::OFF_KH, &tmKh, fb, kb * BK, j * BN, h);
           if (SPLIT3) {
-            tma_load_3d(sa + Cfg::QBOX + Cfg::KBOX, &tmQl, fb, kb * BK, qt * BM, h);
-            tma_load_3d(sa + 2 * Cfg::QBOX + Cfg::KBOX, &tmKl, fb, kb * BK, j * BN, h);
+            tma_load_3d(sa + Cfg::OFF_QL, &tmQl, fb, kb * BK, qt * BM, h);
+            tma_load_3d(sa + Cfg::OFF_KL, &tmKl, fb, kb * BK, j * BN, h);
           }
           rs.note_issue();
           rs.advance();
@@ -295,13 +339,14 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
           for (int kk = 0; kk < BK / 8; ++kk) {
             const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
             const uint64_t qh = sdesc_kmajor_sw128(sa + kk * 32);
-            const uint64_t kh = sdesc_kmajor_sw128(sa + Cfg::QBOX + kk * 32);
-            mma_tf32(tmem + Cfg::S_BIG, qh, kh, IDESC_S, acc);
+            const uint64_t kh = sdesc_kmajor_sw128(sa + Cfg::OFF_KH + kk * 32);
             if (SPLIT3) {
-              const uint64_t ql = sdesc_kmajor_sw128(sa + Cfg::QBOX + Cfg::KBOX + kk * 32);
-              const uint64_t kl = sdesc_kmajor_sw128(sa + 2 * Cfg::QBOX + Cfg::KBOX + kk * 32);
-              mma_tf32(tmem + Cfg::S_SMALL, qh, kl, IDESC_S, acc);
+              // [S_BIG | S_SMALL] (+)= Qh . [Kh | Kl]^T, then S_SMALL += Ql . Kh^T.
+              const uint64_t ql = sdesc_kmajor_sw128(sa + Cfg::OFF_QL + kk * 32);
+              mma_tf32(tmem + Cfg::S_BIG, qh, kh, IDESC_S2, acc);
               mma_tf32(tmem + Cfg::S_SMALL, ql, kh, IDESC_S, 1u);
+            } else {
+              mma_tf32(tmem + Cfg::S_BIG, qh, kh, IDESC_S, acc);
             }
           }
           mma_commit(smem_addr(&sempty[rs.stage]));
@@ -324,11 +369,12 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
             const uint32_t acc = (vb | kk) != 0 ? 1u : 0u;
             const uint32_t key = vb * BK + kk * 8;
             const uint64_t vh = sdesc_kmajor_sw128(sa + kk * 32);
-            mma_tf32_ts(tmem + Cfg::PV_BIG, tmem + Cfg::S_BIG + key, vh, IDESC_PV, acc);
             if (SPLIT3) {
-              const uint64_t vl = sdesc_kmajor_sw128(sa + Cfg::VBOX + kk * 32);
-              mma_tf32_ts(tmem + Cfg::PV_SMALL, tmem + Cfg::S_BIG + key, vl, IDESC_PV, acc);
+              // V^T hi and lo rows are contiguous: one B operand of 2*DHP rows.
+              mma_tf32_ts(tmem + Cfg::PV_BIG, tmem + Cfg::S_BIG + key, vh, IDESC_PV2, acc);
               mma_tf32_ts(tmem + Cfg::PV_SMALL, tmem + Cfg::S_SMALL + key, vh, IDESC_PV, 1u);
+            } else {
+              mma_tf32_ts(tmem + Cfg::PV_BIG, tmem + Cfg::S_BIG + key, vh, IDESC_PV, acc);
             }
           }
           mma_commit(smem_addr(&vempty[rv.stage]));
@@ -351,8 +397,11 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
 #pragma unroll
     for (int d = 0; d < DHP; ++d) o[d] = 0.f;
     bool ok = true;
+    if (FUSED && j0 < j1)
+      ok = fused_split_qk<DHP, SPLIT3>(smem_raw + (base - smem_addr(smem_raw)), rbar, sfull,
+                                       threadIdx.x - 64, p.qscale, abort_p, p.status);
     int it = 0;
-    for (int j = j0; j < j1; ++j, ++it) {
+    for (int j = j0; ok && j < j1; ++j, ++it) {
       if (!mbar_wait(smem_addr(&s_bar), it & 1, abort_p, p.status)) {
         ok = false;
         break;
@@ -531,35 +580,15 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
     }
   } else if (FUSED) {
     // ---------------------------------------------------- operand converters
-    // Raw fp32 slices land by TMA: Q and K straight into their hi slots, V
-    // rows into a staging area.  Each is split in place (Q also scaled) and V
-    // transposed into its K-major V^T slots, then handed to the MMA warp.
+    // Q and K are split together with the softmax warps; V rows, staged by
+    // TMA, are split and transposed into the K-major V^T slots here.
     const int ct = threadIdx.x - 192;  // 0..127
     const int cw = ct >> 5;            // converter warp 0..3
     uint8_t* sm = smem_raw + (base - smem_addr(smem_raw));
     bool ok = j0 < j1;
-    for (int kb = 0; ok && kb < Cfg::NKB; ++kb) {
-      if (!mbar_wait(smem_addr(&rbar[kb]), 0, abort_p, p.status)) {
-        ok = false;
-        break;
-      }
-      uint8_t* st = sm + kb * Cfg::S_STAGE;
-#pragma unroll 4
-      for (int i = ct; i < Cfg::QBOX / 16; i += 128) {
-        float4 hi, lo;
-        float4* qv = reinterpret_cast<float4*>(st + i * 16);
-        float4* kv = reinterpret_cast<float4*>(st + Cfg::QBOX + i * 16);
-        split4(*qv, p.qscale, hi, lo);
-        *qv = hi;
-        if (SPLIT3) *reinterpret_cast<float4*>(st + Cfg::QBOX + Cfg::KBOX + i * 16) = lo;
-        split4(*kv, 1.f, hi, lo);
-        *kv = hi;
-        if (SPLIT3) *reinterpret_cast<float4*>(st + 2 * Cfg::QBOX + Cfg::KBOX + i * 16) = lo;
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&sfull[kb]));
-    }
+    if (ok)
+      ok = fused_split_qk<DHP, SPLIT3>(sm, rbar, sfull, threadIdx.x - 64, p.qscale, abort_p,
+                                       p.status);
     // V: staging slice vb holds keys vb*32.. as DHP/32 boxes of [32 keys x 32
     // columns] (128-byte swizzle).  Lane = key: a 16-byte read of four
     // columns of its row, four 4-byte writes down the V^T columns.

@@ -195,12 +195,15 @@ def max_over_ranks(x: float, world: int) -> float:
 
 
 class L2Flusher:
-    """Writes a buffer larger than the 126 MB L2 between timed steps."""
+    """Writes a buffer larger than the 126 MB L2 between timed steps.  At
+    512 MB the write keeps the GPU busy (~80 us) while the host enqueues the
+    step, so the step's events time the device work, not the launch path
+    (which the e2e figure includes)."""
 
     def __init__(self):
         import torch
 
-        self.buf = torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+        self.buf = torch.empty(512 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
 
     def __call__(self):
         self.buf.fill_(1.0)
