@@ -23,7 +23,7 @@ PREC = {None: -1, "default": -1, "3xtf32": 0, "tf32": 1}
 # Every symbol include/attnb.h declares.
 EXPORTED = [
     "attnb_last_error", "attnb_version", "attnb_stream_status", "attnb_selftest_wait_timeout",
-    "attnb_profile_enable", "attnb_profile_read",
+    "attnb_profile_enable", "attnb_profile_read", "attnb_host_alloc", "attnb_host_free",
     "attnb_sgemm", "attnb_gemm_jit", "attnb_sgemm_dev", "attnb_linear_dev",
     "attnb_attn_step_dense", "attnb_attn_step_dense_dev", "attnb_attn_step_dense_noalloc",
     "attnb_attn_block_dense", "attnb_attn_block_dense_dev",
@@ -62,6 +62,8 @@ def lib() -> ctypes.CDLL:
         L.attnb_profile_enable.argtypes = [i]
         L.attnb_profile_read.argtypes = [ctypes.c_char_p, ctypes.POINTER(ctypes.c_double),
                                          ctypes.POINTER(ctypes.c_int)]
+        L.attnb_host_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
+        L.attnb_host_free.argtypes = [vp]
         L.attnb_sgemm.argtypes = [vp, i, i, vp, i, vp, f, f, i]
         L.attnb_gemm_jit.argtypes = [vp, i, i, vp, i, vp, f, f, i]
         L.attnb_sgemm_dev.argtypes = [vp, i, vp, i, vp, i, i, i, i, f, f, i, vp]

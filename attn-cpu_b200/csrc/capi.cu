@@ -238,6 +238,22 @@ int attnb_profile_read(const char* kernel, double* total_ms, int* launches) {
   return profile_read(kernel, total_ms, launches);
 }
 
+int attnb_host_alloc(size_t bytes, void** ptr) {
+  return guarded([&] {
+    if (!ptr) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    *ptr = nullptr;
+    if (bytes == 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "bytes must be positive");
+    *ptr = host_pool_alloc(bytes);
+  });
+}
+
+int attnb_host_free(void* ptr) {
+  return guarded([&] {
+    if (!host_pool_free(ptr))
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "pointer was not allocated by attnb_host_alloc");
+  });
+}
+
 int attnb_stream_status(void* stream) {
   return guarded([&] {
     DeviceCtx& c = current_ctx();

@@ -120,6 +120,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   using Cfg = GemmCfg<BN, SPLIT3>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+  // 3xTF32: A_hi.[B_hi | B_lo] as one MMA of width 2*BN (B_lo follows B_hi in
+  // the stage, the small accumulator follows the big one in TMEM), then
+  // A_lo.B_hi into the small accumulator: two MMAs per K step for three
+  // products.
+  constexpr uint32_t IDESC2 = idesc_tf32(BM, 2 * BN);
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[STAGES], empty_bar[STAGES];
@@ -134,6 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto sB_hi = [&](int s) {
     return tiles_base + s * Cfg::STAGE_BYTES + (SPLIT3 ? 2 : 1) * Cfg::A_BYTES;
   };
+  static_assert(!SPLIT3 || 2 * BN <= 256, "double-width MMA: N <= 256");
   auto sB_lo = [&](int s) {
     return tiles_base + s * Cfg::STAGE_BYTES + 2 * Cfg::A_BYTES + Cfg::B_BYTES;
   };
@@ -244,12 +250,12 @@ __global__ void __launch_bounds__(kThreads, 1)
               const uint32_t acc = (kb != kb0 || kk != 0) ? 1u : 0u;
               const uint64_t a_hi = sdesc_kmajor_sw128(sA_hi(stage) + kk * 32);
               const uint64_t b_hi = sdesc_kmajor_sw128(sB_hi(stage) + kk * 32);
-              mma_tf32(d_big, a_hi, b_hi, IDESC, acc);
               if (SPLIT3) {
                 const uint64_t a_lo = sdesc_kmajor_sw128(sA_lo(stage) + kk * 32);
-                const uint64_t b_lo = sdesc_kmajor_sw128(sB_lo(stage) + kk * 32);
-                mma_tf32(d_small, a_hi, b_lo, IDESC, acc);
+                mma_tf32(d_big, a_hi, b_hi, IDESC2, acc);
                 mma_tf32(d_small, a_lo, b_hi, IDESC, 1u);
+              } else {
+                mma_tf32(d_big, a_hi, b_hi, IDESC, acc);
               }
             }
             mma_commit(smem_addr(&empty_bar[stage]));

@@ -10,8 +10,10 @@
 #include <pybind11/numpy.h>
 #include <pybind11/pybind11.h>
 
+#include <cmath>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "../../include/attnb.h"
 
@@ -25,6 +27,21 @@ void rethrow(int rc) {
   const std::string msg = attnb_last_error();
   if (rc == ATTNB_ERR_INVALID_ARGUMENT) throw std::invalid_argument(msg);
   throw std::runtime_error(msg);
+}
+
+// A new, uninitialised result array in page-locked memory from the library's
+// pool (the device-to-host copy of the result then runs by DMA at full rate
+// and touches no fresh pages), or in ordinary memory when the pool is full.
+// The block returns to the pool when the array is freed.
+py::array_t<float> result_array(std::vector<py::ssize_t> shape) {
+  size_t n = 1;
+  for (py::ssize_t d : shape) n *= (size_t)d;
+  void* p = nullptr;
+  if (n > 0 && attnb_host_alloc(n * sizeof(float), &p) == ATTNB_OK && p) {
+    py::capsule owner(p, [](void* q) { attnb_host_free(q); });
+    return py::array_t<float>(shape, static_cast<float*>(p), owner);
+  }
+  return py::array_t<float>(shape);
 }
 
 py::array_t<float> mha_block_dense_py(farray x, farray W_in, farray b_in, farray W_out,
@@ -43,7 +60,7 @@ py::array_t<float> mha_block_dense_py(farray x, farray W_in, farray b_in, farray
   if ((int)b_out.shape(0) != D) throw std::invalid_argument("b_out shape must be [D]");
   if (num_heads <= 0 || (D % num_heads) != 0)
     throw std::invalid_argument("num_heads must divide D");
-  py::array_t<float> y({T, D});
+  py::array_t<float> y = result_array({T, D});
   const float *px = x.data(), *pwi = W_in.data(), *pbi = b_in.data(), *pwo = W_out.data(),
               *pbo = b_out.data();
   float* py_ = y.mutable_data();
@@ -64,10 +81,15 @@ py::array_t<float> gemm_common(farray A, farray B, float alpha, float beta, int 
   const int M = (int)A.shape(0), K = (int)A.shape(1), KB = (int)B.shape(0),
             N = (int)B.shape(1);
   if (K != KB) throw std::invalid_argument("Inner dim mismatch: A[M,K] x B[K,N]");
-  // Zero-initialised, so beta != 0 scales zeros (the reference reads an
-  // uninitialised buffer there, src/bindings.cpp:64-71).
-  py::array_t<float> C({M, N});
-  if ((size_t)M * N) std::fill(C.mutable_data(), C.mutable_data() + (size_t)M * N, 0.f);
+  // C starts as zeros, so beta * C contributes nothing for a finite beta and
+  // the call runs with beta = 0 (C never read); a non-finite beta keeps its
+  // NaN product with explicit zeros, and K = 0 (C left untouched) returns
+  // them.  (The reference reads an uninitialised buffer there,
+  // src/bindings.cpp:64-71.)
+  py::array_t<float> C = result_array({M, N});
+  if ((size_t)M * N && (K <= 0 || !std::isfinite(beta)))
+    std::fill(C.mutable_data(), C.mutable_data() + (size_t)M * N, 0.f);
+  if (std::isfinite(beta)) beta = 0.f;
   const float *pa = A.data(), *pb = B.data();
   float* pc = C.mutable_data();
   int rc;
@@ -96,7 +118,7 @@ py::array_t<float> attn_step_dense_py(farray Q, farray K, farray V) {
                  (int64_t)K.shape(1) * K.shape(2), (int64_t)K.shape(2), 1};
   attnb_tensor v{V.data(), (int)V.shape(0), (int)V.shape(1), (int)V.shape(2),
                  (int64_t)V.shape(1) * V.shape(2), (int64_t)V.shape(2), 1};
-  py::array_t<float> O({H, Dh});
+  py::array_t<float> O = result_array({H, Dh});
   attnb_mtensor o{O.mutable_data(), H, 1, Dh, (int64_t)Dh, 0, 1};
   int rc;
   {
@@ -116,7 +138,7 @@ py::array_t<float> attn_block_dense_py(farray Q, farray K, farray V, bool causal
                  (int64_t)K.shape(1) * K.shape(2), (int64_t)K.shape(2), 1};
   attnb_tensor v{V.data(), (int)V.shape(0), (int)V.shape(1), (int)V.shape(2),
                  (int64_t)V.shape(1) * V.shape(2), (int64_t)V.shape(2), 1};
-  py::array_t<float> O({H, L, Dh});
+  py::array_t<float> O = result_array({H, L, Dh});
   attnb_mtensor o{O.mutable_data(), H, L, Dh, (int64_t)L * Dh, (int64_t)Dh, 1};
   int rc;
   {

@@ -68,6 +68,7 @@ DeviceCtx& current_ctx() {
   ATTNB_CUDA(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking));
   ATTNB_CUDA(cudaMalloc(&c->status, sizeof(int)));
   ATTNB_CUDA(cudaMemset(c->status, 0, sizeof(int)));
+  ATTNB_CUDA(cudaMallocHost(&c->status_host, sizeof(int)));
   ATTNB_CUDA(cudaMalloc(&c->merge_counters, 2 * kMergeCounters * sizeof(unsigned)));
   ATTNB_CUDA(cudaMemset(c->merge_counters, 0, 2 * kMergeCounters * sizeof(unsigned)));
   DeviceCtx& ref = *c;
@@ -231,8 +232,13 @@ void selftest_wait_timeout(DeviceCtx& c, int limit_us, cudaStream_t s) {
 
 int consume_status(DeviceCtx& c, cudaStream_t stream) {
   int h = 0;
-  ATTNB_CUDA(cudaMemcpyAsync(&h, c.status, sizeof(int), cudaMemcpyDeviceToHost, stream));
-  ATTNB_CUDA(cudaStreamSynchronize(stream));
+  {
+    std::lock_guard<std::mutex> g(c.status_mu);
+    ATTNB_CUDA(cudaMemcpyAsync(c.status_host, c.status, sizeof(int), cudaMemcpyDeviceToHost,
+                               stream));
+    ATTNB_CUDA(cudaStreamSynchronize(stream));
+    h = *c.status_host;
+  }
   if (h) {
     // An aborted kernel may have left merge tickets part-way.
     ATTNB_CUDA(cudaMemsetAsync(c.merge_counters, 0, 2 * kMergeCounters * sizeof(unsigned), stream));
@@ -241,6 +247,56 @@ int consume_status(DeviceCtx& c, cudaStream_t stream) {
     return ATTNB_ERR_DEVICE_TIMEOUT;
   }
   return ATTNB_OK;
+}
+
+// ------------------------------------------------------ pinned host pool
+namespace {
+struct HostPool {
+  std::mutex mu;
+  std::vector<void*> free_list[64];
+  std::map<void*, int> live;  // block -> size class (log2 bytes)
+  size_t held = 0;            // bytes of all blocks, live or free
+  size_t cap = 0;
+  HostPool() {
+    const char* e = std::getenv("ATTNB_PINNED_POOL_MB");
+    const long mb = e ? std::atol(e) : 1024;
+    cap = (size_t)(mb > 0 ? mb : 0) << 20;
+  }
+};
+HostPool& host_pool() {
+  static HostPool* p = new HostPool();  // never destroyed: blocks may outlive exit order
+  return *p;
+}
+}  // namespace
+
+void* host_pool_alloc(size_t bytes) {
+  int cls = 12;
+  while (((size_t)1 << cls) < bytes) ++cls;
+  if (cls >= 63) return nullptr;
+  HostPool& hp = host_pool();
+  std::lock_guard<std::mutex> g(hp.mu);
+  void* p = nullptr;
+  if (!hp.free_list[cls].empty()) {
+    p = hp.free_list[cls].back();
+    hp.free_list[cls].pop_back();
+  } else {
+    const size_t sz = (size_t)1 << cls;
+    if (hp.held + sz > hp.cap) return nullptr;
+    ATTNB_CUDA(cudaHostAlloc(&p, sz, cudaHostAllocPortable));
+    hp.held += sz;
+  }
+  hp.live.emplace(p, cls);
+  return p;
+}
+
+bool host_pool_free(void* p) {
+  HostPool& hp = host_pool();
+  std::lock_guard<std::mutex> g(hp.mu);
+  auto it = hp.live.find(p);
+  if (it == hp.live.end()) return false;
+  hp.free_list[it->second].push_back(p);
+  hp.live.erase(it);
+  return true;
 }
 
 }  // namespace attnb

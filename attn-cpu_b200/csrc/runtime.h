@@ -38,6 +38,8 @@ struct DeviceCtx {
   int num_sms = 0;
   cudaStream_t stream = nullptr;  // used by the host-pointer entry points
   int* status = nullptr;          // device status word (bit 0: wait time-out)
+  int* status_host = nullptr;     // pinned mirror the status word is read into
+  std::mutex status_mu;           // guards status_host
   std::mutex mu;                  // serialises host-pointer calls on this device
   DeviceBuffer io;                // device copies of host inputs/outputs
   DeviceBuffer scratch_host_path; // kernel scratch for host-pointer calls
@@ -99,5 +101,13 @@ void selftest_wait_timeout(DeviceCtx& c, int limit_us, cudaStream_t s);
 
 // Reads and clears the device status word of ctx (synchronises `stream`).
 int consume_status(DeviceCtx& c, cudaStream_t stream);
+
+// Page-locked host blocks for results handed to callers (attnb_host_alloc):
+// power-of-two size classes from 4 KiB, recycled on free, at most
+// ATTNB_PINNED_POOL_MB (default 1024) MiB held.  host_pool_alloc returns
+// nullptr when the cap would be exceeded.
+void* host_pool_alloc(size_t bytes);
+// Returns a block to its size class; false if `p` is not a live pool block.
+bool host_pool_free(void* p);
 
 }  // namespace attnb

@@ -23,6 +23,7 @@
 #ifndef ATTNB_H
 #define ATTNB_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #if defined(__GNUC__)
@@ -90,6 +91,16 @@ ATTNB_API int attnb_selftest_wait_timeout(int limit_us, void* stream);
  * milliseconds and launch count for `kernel`, and forgets them. */
 ATTNB_API int attnb_profile_enable(int on);
 ATTNB_API int attnb_profile_read(const char* kernel, double* total_ms, int* launches);
+
+/* Page-locked host memory for results (no counterpart in the reference).
+ * Host-pointer calls move data by DMA at full PCIe rate only to and from
+ * page-locked memory; these blocks come from a recycled pool (power-of-two
+ * size classes, at most ATTNB_PINNED_POOL_MB MiB, default 1024).  The Python
+ * module returns its result arrays in them.  attnb_host_alloc sets *ptr to
+ * NULL (and returns ATTNB_OK) when the pool is full; attnb_host_free rejects
+ * pointers it did not hand out with ATTNB_ERR_INVALID_ARGUMENT. */
+ATTNB_API int attnb_host_alloc(size_t bytes, void** ptr);
+ATTNB_API int attnb_host_free(void* ptr);
 
 /* ---------------------------------------------------------------- SGEMM */
 /* C[M,N] = alpha * A[M,K] . B[K,N] + beta * C.
