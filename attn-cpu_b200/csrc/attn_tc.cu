@@ -18,8 +18,9 @@
 //   finished PV tile into an fp32 register accumulator:
 //     O = O * 2^(m_old - m_new) + PV.
 //   Scores never leave the SM; O is normalised once at the end.  When few
-//   (head, query-tile) pairs exist, the key range is split over CTAs and a
-//   small kernel merges the partial (m, l, O).
+//   (head, query-tile) pairs exist, the key range is split over the CTAs of a
+//   thread-block cluster, which combine their (m, l, O) rows through
+//   distributed shared memory.
 //
 // Operands arrive pre-packed by split.cu: Q scaled by log2(e)/sqrt(Dh), head
 // size zero-padded to a multiple of 32, V transposed per head (K-major for the
@@ -41,9 +42,11 @@ namespace {
 constexpr int BM = 128;        // query rows per CTA
 constexpr int BN = 128;        // keys per KV tile
 constexpr int BK = 32;         // fp32 elements per 128-byte swizzle row
-constexpr int kThreads = 192;  // warp 0 TMA, warp 1 MMA, warps 2-5 softmax
-constexpr int kThreadsFused = 320;  // + warps 6-9 converting raw fp32 operands
+constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax (two groups)
 constexpr float kLog2e = 1.4426950408889634f;
+constexpr int kMaxSplits = 8;  // key splits of a query tile: one portable cluster
+// Fused form: V slices split by warp 0 (the rest by the eight softmax warps).
+constexpr int kVSlicesWarp0 = 2;
 
 template <int DHP, bool SPLIT3>
 struct AttnCfg {
@@ -68,11 +71,12 @@ struct AttnCfg {
   static constexpr int SMEM = RING_BYTES + 1024;
   // Fused form: raw V rows of the tile's key slices staged past the rings.
   static constexpr int SMEM_FUSED = RING_BYTES + (BN / BK) * VBOX + 1024;
-  // Split merge: another split's partial tile ([DHP][128] floats) and its
-  // (m, l) row pairs, bulk-copied into the idle rings.
-  static constexpr int PART_TILE = DHP * BM * 4;
-  static constexpr int PART_ML = BM * 8;
-  static constexpr int MAX_MERGE = RING_BYTES / (PART_TILE + PART_ML);
+  // Split merge: each CTA of a cluster stages its unnormalised rows in its
+  // idle rings as [O (DHP floats) | m | l | valid | spare] (OP floats, a
+  // multiple of 16 bytes) and receives the other splits' rows of its share
+  // of the tile behind them.
+  static constexpr int OP = DHP + 4;
+  static constexpr int RECV = BM * OP * 4;
   static constexpr int S_BIG = 0;
   static constexpr int S_SMALL = BN;
   static constexpr int PV_BIG = NPART * BN;
@@ -81,7 +85,7 @@ struct AttnCfg {
   static_assert(DHP % 32 == 0 && DHP <= 128, "head size padded to 32..128");
   static_assert(V_STAGES >= 2, "V ring needs two stages");
   static_assert(BM * (DHP + 1) * 4 <= S_STAGES * S_STAGE, "output staging fits the S ring");
-  static_assert(MAX_MERGE >= 1, "merge buffers fit the rings");
+  static_assert(RECV + BM * OP * 4 <= RING_BYTES, "merge staging fits the rings");
   static_assert(PV_BIG + NPART * DHP <= TMEM_COLS, "TMEM budget");
 };
 
@@ -124,9 +128,6 @@ struct AttnParams {
   const float* v;
   int64_t qsH, qsT, qsD, ksH, ksT, ksD, vsH, vsT, vsD;
   float qscale;
-  float* part_o;       // [nsplit][H][qtiles][DHP][128] (nsplit > 1)
-  float2* part_ml;     // [nsplit][H][qtiles][128]
-  unsigned* counters;  // [H * qtiles] arrival tickets, zero between calls
   int* status;
 };
 
@@ -145,8 +146,14 @@ __device__ __forceinline__ bool fused_split_qk(uint8_t* ring, const uint64_t* rb
                                                uint64_t* sfull, int t, float qscale,
                                                volatile int* abort_p, int* status) {
   using Cfg = AttnCfg<DHP, SPLIT3>;
+  bool good = true;
   for (int kb = 0; kb < Cfg::NKB; ++kb) {
-    if (!mbar_wait(smem_addr(&rbar[kb]), 0, abort_p, status)) return false;
+    // Lanes of a warp pass the same __syncwarp whatever their waits returned.
+    if (good && !mbar_wait(smem_addr(&rbar[kb]), 0, abort_p, status)) good = false;
+    if (!good) {
+      __syncwarp();
+      continue;
+    }
     uint8_t* st = ring + kb * Cfg::S_STAGE;
 #pragma unroll
     for (int i = t; i < Cfg::QBOX / 16; i += 256) {
@@ -164,14 +171,131 @@ __device__ __forceinline__ bool fused_split_qk(uint8_t* ring, const uint64_t* rb
     __syncwarp();
     if ((t & 31) == 0) mbar_arrive(smem_addr(&sfull[kb]));
   }
-  return true;
+  return good;
+}
+
+// Fused form, PV operand: splits and transposes raw V slice `vb` (32 keys,
+// staged by TMA as DHP/32 boxes of [32 keys x 32 columns], 128-byte swizzle)
+// into the K-major V^T slots of V stage vb.  Lane = key: a 16-byte read of
+// four columns of its row, four 4-byte writes down the V^T columns; the
+// calling warp takes column groups gi = gi0, gi0 + gstep, ...
+template <int DHP, bool SPLIT3>
+__device__ __forceinline__ void fused_split_v_slice(uint8_t* ring, int vb, int lane, int gi0,
+                                                    int gstep) {
+  using Cfg = AttnCfg<DHP, SPLIT3>;
+  const uint8_t* raw = ring + Cfg::RING_BYTES + vb * Cfg::VBOX;
+  uint8_t* st = ring + Cfg::S_STAGES * Cfg::S_STAGE + vb * Cfg::V_STAGE;
+#pragma unroll 4
+  for (int gi = gi0; gi < DHP / 4; gi += gstep) {
+    const int bx = gi >> 3, c = gi & 7;
+    const float4 x =
+        *reinterpret_cast<const float4*>(raw + bx * 4096 + lane * 128 + ((c ^ (lane & 7)) << 4));
+    float4 hi, lo;
+    split4(x, 1.f, hi, lo);
+    const float hv[4] = {hi.x, hi.y, hi.z, hi.w};
+    const float lv[4] = {lo.x, lo.y, lo.z, lo.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int d = gi * 4 + i;
+      const uint32_t off = d * 128 + (((lane >> 2) ^ (d & 7)) << 4) + (lane & 3) * 4;
+      *reinterpret_cast<float*>(st + off) = hv[i];
+      if (SPLIT3) *reinterpret_cast<float*>(st + Cfg::VBOX + off) = lv[i];
+    }
+  }
+  fence_proxy_async_smem();
+}
+
+// Final rows of a split tile.  CTA rank q of the cluster owns rows
+// [q * rows_per, ...), rows_per = ceil(128 / nsplit): every CTA bulk-copies
+// the staged rows each peer owns into that peer's receive area (one copy per
+// peer, signalled on the peer's recv_bar), then combines its own rows with
+// the received ones from local shared memory -- the online-softmax merge
+// m_* = max m_s, O = sum 2^(m_s - m_*) O_s, l likewise -- normalises and
+// stores them; the 256 threads of warps 2-9 take (row, 4 columns) items, so
+// consecutive threads write consecutive output columns.  Nothing is stored
+// when any split reported a failed wait.
+template <int DHP, bool SPLIT3>
+__device__ __forceinline__ void cluster_merge(uint32_t base, uint32_t recv_bar,
+                                              const AttnParams& p, int qt, int h,
+                                              volatile int* abort_p) {
+  using Cfg = AttnCfg<DHP, SPLIT3>;
+  constexpr int C4 = DHP / 4;
+  const int ns = p.nsplit;
+  const int me = (int)cluster_ctarank();
+  const int rows_per = (BM + ns - 1) / ns;
+  const int row0 = me * rows_per;
+  const int nrows = min(rows_per, BM - row0);  // rows this CTA receives and merges
+  if (threadIdx.x == 64) {
+    for (int q = 0; q < ns; ++q) {
+      if (q == me) continue;
+      const int k = me < q ? me : me - 1;  // this CTA's slot in q's receive area
+      const int qrows = min(rows_per, BM - q * rows_per);
+      bulk_copy_to_peer(map_shared_rank(base + Cfg::RECV + k * rows_per * Cfg::OP * 4, q),
+                        base + q * rows_per * Cfg::OP * 4, qrows * Cfg::OP * 4,
+                        map_shared_rank(recv_bar, q));
+    }
+  }
+  const float* own = reinterpret_cast<const float*>(
+      static_cast<const uint8_t*>(__cvta_shared_to_generic(base)));
+  const float* recv = own + Cfg::RECV / 4;
+  // Every split's rows carry its validity flag (the first row's suffices).
+  bool valid = mbar_wait(recv_bar, 0, abort_p, p.status);
+  for (int s = 0; valid && s < ns; ++s) {
+    const float* first = s == me ? own : recv + (s < me ? s : s - 1) * rows_per * Cfg::OP;
+    valid = first[DHP + 2] != 0.f;
+  }
+  if (!valid) {
+    // Copies that never landed (only after an abort) finish before the exit.
+    if (threadIdx.x == 64) {
+      const uint64_t t0 = globaltimer();
+      while (!mbar_try_wait(recv_bar, 0) && globaltimer() - t0 < ATTNB_WAIT_LIMIT_NS) {
+      }
+    }
+    return;
+  }
+  const int vrows = min(nrows, p.L - qt * BM - row0);  // rows inside the output
+  const bool vec = p.osD == 1 && (p.osT & 3) == 0 && (p.osH & 3) == 0 &&
+                   (reinterpret_cast<uintptr_t>(p.O) & 15u) == 0;
+  for (int item = threadIdx.x - 64; item < vrows * C4; item += 256) {
+    const int lr = item / C4, d = (item % C4) * 4;
+    auto row_of = [&](int s) {
+      return s == me ? own + (row0 + lr) * Cfg::OP
+                     : recv + ((s < me ? s : s - 1) * rows_per + lr) * Cfg::OP;
+    };
+    float mstar = -INFINITY;
+    for (int s = 0; s < ns; ++s) mstar = fmaxf(mstar, row_of(s)[DHP]);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float lsum = 0.f;
+    for (int s = 0; s < ns; ++s) {
+      const float* rs = row_of(s);
+      const float2 ml = *reinterpret_cast<const float2*>(rs + DHP);
+      const float w = ml.x == -INFINITY ? 0.f : fast_exp2(ml.x - mstar);
+      const float4 v = *reinterpret_cast<const float4*>(rs + d);
+      lsum = fmaf(w, ml.y, lsum);
+      acc.x = fmaf(w, v.x, acc.x);
+      acc.y = fmaf(w, v.y, acc.y);
+      acc.z = fmaf(w, v.z, acc.z);
+      acc.w = fmaf(w, v.w, acc.w);
+    }
+    const float inv = 1.f / lsum;
+    float* orow = p.O + h * p.osH + (int64_t)(qt * BM + row0 + lr) * p.osT;
+    if (vec && d + 3 < p.Dh) {
+      *reinterpret_cast<float4*>(orow + d) =
+          make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    } else {
+      const float v[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        if (d + k < p.Dh) orow[(int64_t)(d + k) * p.osD] = v[k];
+    }
+  }
 }
 
 // FUSED: every CTA owns one key tile, loaded raw by TMA and split in shared
-// memory by warps 2-9 (Q, K) and 6-9 (V).  Otherwise warp 0 streams
-// pre-packed tiles.
+// memory (Q/K by the softmax warps 2-9 before their softmax, V by warp 0).
+// Otherwise warp 0 streams pre-packed tiles.
 template <int DHP, bool SPLIT3, bool FUSED>
-__global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
                    const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
                    const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
@@ -193,7 +317,7 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t sfull[SST], sempty[SST], vfull[VST], vempty[VST];
-  __shared__ __align__(8) uint64_t s_bar, p_bar, pv_bar, final_bar, merge_bar;
+  __shared__ __align__(8) uint64_t s_bar, p_bar, pv_bar, final_bar, recv_bar;
   __shared__ __align__(8) uint64_t rbar[FUSED ? 8 : 1];  // fused: raw Q/K (per slice), V slices
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
@@ -224,14 +348,14 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
       mbar_init(smem_addr(&sempty[i]), 1);
     }
     for (int i = 0; i < VST; ++i) {
-      mbar_init(smem_addr(&vfull[i]), FUSED ? 4 : 1);
+      mbar_init(smem_addr(&vfull[i]), FUSED && i >= kVSlicesWarp0 ? 8 : 1);
       mbar_init(smem_addr(&vempty[i]), 1);
     }
     mbar_init(smem_addr(&s_bar), 1);
-    mbar_init(smem_addr(&p_bar), 4);
+    mbar_init(smem_addr(&p_bar), 8);  // one arrival per softmax warp
     mbar_init(smem_addr(&pv_bar), 1);
     mbar_init(smem_addr(&final_bar), 1);
-    mbar_init(smem_addr(&merge_bar), 1);
+    mbar_init(smem_addr(&recv_bar), 1);
     if (FUSED)
       for (int i = 0; i < 8; ++i) mbar_init(smem_addr(&rbar[i]), 1);
     fence_barrier_init();
@@ -248,27 +372,42 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
   grid_dep_wait();  // packed operands (or, fused, the raw ones) come from earlier kernels
 
   if (warp == 0) {
-    if (FUSED && lane == 0 && j0 < j1) {
+    if (FUSED && j0 < j1) {
       // ----------------------------------------------- raw loads (fused form)
-      // The only key tile's Q/K slices into the S stages' hi slots, its V
-      // rows (32 keys x 32 columns per box) into the staging area.
+      // Lane 0 loads the only key tile's Q/K slices into the S stages' hi
+      // slots and its V rows (32 keys x 32 columns per box) into the staging
+      // area; then the warp splits the first V slices while the softmax warps
+      // split Q/K (and, after that, the remaining V slices).
       const int j = j0;
       const int nvb = min(BN / BK, (p.T - j * BN + BK - 1) / BK);
-      for (int kb = 0; kb < Cfg::NKB; ++kb) {
-        const uint32_t rb = smem_addr(&rbar[kb]), sa = s_addr(kb);
-        mbar_arrive_expect_tx(rb, Cfg::QBOX + Cfg::KBOX);
-        tma_load_3d(sa, &tmQh, rb, kb * BK, qt * BM, h);
-        tma_load_3d(sa + Cfg::OFF_KH, &tmKh, rb, kb * BK, j * BN, h);
+      if (lane == 0) {
+        for (int kb = 0; kb < Cfg::NKB; ++kb) {
+          const uint32_t rb = smem_addr(&rbar[kb]), sa = s_addr(kb);
+          mbar_arrive_expect_tx(rb, Cfg::QBOX + Cfg::KBOX);
+          tma_load_3d(sa, &tmQh, rb, kb * BK, qt * BM, h);
+          tma_load_3d(sa + Cfg::OFF_KH, &tmKh, rb, kb * BK, j * BN, h);
+        }
+        for (int vb = 0; vb < nvb; ++vb) {
+          const uint32_t rb = smem_addr(&rbar[Cfg::NKB + vb]);
+          const uint32_t va = base + Cfg::RING_BYTES + vb * Cfg::VBOX;
+          mbar_arrive_expect_tx(rb, Cfg::VBOX);
+          for (int bx = 0; bx < DHP / 32; ++bx)
+            tma_load_3d(va + bx * 4096, &tmVh, rb, bx * 32, j * BN + vb * BK, h);
+        }
       }
-      for (int vb = 0; vb < nvb; ++vb) {
-        const uint32_t rb = smem_addr(&rbar[Cfg::NKB + vb]);
-        const uint32_t va = base + Cfg::RING_BYTES + vb * Cfg::VBOX;
-        mbar_arrive_expect_tx(rb, Cfg::VBOX);
-        for (int bx = 0; bx < DHP / 32; ++bx)
-          tma_load_3d(va + bx * 4096, &tmVh, rb, bx * 32, j * BN + vb * BK, h);
+      __syncwarp();
+      uint8_t* ring = smem_raw + (base - smem_addr(smem_raw));
+      bool conv = true;
+      for (int vb = 0; vb < min(nvb, kVSlicesWarp0); ++vb) {
+        if (conv && !mbar_wait(smem_addr(&rbar[Cfg::NKB + vb]), 0, abort_p, p.status))
+          conv = false;
+        if (conv) fused_split_v_slice<DHP, SPLIT3>(ring, vb, lane, 0, 1);
+        __syncwarp();
+        if (conv && lane == 0) mbar_arrive(smem_addr(&vfull[vb]));
       }
       // Every copy lands before the CTA can exit (they are never cancelled).
-      for (int i = 0; i < Cfg::NKB + nvb; ++i) drain_wait(smem_addr(&rbar[i]), 0, p.status);
+      if (lane == 0)
+        for (int i = 0; i < Cfg::NKB + nvb; ++i) drain_wait(smem_addr(&rbar[i]), 0, p.status);
     }
     if (!FUSED && lane == 0) {
       // ------------------------------------------------------------ producer
@@ -386,59 +525,118 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
       mma_commit(smem_addr(&final_bar));
       drain_wait(smem_addr(&final_bar), 0, p.status);
     }
-  } else if (warp < 6) {
-    // ----------------------------------------------------- softmax / output
-    const int quarter = warp & 3;
+  } else {
+    // ------------------------------------------------ softmax / output (8 warps)
+    // Two warpgroups share every query row (TMEM lane): group g (warps 2-5:
+    // g = 0, warps 6-9: g = 1) takes key columns [64g, 64g + 64) of each S
+    // tile and output chunks [c_lo, c_hi) of the head dimension.  The row max
+    // is exchanged through shared memory once per tile; the row sums are kept
+    // per group and added at the end.
+    const int g = warp >= 6 ? 1 : 0;
+    const int sw = warp - 2;       // softmax warp 0..7
+    const int quarter = warp & 3;  // TMEM lanes [32 * quarter, +32)
     const int r = quarter * 32 + lane;
     const int qrow = qt * BM + r;
+    const bool leader = sw == 0 && lane == 0;
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    constexpr int NCH = DHP / 32;       // 32-column chunks of the output row
+    constexpr int CH0 = (NCH + 1) / 2;  // chunks of group 0 (group 1: the rest)
+    constexpr int SCOLS = BN / 2;       // S columns per group
+    const int c_lo = g ? CH0 : 0, c_hi = g ? NCH : CH0;
+    uint8_t* ring = smem_raw + (base - smem_addr(smem_raw));
+    __shared__ float red[2][BM];        // per-group row values being exchanged
+    __shared__ int fail_slot[2];        // failures, by the parity of the tile they stop
+    if (threadIdx.x == 64) fail_slot[0] = fail_slot[1] = 0;
+    named_bar_sync(1, 256);
     float m = -INFINITY, l = 0.f;
-    float o[DHP];
+    float o[CH0 * 32];
 #pragma unroll
-    for (int d = 0; d < DHP; ++d) o[d] = 0.f;
-    bool ok = true;
-    if (FUSED && j0 < j1)
-      ok = fused_split_qk<DHP, SPLIT3>(smem_raw + (base - smem_addr(smem_raw)), rbar, sfull,
-                                       threadIdx.x - 64, p.qscale, abort_p, p.status);
+    for (int d = 0; d < CH0 * 32; ++d) o[d] = 0.f;
+    // Every thread runs the same number of loop iterations and passes the
+    // same barriers: a failed wait is recorded (sticky) and acted on by all
+    // threads together at the next per-tile exchange.
+    auto record_fail = [&](int slot) {
+      fail_slot[slot & 1] = 1;
+      softmax_failed = 1;
+    };
+    if (FUSED && j0 < j1) {
+      bool conv = fused_split_qk<DHP, SPLIT3>(ring, rbar, sfull, threadIdx.x - 64, p.qscale,
+                                              abort_p, p.status);
+      const int nvb = min(BN / BK, (p.T - j0 * BN + BK - 1) / BK);
+      for (int vb = kVSlicesWarp0; vb < nvb; ++vb) {
+        if (conv && !mbar_wait(smem_addr(&rbar[Cfg::NKB + vb]), 0, abort_p, p.status))
+          conv = false;
+        if (conv) fused_split_v_slice<DHP, SPLIT3>(ring, vb, lane, sw, 8);
+        __syncwarp();
+        if (conv && lane == 0) mbar_arrive(smem_addr(&vfull[vb]));
+      }
+      if (!conv) record_fail(0);
+    }
     int it = 0;
-    for (int j = j0; ok && j < j1; ++j, ++it) {
-      if (!mbar_wait(smem_addr(&s_bar), it & 1, abort_p, p.status)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const int kbase = j * BN;
+    for (int j = j0; j < j1; ++j, ++it) {
+      const bool got_s = mbar_wait(smem_addr(&s_bar), it & 1, abort_p, p.status);
+      const int kbase = j * BN + g * SCOLS;
       const int kmax = p.causal ? min(p.T - 1, qrow) : p.T - 1;  // last valid key
+      // 16-column TMEM accesses, the big and small halves of a 3xTF32 score
+      // loaded together.  In 1xTF32 with head sizes up to 64 the row's scores
+      // also stay in registers between the max and the exponent passes (TMEM
+      // is read once); otherwise those registers are needed elsewhere.
+      constexpr bool KEEP_S = !SPLIT3 && DHP <= 64;
+      float sv[KEEP_S ? SCOLS : 1];
       float tmax = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t sb[32], ss[32];
-        tmem_ld32(tmem + lane_off + Cfg::S_BIG + c * 32, sb);
-        if (SPLIT3) tmem_ld32(tmem + lane_off + Cfg::S_SMALL + c * 32, ss);
+      if (got_s) {
+        tc_fence_after();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float v = __uint_as_float(sb[i]) + (SPLIT3 ? __uint_as_float(ss[i]) : 0.f);
-          if (kbase + c * 32 + i <= kmax) tmax = fmaxf(tmax, v);
+        for (int c = 0; c < SCOLS / 16; ++c) {
+          uint32_t sb[16], ss[16];
+          const uint32_t col = g * SCOLS + c * 16;
+          if (SPLIT3)
+            tmem_ld16x2(tmem + lane_off + Cfg::S_BIG + col, sb,
+                        tmem + lane_off + Cfg::S_SMALL + col, ss);
+          else
+            tmem_ld16(tmem + lane_off + Cfg::S_BIG + col, sb);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const float v = __uint_as_float(sb[i]) + (SPLIT3 ? __uint_as_float(ss[i]) : 0.f);
+            if constexpr (KEEP_S) sv[c * 16 + i] = v;
+            if (kbase + c * 16 + i <= kmax) tmax = fmaxf(tmax, v);
+          }
         }
+      } else {
+        record_fail(it);
       }
+      red[g][r] = tmax;
+      named_bar_sync(1, 256);
+      if (fail_slot[it & 1]) break;  // the same decision in every thread
+      tmax = fmaxf(tmax, red[g ^ 1][r]);
       const float m_new = fmaxf(m, tmax);
       float lsum = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t sb[32], ss[32];
-        tmem_ld32(tmem + lane_off + Cfg::S_BIG + c * 32, sb);
-        if (SPLIT3) tmem_ld32(tmem + lane_off + Cfg::S_SMALL + c * 32, ss);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float v = __uint_as_float(sb[i]) + (SPLIT3 ? __uint_as_float(ss[i]) : 0.f);
-          const float pv = (kbase + c * 32 + i <= kmax) ? fast_exp2(v - m_new) : 0.f;
+      for (int c = 0; c < SCOLS / 16; ++c) {
+        uint32_t sb[16], ss[16];
+        const uint32_t col = g * SCOLS + c * 16;
+        if constexpr (!KEEP_S) {
+          if (SPLIT3)
+            tmem_ld16x2(tmem + lane_off + Cfg::S_BIG + col, sb,
+                        tmem + lane_off + Cfg::S_SMALL + col, ss);
+          else
+            tmem_ld16(tmem + lane_off + Cfg::S_BIG + col, sb);
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float v;
+          if constexpr (KEEP_S)
+            v = sv[c * 16 + i];
+          else
+            v = __uint_as_float(sb[i]) + (SPLIT3 ? __uint_as_float(ss[i]) : 0.f);
+          const float pv = (kbase + c * 16 + i <= kmax) ? fast_exp2(v - m_new) : 0.f;
           lsum += pv;
           const float hi = tf32_round(pv);
           sb[i] = __float_as_uint(hi);
           ss[i] = __float_as_uint(pv - hi);
         }
-        tmem_st32(tmem + lane_off + Cfg::S_BIG + c * 32, sb);
-        if (SPLIT3) tmem_st32(tmem + lane_off + Cfg::S_SMALL + c * 32, ss);
+        tmem_st16(tmem + lane_off + Cfg::S_BIG + col, sb);
+        if (SPLIT3) tmem_st16(tmem + lane_off + Cfg::S_SMALL + col, ss);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -448,129 +646,111 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
       l = l * alpha + lsum;
       m = m_new;
       if (!mbar_wait(smem_addr(&pv_bar), it & 1, abort_p, p.status)) {
-        ok = false;
-        break;
+        record_fail(it + 1);  // acted on at the next exchange (or after the loop)
+        continue;
       }
       tc_fence_after();
 #pragma unroll
-      for (int c = 0; c < DHP / 32; ++c) {
-        uint32_t vb[32], vs[32];
-        tmem_ld32(tmem + lane_off + Cfg::PV_BIG + c * 32, vb);
-        if (SPLIT3) tmem_ld32(tmem + lane_off + Cfg::PV_SMALL + c * 32, vs);
+      for (int c = 0; c < 2 * CH0; ++c) {
+        if (2 * c_lo + c >= 2 * c_hi) break;
+        uint32_t vb[16], vs[16];
+        const uint32_t col = c_lo * 32 + c * 16;
+        if (SPLIT3)
+          tmem_ld16x2(tmem + lane_off + Cfg::PV_BIG + col, vb,
+                      tmem + lane_off + Cfg::PV_SMALL + col, vs);
+        else
+          tmem_ld16(tmem + lane_off + Cfg::PV_BIG + col, vb);
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          o[c * 32 + i] = fmaf(o[c * 32 + i], alpha,
+        for (int i = 0; i < 16; ++i)
+          o[c * 16 + i] = fmaf(o[c * 16 + i], alpha,
                                __uint_as_float(vb[i]) + (SPLIT3 ? __uint_as_float(vs[i]) : 0.f));
       }
       tc_fence_before();
     }
-    // Rows are owned one per thread, so global traffic goes through layouts
-    // that keep a warp's accesses contiguous: split partials are stored
-    // column-major per tile ([d][row]) and read back with bulk copies, and the
-    // final tile is staged in the (now idle) shared-memory rings and written
-    // with TMA stores (or row by row when the output view does not allow TMA).
-    const size_t tile_id = (size_t)h * p.qtiles + qt;
-    uint8_t* ring = smem_raw + (base - smem_addr(smem_raw));
+    // Rows are owned one per thread pair, so the output tile is staged in the
+    // (now idle) shared-memory rings and written with TMA stores (or row by
+    // row when the output view does not allow TMA); split tiles are staged
+    // there for the cluster merge instead.
     // Wait results can differ between threads after an abort; every branch
-    // below that holds a barrier of the four softmax warps is taken on a
-    // decision they share.
+    // below that holds a barrier of the softmax warps is taken on a decision
+    // they share.
     auto all_ok = [&](bool mine) {
       if (!mine) softmax_failed = 1;
-      named_bar_sync(1, 128);
+      named_bar_sync(1, 256);
       return softmax_failed == 0;
     };
-    ok = all_ok(ok);
-    bool write_out = (p.nsplit == 1) && ok;
-    if (p.nsplit > 1 && ok) {
-      const size_t pbase = ((size_t)split * p.H * p.qtiles + tile_id) * BM;
-      float* po = p.part_o + pbase * DHP;
+    bool ok = all_ok(true);
+    // Row sum over both groups (m is already common).
+    red[g][r] = l;
+    named_bar_sync(1, 256);
+    l += red[g ^ 1][r];
+    if (p.nsplit > 1) {
+      // Stage this split's unnormalised rows for the cluster merge after the
+      // role branches (16-byte writes at a 16-byte-aligned pitch: conflict
+      // free), and arm the barrier that receives the other splits' rows.
+      float* so = reinterpret_cast<float*>(ring);
+      if (ok) {
 #pragma unroll
-      for (int d = 0; d < DHP; ++d) po[(size_t)d * BM + r] = o[d];
-      p.part_ml[pbase + r] = make_float2(m, l);
-      __threadfence();
-      named_bar_sync(1, 128);
-      __shared__ int s_last;
-      unsigned* cnt = p.counters + tile_id;
-      // The ticket wraps to 0 on the last arrival, ready for the next call.
-      if (r == 0) s_last = (atomicInc(cnt, (unsigned)(p.nsplit - 1)) == (unsigned)(p.nsplit - 1));
-      named_bar_sync(1, 128);
-      if (s_last) {
-        // Fetch every other split's partial tile and (m, l) pairs at once.
-        const int nother = p.nsplit - 1;  // <= Cfg::MAX_MERGE (host plan)
-        if (r == 0) {
-          __threadfence();
-          fence_proxy_async_global();
-          const uint32_t mb = smem_addr(&merge_bar);
-          mbar_arrive_expect_tx(mb, nother * (Cfg::PART_TILE + Cfg::PART_ML));
-          int k = 0;
-          for (int sp = 0; sp < p.nsplit; ++sp) {
-            if (sp == split) continue;
-            const size_t qb = ((size_t)sp * p.H * p.qtiles + tile_id) * BM;
-            bulk_load(base + k * Cfg::PART_TILE, p.part_o + qb * DHP, Cfg::PART_TILE, mb);
-            bulk_load(base + nother * Cfg::PART_TILE + k * Cfg::PART_ML, p.part_ml + qb,
-                      Cfg::PART_ML, mb);
-            ++k;
-          }
-        }
-        const bool got = all_ok(mbar_wait(smem_addr(&merge_bar), 0, abort_p, p.status));
-        if (got) {
-          // Fold them into this CTA's own (m, l, o) with the running-max update.
-          const float* tiles = reinterpret_cast<const float*>(ring);
-          const float2* mls =
-              reinterpret_cast<const float2*>(ring + nother * Cfg::PART_TILE);
-          for (int k = 0; k < nother; ++k) {
-            const float2 ml = mls[k * BM + r];
-            const float m_new = fmaxf(m, ml.x);
-            const float a = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
-            const float b2 = (ml.x == -INFINITY) ? 0.f : fast_exp2(ml.x - m_new);
-            l = l * a + ml.y * b2;
-            const float* t = tiles + (size_t)k * DHP * BM + r;
+        for (int c = 0; c < CH0; ++c) {
+          if (c_lo + c >= c_hi) break;
 #pragma unroll
-            for (int d = 0; d < DHP; ++d) o[d] = fmaf(o[d], a, t[d * BM] * b2);
-            m = m_new;
-          }
-          write_out = true;
+          for (int q = 0; q < 8; ++q)
+            *reinterpret_cast<float4*>(so + r * Cfg::OP + (c_lo + c) * 32 + q * 4) =
+                make_float4(o[c * 32 + q * 4], o[c * 32 + q * 4 + 1], o[c * 32 + q * 4 + 2],
+                            o[c * 32 + q * 4 + 3]);
         }
-        // Copies that never landed (only after an abort) finish before exit.
-        if (!got && r == 0) drain_wait(smem_addr(&merge_bar), 0, p.status);
-        named_bar_sync(1, 128);  // merge buffers are read before staging reuses them
+        if (g == 0) *reinterpret_cast<float2*>(so + r * Cfg::OP + DHP) = make_float2(m, l);
+      }
+      if (g == 0) so[r * Cfg::OP + DHP + 2] = ok ? 1.f : 0.f;
+      fence_proxy_async_smem();  // the rows leave by bulk copies (async proxy)
+      if (leader) {
+        const int rows_per = (BM + p.nsplit - 1) / p.nsplit;
+        const int mine = min(rows_per, BM - (int)cluster_ctarank() * rows_per);
+        mbar_arrive_expect_tx(smem_addr(&recv_bar), (p.nsplit - 1) * mine * Cfg::OP * 4);
       }
     }
+    const bool write_out = (p.nsplit == 1) && ok;
     if (write_out) {
       const float inv = 1.f / l;
       if (p.o_tma) {
         // DHP/32 boxes of [128 rows x 32 columns], 128-byte swizzled, each
-        // thread writing its row as eight 16-byte chunks.
+        // thread writing its row of its group's boxes as 16-byte chunks.
 #pragma unroll
-        for (int bx = 0; bx < DHP / 32; ++bx) {
-          uint8_t* box = ring + bx * (BM * 128);
+        for (int c = 0; c < CH0; ++c) {
+          if (c_lo + c >= c_hi) break;
+          uint8_t* box = ring + (c_lo + c) * (BM * 128);
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {
-            const int d = bx * 32 + c * 4;
-            *reinterpret_cast<float4*>(box + r * 128 + ((c ^ (r & 7)) << 4)) =
+          for (int q = 0; q < 8; ++q) {
+            const int d = c * 32 + q * 4;
+            *reinterpret_cast<float4*>(box + r * 128 + ((q ^ (r & 7)) << 4)) =
                 make_float4(o[d] * inv, o[d + 1] * inv, o[d + 2] * inv, o[d + 3] * inv);
           }
         }
         fence_proxy_async_smem();
-        named_bar_sync(1, 128);
-        if (r == 0) {
+        named_bar_sync(1, 256);
+        if (leader) {
 #pragma unroll
-          for (int bx = 0; bx < DHP / 32; ++bx)
+          for (int bx = 0; bx < NCH; ++bx)
             tma_store_3d(&tmO, base + bx * (BM * 128), bx * 32, qt * BM, h);
           bulk_commit_group();
           bulk_wait_read_all();
         }
       } else {
         // Stage the normalised tile (row stride DHP + 1: conflict-free column
-        // writes), then write each row with the warp's lanes along the row.
+        // writes), then write each row with a warp's lanes along the row.
         float* stile = reinterpret_cast<float*>(ring);
 #pragma unroll
-        for (int d = 0; d < DHP; ++d) stile[r * (DHP + 1) + d] = o[d] * inv;
-        named_bar_sync(1, 128);
+        for (int c = 0; c < CH0; ++c) {
+          if (c_lo + c >= c_hi) break;
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            stile[r * (DHP + 1) + (c_lo + c) * 32 + i] = o[c * 32 + i] * inv;
+        }
+        named_bar_sync(1, 256);
         const int rows = min(BM, p.L - qt * BM);
         float* obase = p.O + h * p.osH + (int64_t)qt * BM * p.osT;
 #pragma unroll 4
-        for (int rr = quarter; rr < rows; rr += 4) {
+        for (int rr = sw; rr < rows; rr += 8) {
           float* orow = obase + (int64_t)rr * p.osT;
 #pragma unroll
           for (int dd = 0; dd < DHP; dd += 32)
@@ -578,46 +758,18 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
         }
       }
     }
-  } else if (FUSED) {
-    // ---------------------------------------------------- operand converters
-    // Q and K are split together with the softmax warps; V rows, staged by
-    // TMA, are split and transposed into the K-major V^T slots here.
-    const int ct = threadIdx.x - 192;  // 0..127
-    const int cw = ct >> 5;            // converter warp 0..3
-    uint8_t* sm = smem_raw + (base - smem_addr(smem_raw));
-    bool ok = j0 < j1;
-    if (ok)
-      ok = fused_split_qk<DHP, SPLIT3>(sm, rbar, sfull, threadIdx.x - 64, p.qscale, abort_p,
-                                       p.status);
-    // V: staging slice vb holds keys vb*32.. as DHP/32 boxes of [32 keys x 32
-    // columns] (128-byte swizzle).  Lane = key: a 16-byte read of four
-    // columns of its row, four 4-byte writes down the V^T columns.
-    const int nvb = ok ? min(BN / BK, (p.T - j0 * BN + BK - 1) / BK) : 0;
-    for (int vb = 0; vb < nvb; ++vb) {
-      if (!mbar_wait(smem_addr(&rbar[Cfg::NKB + vb]), 0, abort_p, p.status)) break;
-      const uint8_t* raw = sm + Cfg::RING_BYTES + vb * Cfg::VBOX;
-      uint8_t* st = sm + SST * Cfg::S_STAGE + vb * Cfg::V_STAGE;
-#pragma unroll
-      for (int g = cw; g < DHP / 4; g += 4) {
-        const int bx = g >> 3, c = g & 7;
-        const float4 x = *reinterpret_cast<const float4*>(raw + bx * 4096 + lane * 128 +
-                                                          ((c ^ (lane & 7)) << 4));
-        float4 hi, lo;
-        split4(x, 1.f, hi, lo);
-        const float hv[4] = {hi.x, hi.y, hi.z, hi.w};
-        const float lv[4] = {lo.x, lo.y, lo.z, lo.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int d = g * 4 + i;
-          const uint32_t off = d * 128 + (((lane >> 2) ^ (d & 7)) << 4) + (lane & 3) * 4;
-          *reinterpret_cast<float*>(st + off) = hv[i];
-          if (SPLIT3) *reinterpret_cast<float*>(st + Cfg::VBOX + off) = lv[i];
-        }
-      }
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_addr(&vfull[vb]));
-    }
+  }
+
+  // ------------------------------------------------------------- split merge
+  // The CTAs of a cluster hold the key splits of one (head, query tile).
+  // After the first barrier every CTA reads the staged rows of all splits
+  // through distributed shared memory and writes its share of the output
+  // rows; the second keeps every CTA's shared memory alive until the others
+  // are done reading it.  Every thread passes both barriers.
+  if (p.nsplit > 1) {
+    cluster_sync_all();
+    if (warp >= 2) cluster_merge<DHP, SPLIT3>(base, smem_addr(&recv_bar), p, qt, h, abort_p);
+    cluster_sync_all();
   }
 
   tc_fence_before();
@@ -644,17 +796,15 @@ void launch_attn(const CUtensorMap* maps, const AttnParams& prm, int qtiles, cud
   }
   constexpr int smem = FUSED ? Cfg::SMEM_FUSED : Cfg::SMEM;
   const dim3 grid(qtiles, prm.nsplit, prm.H);
-  ATTNB_CUDA(launch_pdl(attn_tc_kernel<DHP, SPLIT3, FUSED>, grid,
-                        dim3(FUSED ? kThreadsFused : kThreads), smem, s, maps[0], maps[1],
-                        maps[2], maps[3], maps[4], maps[5], maps[6], prm));
-}
-
-int max_merge(int dhp, bool split3) {
-  switch (dhp) {
-    case 32: return split3 ? AttnCfg<32, true>::MAX_MERGE : AttnCfg<32, false>::MAX_MERGE;
-    case 64: return split3 ? AttnCfg<64, true>::MAX_MERGE : AttnCfg<64, false>::MAX_MERGE;
-    case 96: return split3 ? AttnCfg<96, true>::MAX_MERGE : AttnCfg<96, false>::MAX_MERGE;
-    default: return split3 ? AttnCfg<128, true>::MAX_MERGE : AttnCfg<128, false>::MAX_MERGE;
+  if (prm.nsplit > 1) {
+    // The key splits of a (head, query tile) form one cluster (merge through
+    // distributed shared memory).
+    ATTNB_CUDA(launch_pdl_cluster(attn_tc_kernel<DHP, SPLIT3, FUSED>, grid, dim3(kThreads), smem,
+                                  s, dim3(1, prm.nsplit, 1), maps[0], maps[1], maps[2], maps[3],
+                                  maps[4], maps[5], maps[6], prm));
+  } else {
+    ATTNB_CUDA(launch_pdl(attn_tc_kernel<DHP, SPLIT3, FUSED>, grid, dim3(kThreads), smem, s,
+                          maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], maps[6], prm));
   }
 }
 
@@ -696,10 +846,9 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
   // Split the key range when (head, query tile) pairs cannot fill the GPU.
   const int pairs = H * p.qtiles;
   int ns = 1;
-  if (!causal && pairs < num_sms && pairs <= kMergeCounters)
-    ns = std::min(n_kv, std::max(1, num_sms / pairs));
-  // The last CTA of a tile pulls every other split into shared memory at once.
-  ns = std::min(ns, 1 + max_merge(p.dhp, p.split3));
+  if (!causal && pairs < num_sms) ns = std::min(n_kv, std::max(1, num_sms / pairs));
+  // The splits of a tile form one thread-block cluster (at most 8 portable).
+  ns = std::min(ns, kMaxSplits);
   p.tiles_per_split = (n_kv + ns - 1) / ns;
   p.nsplit = (n_kv + p.tiles_per_split - 1) / p.tiles_per_split;
   p.fusable = p.tiles_per_split == 1 && p.dhp <= 64;
@@ -716,16 +865,13 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
   p.off_q = take(q * parts);
   p.off_k = take(k * parts);
   p.off_v = take(v * parts);
-  const size_t tile_rows = (size_t)p.nsplit * H * p.qtiles * BM;
-  p.off_po = p.nsplit > 1 ? take(tile_rows * p.dhp * 4) : 0;
-  p.off_pml = p.nsplit > 1 ? take(tile_rows * 8) : 0;
   p.ws_bytes = off;
   return p;
 }
 
 void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View3& V,
-                 const MView3& O, bool causal, void* ws, unsigned* counters, int* status,
-                 int num_sms, cudaStream_t s) {
+                 const MView3& O, bool causal, void* ws, int* status, int num_sms,
+                 cudaStream_t s) {
   char* w = static_cast<char*>(ws);
   const float qscale = kLog2e / std::sqrt(static_cast<float>(p.Dh));
   CUtensorMap maps[7] = {};
@@ -805,9 +951,6 @@ void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View
   prm.vsT = V.sT;
   prm.vsD = V.sD;
   prm.qscale = qscale;
-  prm.part_o = p.nsplit > 1 ? reinterpret_cast<float*>(w + p.off_po) : nullptr;
-  prm.part_ml = p.nsplit > 1 ? reinterpret_cast<float2*>(w + p.off_pml) : nullptr;
-  prm.counters = counters;
   prm.status = status;
   ProfScope prof("attn_tc", s);
   if (p.split3) dispatch_dhp<true>(p.dhp, fused, maps, prm, p.qtiles, s);

@@ -172,7 +172,7 @@ void block_dev(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor*
   if (attn_tc_supported(Q->Dh)) {
     const AttnTcPlan p =
         attn_tc_plan(Q->H, Q->T, K->T, Q->Dh, causal != 0, precision, c.num_sms);
-    attn_tc_run(p, q, k, v, o, causal != 0, ws, merge_counters(c, s), c.status, c.num_sms, s);
+    attn_tc_run(p, q, k, v, o, causal != 0, ws, c.status, c.num_sms, s);
   } else {
     attn_block_simt_launch(q, k, v, o, causal != 0, s);
   }

@@ -18,9 +18,10 @@
 //               and each finished accumulator to the epilogue;
 //   warps 2-5   epilogue: tcgen05.ld the accumulator (lane = row), apply
 //               alpha / beta / bias, store to C, release the slot.
-// 1xTF32: one 128x256 accumulator per tile; the two slots let the epilogue of
-// tile i overlap the MMAs of tile i+1.
-// 3xTF32 (128x128 tiles): hi*hi goes to a "big" accumulator and
+// 1xTF32: one 128xBN accumulator per tile (BN = 256, or 128 / 64 when the
+// product has too few wide tiles to occupy every SM); the two slots let the
+// epilogue of tile i overlap the MMAs of tile i+1.
+// 3xTF32 (128x128 or 128x64 tiles): hi*hi goes to a "big" accumulator and
 // hi*lo + lo*hi to a separate "small" one, and both are drained into fp32
 // registers every 256 K values, alternating slots, so the epilogue's
 // round-to-nearest fp32 sums carry the long-K accumulation.
@@ -378,6 +379,16 @@ void launch_gemm(const GemmPlan& p, const CUtensorMap& a_hi, const CUtensorMap& 
                         status));
 }
 
+// Output tile width: the widest (256 for 1xTF32, 128 for 3xTF32, whose MMAs
+// are already 2*BN wide) that still gives every SM a tile; narrower tiles for
+// small products that would otherwise leave most SMs idle.
+int pick_bn(int M, int N, bool split3, int num_sms) {
+  const int tiles_m = (M + BM - 1) / BM;
+  for (int bn = split3 ? 128 : 256; bn > 64; bn /= 2)
+    if ((int64_t)tiles_m * ((N + bn - 1) / bn) >= num_sms) return bn;
+  return 64;
+}
+
 }  // namespace
 
 GemmPlan gemm_plan(int M, int N, int K, int precision) {
@@ -430,18 +441,29 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
   jobs[1] = b_kmajor ? PackJob{B, 0, ldb, 1, 1, p.N, p.K, p.N, p.Kp, false, 1.f, b_hi, b_lo}
                      : PackJob{B, 0, ldb, 1, 1, p.K, p.N, p.N, p.Kp, true, 1.f, b_hi, b_lo};
   pack_launch(jobs, 2, p.split3, num_sms, s);
-  const int bn = p.split3 ? 128 : 256;
+  const int bn = pick_bn(p.M, p.N, p.split3, num_sms);
   const CUtensorMap tA_hi = make_tmap_2d(a_hi, p.M, p.Kp, p.Kp, BM, BK);
   const CUtensorMap tB_hi = make_tmap_2d(b_hi, p.N, p.Kp, p.Kp, bn, BK);
   ProfScope prof("gemm_tc", s);
   if (p.split3) {
     const CUtensorMap tA_lo = make_tmap_2d(a_lo, p.M, p.Kp, p.Kp, BM, BK);
     const CUtensorMap tB_lo = make_tmap_2d(b_lo, p.N, p.Kp, p.Kp, bn, BK);
-    launch_gemm<128, true>(p, tA_hi, tA_lo, tB_hi, tB_lo, C, ldc, alpha, beta, bias, status,
-                           num_sms, s);
-  } else {
-    launch_gemm<256, false>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias, status,
+    if (bn == 128)
+      launch_gemm<128, true>(p, tA_hi, tA_lo, tB_hi, tB_lo, C, ldc, alpha, beta, bias, status,
+                             num_sms, s);
+    else
+      launch_gemm<64, true>(p, tA_hi, tA_lo, tB_hi, tB_lo, C, ldc, alpha, beta, bias, status,
                             num_sms, s);
+  } else {
+    if (bn == 256)
+      launch_gemm<256, false>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias, status,
+                              num_sms, s);
+    else if (bn == 128)
+      launch_gemm<128, false>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias, status,
+                              num_sms, s);
+    else
+      launch_gemm<64, false>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias, status,
+                             num_sms, s);
   }
 }
 

@@ -48,16 +48,15 @@ struct AttnTcPlan {
   // One key tile per CTA and dhp <= 64: when the views allow TMA reads, the
   // kernel loads and splits the raw operands itself (no packing launch).
   bool fusable;
-  size_t off_q, off_k, off_v, off_po, off_pml, ws_bytes;
+  size_t off_q, off_k, off_v, ws_bytes;
 };
 // Head sizes the tensor-core kernel takes (padded to a multiple of 32, <= 128).
 bool attn_tc_supported(int Dh);
 AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision, int num_sms);
-// `ws` holds plan.ws_bytes bytes (packed operands and split partials);
-// `counters` kMergeCounters zeroed merge tickets (left zeroed on success).
+// `ws` holds plan.ws_bytes bytes (packed operands).
 void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View3& V,
-                 const MView3& O, bool causal, void* ws, unsigned* counters, int* status,
-                 int num_sms, cudaStream_t s);
+                 const MView3& O, bool causal, void* ws, int* status, int num_sms,
+                 cudaStream_t s);
 
 // ------------------------------------------------ operand packing (K2)
 // One packing job: a strided 3-D source src[h][r][c] (r < R, c < C), times
@@ -95,6 +94,27 @@ cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t s
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// As launch_pdl, with the grid tiled into thread-block clusters of `cluster`.
+template <class... KArgs, class... Args>
+cudaError_t launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                               cudaStream_t s, dim3 cluster, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = cluster.x;
+  attr[1].val.clusterDim.y = cluster.y;
+  attr[1].val.clusterDim.z = cluster.z;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
 }
 

@@ -69,15 +69,9 @@ DeviceCtx& current_ctx() {
   ATTNB_CUDA(cudaMalloc(&c->status, sizeof(int)));
   ATTNB_CUDA(cudaMemset(c->status, 0, sizeof(int)));
   ATTNB_CUDA(cudaMallocHost(&c->status_host, sizeof(int)));
-  ATTNB_CUDA(cudaMalloc(&c->merge_counters, 2 * kMergeCounters * sizeof(unsigned)));
-  ATTNB_CUDA(cudaMemset(c->merge_counters, 0, 2 * kMergeCounters * sizeof(unsigned)));
   DeviceCtx& ref = *c;
   g_ctx.emplace(dev, std::move(c));
   return ref;
-}
-
-unsigned* merge_counters(DeviceCtx& c, cudaStream_t stream) {
-  return c.merge_counters + (stream == c.stream ? 0 : kMergeCounters);
 }
 
 void* dev_scratch(DeviceCtx& c, size_t bytes, cudaStream_t stream) {
@@ -240,8 +234,6 @@ int consume_status(DeviceCtx& c, cudaStream_t stream) {
     h = *c.status_host;
   }
   if (h) {
-    // An aborted kernel may have left merge tickets part-way.
-    ATTNB_CUDA(cudaMemsetAsync(c.merge_counters, 0, 2 * kMergeCounters * sizeof(unsigned), stream));
     ATTNB_CUDA(cudaMemsetAsync(c.status, 0, sizeof(int), stream));
     ATTNB_CUDA(cudaStreamSynchronize(stream));
     return ATTNB_ERR_DEVICE_TIMEOUT;

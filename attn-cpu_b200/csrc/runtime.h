@@ -45,18 +45,7 @@ struct DeviceCtx {
   DeviceBuffer scratch_host_path; // kernel scratch for host-pointer calls
   std::mutex scratch_mu;
   DeviceBuffer scratch_dev_path;  // kernel scratch for _dev calls (per device)
-  // Arrival tickets of the attention split merge, zero between calls (each
-  // tile's ticket wraps back to 0 after its last split; a time-out re-zeroes
-  // them).  First half for the host-pointer path, second for _dev calls.
-  unsigned* merge_counters = nullptr;
 };
-
-// Tickets per half of DeviceCtx::merge_counters: the split merge runs only
-// when fewer (head, query-tile) pairs than this exist.
-constexpr int kMergeCounters = 256;
-
-// The half of the merge tickets that calls on `stream` use.
-unsigned* merge_counters(DeviceCtx& c, cudaStream_t stream);
 
 // Context of the current CUDA device (created on first use).
 DeviceCtx& current_ctx();

@@ -85,38 +85,76 @@ __device__ void pack_rows(const PackJob& j, bool split3, int lb, int nb) {
   }
 }
 
-// out[h][c][r] = src[h][r][c] through 32x32 shared-memory tiles.
-__device__ void pack_transposed(const PackJob& j, bool split3, int lb, int nb, float (*tile)[33]) {
-  const int tiles_c = (j.rows_out + 31) / 32, tiles_r = (j.cols_out + 31) / 32;
+// out[h][c][r] = src[h][r][c] through 64x64 shared-memory tiles (row pitch
+// 65: the transposed writes spread over the banks).  Sixteen threads cover a
+// 64-wide row with 16-byte accesses on both sides when the source allows.
+constexpr int kTile = 64;
+constexpr int kTilePitch = kTile + 1;
+
+__device__ void pack_transposed(const PackJob& j, bool split3, int lb, int nb, float* tile) {
+  const int tiles_c = (j.rows_out + kTile - 1) / kTile, tiles_r = (j.cols_out + kTile - 1) / kTile;
   const int64_t ntiles = (int64_t)j.H * tiles_c * tiles_r;
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  const int t16 = threadIdx.x & 15, row_in = threadIdx.x >> 4;  // 16 rows per pass
+  const bool vec = j.sC == 1 && (j.sR & 3) == 0 && (j.sH & 3) == 0 &&
+                   (reinterpret_cast<uintptr_t>(j.src) & 15u) == 0;
+  const bool vec_out = (j.cols_out & 3) == 0;
   for (int64_t t = lb; t < ntiles; t += nb) {
     const int h = static_cast<int>(t / ((int64_t)tiles_c * tiles_r));
     const int rem = static_cast<int>(t % ((int64_t)tiles_c * tiles_r));
-    const int c0 = (rem % tiles_c) * 32, r0 = (rem / tiles_c) * 32;
+    const int c0 = (rem % tiles_c) * kTile, r0 = (rem / tiles_c) * kTile;
     const float* s = j.src + h * j.sH;
-    __syncthreads();
-    for (int y = ty; y < 32; y += 8) {
-      const int r = r0 + y, c = c0 + tx;
-      tile[y][tx] = (r < j.R && c < j.C) ? s[r * j.sR + c * j.sC] * j.scale : 0.f;
+    __syncthreads();  // the previous tile has been written out
+    // Load: source rows r0.. (columns c0 + 4*t16 ..), stored transposed.
+#pragma unroll
+    for (int p = 0; p < kTile / 16; ++p) {
+      const int y = p * 16 + row_in, r = r0 + y, c = c0 + 4 * t16;
+      float x[4] = {0.f, 0.f, 0.f, 0.f};
+      if (r < j.R) {
+        const float* sr = s + (int64_t)r * j.sR;
+        if (vec && c + 3 < j.C) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(sr + c));
+          x[0] = v.x;
+          x[1] = v.y;
+          x[2] = v.z;
+          x[3] = v.w;
+        } else {
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (c + k < j.C) x[k] = sr[(int64_t)(c + k) * j.sC];
+        }
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) tile[(4 * t16 + k) * kTilePitch + y] = x[k] * j.scale;
     }
     __syncthreads();
+    // Store: output rows c0.. (columns r0 + 4*t16 ..), split into hi / lo.
     float* oh = j.hi + (int64_t)h * j.rows_out * j.cols_out;
     float* ol = split3 ? j.lo + (int64_t)h * j.rows_out * j.cols_out : nullptr;
-    for (int y = ty; y < 32; y += 8) {
-      const int c = c0 + y, r = r0 + tx;
-      if (c < j.rows_out && r < j.cols_out) {
-        float hv, lv;
-        split_value(tile[tx][y], split3, hv, lv);
-        oh[(int64_t)c * j.cols_out + r] = hv;
-        if (split3) ol[(int64_t)c * j.cols_out + r] = lv;
+#pragma unroll
+    for (int p = 0; p < kTile / 16; ++p) {
+      const int y = p * 16 + row_in, c = c0 + y, r = r0 + 4 * t16;
+      if (c >= j.rows_out) continue;
+      float hv[4], lv[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) split_value(tile[y * kTilePitch + 4 * t16 + k], split3, hv[k], lv[k]);
+      const int64_t o = (int64_t)c * j.cols_out + r;
+      if (vec_out && r + 3 < j.cols_out) {
+        *reinterpret_cast<float4*>(oh + o) = make_float4(hv[0], hv[1], hv[2], hv[3]);
+        if (split3) *reinterpret_cast<float4*>(ol + o) = make_float4(lv[0], lv[1], lv[2], lv[3]);
+      } else {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          if (r + k < j.cols_out) {
+            oh[o + k] = hv[k];
+            if (split3) ol[o + k] = lv[k];
+          }
       }
     }
   }
 }
 
 __global__ void __launch_bounds__(kThreads) pack_kernel(const __grid_constant__ PackArgs a) {
-  __shared__ float tile[32][33];
+  __shared__ float tile[kTile * kTilePitch];
   // Let the dependent tensor-core kernel start its prologue now; it waits
   // (griddepcontrol.wait) for this grid's writes before reading them.
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
@@ -142,7 +180,7 @@ void pack_launch(const PackJob* jobs, int njobs, bool split3, int num_sms, cudaS
     a.start[i] = total;
     int64_t blocks;
     if (j.transpose) {
-      blocks = (int64_t)j.H * ((j.rows_out + 31) / 32) * ((j.cols_out + 31) / 32);
+      blocks = (int64_t)j.H * ((j.rows_out + kTile - 1) / kTile) * ((j.cols_out + kTile - 1) / kTile);
     } else {
       const int cp4 = j.cols_out / 4;
       const int rpw = 32 / (cp4 >= 32 ? 32 : cp4 >= 16 ? 16 : cp4 >= 8 ? 8 : 4);

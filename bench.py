@@ -49,6 +49,9 @@ WORKLOADS = {
                   desc="SGEMM fp32 1024^3, U[-1,1], beta=0 (gemm)"),
     "sgemm-large": dict(metric="SGEMM TFLOP/s per GPU", unit="TFLOP/s", M=16384, N=16384,
                         K=16384, desc="SGEMM fp32 16384^3, U[-1,1], beta=0 (gemm)"),
+    "prefill-large": dict(metric="MHA prefill TFLOP/s", unit="TFLOP/s", H=32, L=4096, T=4096,
+                          Dh=128, desc="MHA prefill fp32 [1,32,4096,128] non-causal "
+                                       "(attn_block_dense)"),
     "block": dict(metric="attention block TFLOP/s", unit="TFLOP/s", B=4, T=2048, D=4096, H=32,
                   desc="attention block fp32: hidden 4096, 32 heads, Dh 128, batch 4, "
                        "seq 2048 (mha_block_dense)"),
@@ -68,7 +71,7 @@ NCU_TRAFFIC = {
 
 def flops_of(w: str) -> float:
     c = WORKLOADS[w]
-    if w == "prefill":
+    if w.startswith("prefill"):
         return 4.0 * c["H"] * c["L"] * c["T"] * c["Dh"]
     if w == "decode":
         return 4.0 * c["H"] * c["T"] * c["Dh"]
@@ -277,7 +280,7 @@ def setup_workload(w: str, rank: int, precision):
 
     c = WORKLOADS[w]
     g = torch.Generator(device="cuda").manual_seed(1000 + rank)
-    if w == "prefill":
+    if w.startswith("prefill"):
         H, L, T, Dh = c["H"], c["L"], c["T"], c["Dh"]
         Q = torch.randn(H, L, Dh, device="cuda", generator=g)
         K = torch.randn(H, T, Dh, device="cuda", generator=g)
@@ -289,9 +292,9 @@ def setup_workload(w: str, rank: int, precision):
         e2e = lambda: attn_cpu.attn_block_dense(nQ, nK, nV, precision=precision)
         h2d = 4 * (Q.numel() + K.numel() + V.numel())
         d2h = 4 * O.numel()
-        # One launch: each CTA holds one key tile and loads and splits the raw
-        # operands itself (no packing pass).
-        return run, e2e, h2d, d2h, 1
+        # [1,8,512,64]: one launch (each CTA holds one key tile and loads and
+        # splits the raw operands itself); longer sequences: pack + attention.
+        return run, e2e, h2d, d2h, 1 if w == "prefill" else 2
     if w == "decode":
         H, T, Dh = c["H"], c["T"], c["Dh"]
         Q = torch.randn(H, Dh, device="cuda", generator=g)
@@ -337,7 +340,7 @@ def setup_workload(w: str, rank: int, precision):
 # algorithmic work per step.
 def dominant_of(w: str):
     c = WORKLOADS[w]
-    if w == "prefill":
+    if w.startswith("prefill"):
         return "attn_tc", flops_of(w)
     if w == "decode":
         return "decode", bytes_of(w)
@@ -577,7 +580,7 @@ def main():
     head = measure(args.workload, rank, world, args.steps, args.warmup, prec, peaks)
     also = []
     if world == 1 and not args.no_also:
-        for w in ("decode", "sgemm", "sgemm-large", "block"):
+        for w in ("decode", "sgemm", "sgemm-large", "prefill-large", "block"):
             if w == args.workload:
                 continue
             steps = args.steps if w in ("decode", "sgemm") else max(3, min(args.steps, 5))
