@@ -117,8 +117,8 @@ __device__ __forceinline__ uint32_t map_shared_rank(uint32_t addr, uint32_t rank
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
-// 2-D tiled load, no multicast.  x (innermost, elements) must be a multiple
-// of 4 for fp32 so the copy starts on a 16-byte boundary.
+// 2-D tiled load into this CTA's shared memory.  x (innermost, elements)
+// must be a multiple of 4 for fp32 so the copy starts on a 16-byte boundary.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
                                             int x, int y) {
   asm volatile(
@@ -136,8 +136,6 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map
       : "memory");
 }
 
-// Untiled bulk copy global -> shared (no multicast); both addresses 16-byte
-// aligned, bytes a multiple of 16.  Completes on `bar` with `bytes` of tx.
 // Bulk copy from this CTA's shared memory into another CTA's of the cluster
 // (`dst` and `bar` are shared::cluster addresses from map_shared_rank); the
 // destination barrier's transaction count receives the bytes.  Addresses and

@@ -61,10 +61,11 @@ WORKLOADS = {
 # one-pass ncu captures of dram__bytes_read.sum + dram__bytes_write.sum on the
 # same problem; commands and figures in profiles/.  Cold-cache captures.
 NCU_TRAFFIC = {
-    ("prefill", "3xtf32"): None,       # attn_tc, [1,8,512,64]: raw Q/K/V (re-capture pending)
+    ("prefill", "3xtf32"): 3.22e6,     # attn_tc, [1,8,512,64]: raw Q/K/V read once
+    ("prefill-large", "3xtf32"): 5.00e8,  # attn_tc [1,32,4096,128]: packed K/V re-read via L2
     ("decode", "3xtf32"): 1.0798e9,    # decode: K + V once (1.0737e9) + split partials
     ("decode", "tf32"): 1.0798e9,
-    ("sgemm-large", "3xtf32"): 97.78e9,  # gemm_tc 16384^3: packed operands re-read ~24x
+    ("sgemm-large", "3xtf32"): 51.15e9,  # gemm_tc 16384^3: packed operands re-read ~12x
     ("block", "3xtf32"): 6.93e9,       # gemm_tc QKV (5.11e9) + output (1.82e9) projections
 }
 

@@ -26,6 +26,7 @@ def _qkv(H, L, T, Dh, seed):
     (2, 33, 300, 96, False), (1, 70, 70, 48, True), (2, 129, 129, 64, True),
     (32, 256, 256, 128, False), (2, 300, 300, 32, True), (1, 1000, 1000, 64, False),
     (2, 100, 100, 200, False), (1, 70, 70, 160, True),   # head sizes > 128: CUDA-core kernel
+    (6, 300, 300, 64, False), (5, 400, 400, 48, True),   # head counts that 4 does not divide
 ])
 def test_block_vs_oracle(cuda, H, L, T, Dh, causal):
     import attn_cpu
