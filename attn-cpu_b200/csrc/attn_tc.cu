@@ -77,16 +77,24 @@ struct AttnCfg {
   // of the tile behind them.
   static constexpr int OP = DHP + 4;
   static constexpr int RECV = BM * OP * 4;
-  static constexpr int S_BIG = 0;
+  // TMEM: NBUF S buffers ([big | small] key columns each), then NBUF P.V
+  // accumulators ([big | small] head columns).  Two of each when they fit
+  // (1xTF32): S(j+1) then runs during the softmax of tile j, and PV(j) is
+  // folded into the output during the softmax of tile j+1.
+  static constexpr int S_BUF = NPART * BN;
+  static constexpr int PV_BUF = NPART * DHP;
+  static constexpr int NBUF = 2 * (S_BUF + PV_BUF) <= 512 ? 2 : 1;
+  static constexpr int PV_BASE = NBUF * S_BUF;
+  static constexpr int S_BIG = 0;  // within an S buffer
   static constexpr int S_SMALL = BN;
-  static constexpr int PV_BIG = NPART * BN;
-  static constexpr int PV_SMALL = PV_BIG + DHP;
-  static constexpr int TMEM_COLS = SPLIT3 ? 512 : 256;
+  static constexpr int PV_BIG = 0;  // within a P.V accumulator
+  static constexpr int PV_SMALL = DHP;
+  static constexpr int TMEM_COLS = 512;
   static_assert(DHP % 32 == 0 && DHP <= 128, "head size padded to 32..128");
   static_assert(V_STAGES >= 2, "V ring needs two stages");
   static_assert(BM * (DHP + 1) * 4 <= S_STAGES * S_STAGE, "output staging fits the S ring");
   static_assert(RECV + BM * OP * 4 <= RING_BYTES, "merge staging fits the rings");
-  static_assert(PV_BIG + NPART * DHP <= TMEM_COLS, "TMEM budget");
+  static_assert(NBUF * (S_BUF + PV_BUF) <= TMEM_COLS, "TMEM budget");
 };
 
 // Position in a ring of N stages (stage index and the phase parity to wait on).
@@ -317,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t sfull[SST], sempty[SST], vfull[VST], vempty[VST];
-  __shared__ __align__(8) uint64_t s_bar, p_bar, pv_bar, final_bar, recv_bar;
+  __shared__ __align__(8) uint64_t s_bar[2], p_bar, pv_bar[2], final_bar, recv_bar;
   __shared__ __align__(8) uint64_t rbar[FUSED ? 8 : 1];  // fused: raw Q/K (per slice), V slices
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
@@ -351,9 +359,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_addr(&vfull[i]), FUSED && i >= kVSlicesWarp0 ? 8 : 1);
       mbar_init(smem_addr(&vempty[i]), 1);
     }
-    mbar_init(smem_addr(&s_bar), 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_addr(&s_bar[b]), 1);
+      mbar_init(smem_addr(&pv_bar[b]), 1);
+    }
     mbar_init(smem_addr(&p_bar), 8);  // one arrival per softmax warp
-    mbar_init(smem_addr(&pv_bar), 1);
     mbar_init(smem_addr(&final_bar), 1);
     mbar_init(smem_addr(&recv_bar), 1);
     if (FUSED)
@@ -461,17 +471,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---------------------------------------------------------- MMA issuer
       Ring<SST> rs;
       Ring<VST> rv;
-      bool ok = true;
-      int it = 0;
-      for (int j = j0; ok && j < j1; ++j, ++it) {
-        // S(j) overwrites the TMEM columns PV(j-1) read P from.
-        if (it > 0 && !mbar_wait(smem_addr(&pv_bar), (it - 1) & 1, abort_p, p.status)) break;
-        tc_fence_after();
+      // S(j0 + it) into S buffer it % NBUF.
+      auto issue_s = [&](int it) {
+        const uint32_t sbuf = tmem + (it % Cfg::NBUF) * Cfg::S_BUF;
         for (int kb = 0; kb < Cfg::NKB; ++kb) {
-          if (!mbar_wait(smem_addr(&sfull[rs.stage]), rs.phase, abort_p, p.status)) {
-            ok = false;
-            break;
-          }
+          if (!mbar_wait(smem_addr(&sfull[rs.stage]), rs.phase, abort_p, p.status)) return false;
           tc_fence_after();
           const uint32_t sa = s_addr(rs.stage);
 #pragma unroll
@@ -482,25 +486,27 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (SPLIT3) {
               // [S_BIG | S_SMALL] (+)= Qh . [Kh | Kl]^T, then S_SMALL += Ql . Kh^T.
               const uint64_t ql = sdesc_kmajor_sw128(sa + Cfg::OFF_QL + kk * 32);
-              mma_tf32(tmem + Cfg::S_BIG, qh, kh, IDESC_S2, acc);
-              mma_tf32(tmem + Cfg::S_SMALL, ql, kh, IDESC_S, 1u);
+              mma_tf32(sbuf + Cfg::S_BIG, qh, kh, IDESC_S2, acc);
+              mma_tf32(sbuf + Cfg::S_SMALL, ql, kh, IDESC_S, 1u);
             } else {
-              mma_tf32(tmem + Cfg::S_BIG, qh, kh, IDESC_S, acc);
+              mma_tf32(sbuf + Cfg::S_BIG, qh, kh, IDESC_S, acc);
             }
           }
           mma_commit(smem_addr(&sempty[rs.stage]));
           rs.advance();
         }
-        if (!ok) break;
-        mma_commit(smem_addr(&s_bar));
-        if (!mbar_wait(smem_addr(&p_bar), it & 1, abort_p, p.status)) break;
-        tc_fence_after();
+        mma_commit(smem_addr(&s_bar[it % Cfg::NBUF]));
+        return true;
+      };
+      // PV(j0 + it) = P . V with P (in S buffer it % NBUF) read from TMEM, into
+      // P.V accumulator it % NBUF.
+      auto issue_pv = [&](int it) {
+        const uint32_t sbuf = tmem + (it % Cfg::NBUF) * Cfg::S_BUF;
+        const uint32_t pvbuf = tmem + Cfg::PV_BASE + (it % Cfg::NBUF) * Cfg::PV_BUF;
+        const int j = j0 + it;
         const int nvb = min(BN / BK, (p.T - j * BN + BK - 1) / BK);
         for (int vb = 0; vb < nvb; ++vb) {
-          if (!mbar_wait(smem_addr(&vfull[rv.stage]), rv.phase, abort_p, p.status)) {
-            ok = false;
-            break;
-          }
+          if (!mbar_wait(smem_addr(&vfull[rv.stage]), rv.phase, abort_p, p.status)) return false;
           tc_fence_after();
           const uint32_t sa = v_addr(rv.stage);
 #pragma unroll
@@ -510,17 +516,39 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t vh = sdesc_kmajor_sw128(sa + kk * 32);
             if (SPLIT3) {
               // V^T hi and lo rows are contiguous: one B operand of 2*DHP rows.
-              mma_tf32_ts(tmem + Cfg::PV_BIG, tmem + Cfg::S_BIG + key, vh, IDESC_PV2, acc);
-              mma_tf32_ts(tmem + Cfg::PV_SMALL, tmem + Cfg::S_SMALL + key, vh, IDESC_PV, 1u);
+              mma_tf32_ts(pvbuf + Cfg::PV_BIG, sbuf + Cfg::S_BIG + key, vh, IDESC_PV2, acc);
+              mma_tf32_ts(pvbuf + Cfg::PV_SMALL, sbuf + Cfg::S_SMALL + key, vh, IDESC_PV, 1u);
             } else {
-              mma_tf32_ts(tmem + Cfg::PV_BIG, tmem + Cfg::S_BIG + key, vh, IDESC_PV, acc);
+              mma_tf32_ts(pvbuf + Cfg::PV_BIG, sbuf + Cfg::S_BIG + key, vh, IDESC_PV, acc);
             }
           }
           mma_commit(smem_addr(&vempty[rv.stage]));
           rv.advance();
         }
-        if (!ok) break;
-        mma_commit(smem_addr(&pv_bar));
+        mma_commit(smem_addr(&pv_bar[it % Cfg::NBUF]));
+        return true;
+      };
+      // Order: S(0); then per tile it: [S(it + 1) into the other buffer once
+      // PV(it - 1) has read the P it overwrites]; PV(it) once the softmax has
+      // written P(it).  With one buffer, S(it + 1) waits for PV(it) instead.
+      const int n = j1 - j0;
+      bool ok = n > 0 ? issue_s(0) : true;
+      for (int it = 0; ok && it < n; ++it) {
+        if (Cfg::NBUF == 2 && it + 1 < n) {
+          if (it >= 1 && !mbar_wait(smem_addr(&pv_bar[(it - 1) % 2]), ((it - 1) / 2) & 1,
+                                    abort_p, p.status))
+            break;
+          tc_fence_after();
+          if (!issue_s(it + 1)) break;
+        }
+        if (!mbar_wait(smem_addr(&p_bar), it & 1, abort_p, p.status)) break;
+        tc_fence_after();
+        if (!issue_pv(it)) break;
+        if (Cfg::NBUF == 1 && it + 1 < n) {
+          if (!mbar_wait(smem_addr(&pv_bar[0]), it & 1, abort_p, p.status)) break;
+          tc_fence_after();
+          if (!issue_s(it + 1)) break;
+        }
       }
       mma_commit(smem_addr(&final_bar));
       drain_wait(smem_addr(&final_bar), 0, p.status);
@@ -572,34 +600,91 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!conv) record_fail(0);
     }
+    // TMEM accesses: every wait covers two W-column loads -- the big and
+    // small halves of a 3xTF32 value, or two neighbouring 1xTF32 column
+    // blocks -- so few load latencies are exposed per tile.  W = 16 where the
+    // output row already takes 64 registers (head size > 64).
+    constexpr int W = DHP > 64 ? 16 : 32;
+    constexpr int SSTEP = SPLIT3 ? W : 2 * W;  // S columns per wait
+    static_assert(SCOLS % SSTEP == 0, "S columns per group");
+    // The P.V drain updates the output row in place: 16-column loads once
+    // that row takes 64 registers.
+    constexpr int WD = DHP > 64 ? 16 : 32;
+    constexpr int DSTEP = SPLIT3 ? WD : 2 * WD;  // output columns per wait
+    // Folds P.V of tile t (accumulator t % NBUF) into o with its rescale factor
+    // (o <- o * a + PV); false when the wait gave up.
+    auto drain_pv = [&](int t, float a) {
+      if (!mbar_wait(smem_addr(&pv_bar[t % Cfg::NBUF]), (t / Cfg::NBUF) & 1, abort_p, p.status))
+        return false;
+      tc_fence_after();
+      const uint32_t pvb = tmem + lane_off + Cfg::PV_BASE + (t % Cfg::NBUF) * Cfg::PV_BUF;
+      const int ncols = (c_hi - c_lo) * 32;  // this group's output columns
+#pragma unroll
+      for (int c0 = 0; c0 < CH0 * 32; c0 += DSTEP) {
+        if (c0 >= ncols) break;
+        const uint32_t col = c_lo * 32 + c0;
+        uint32_t va[WD], vb[WD];
+        if (SPLIT3) {
+          tmem_ld_pair<WD>(pvb + Cfg::PV_BIG + col, va, pvb + Cfg::PV_SMALL + col, vb);
+#pragma unroll
+          for (int i = 0; i < WD; ++i)
+            o[c0 + i] = fmaf(o[c0 + i], a, __uint_as_float(va[i]) + __uint_as_float(vb[i]));
+        } else if (c0 + 2 * WD <= ncols) {
+          tmem_ld_pair<WD>(pvb + col, va, pvb + col + WD, vb);
+#pragma unroll
+          for (int i = 0; i < WD; ++i) {
+            o[c0 + i] = fmaf(o[c0 + i], a, __uint_as_float(va[i]));
+            o[c0 + WD + i] = fmaf(o[c0 + WD + i], a, __uint_as_float(vb[i]));
+          }
+        } else {
+          tmem_ld_one<WD>(pvb + col, va);
+#pragma unroll
+          for (int i = 0; i < WD; ++i) o[c0 + i] = fmaf(o[c0 + i], a, __uint_as_float(va[i]));
+        }
+      }
+      tc_fence_before();
+      return true;
+    };
+    // With two accumulators, PV(t) is folded in during tile t + 1, after P(t + 1)
+    // has been handed over, so it overlaps the tensor core's next products.
+    constexpr bool DEFER = Cfg::NBUF == 2;
+    float alpha_prev = 1.f;
+    bool pending = false;  // a P.V tile not yet folded into o
     int it = 0;
     for (int j = j0; j < j1; ++j, ++it) {
-      const bool got_s = mbar_wait(smem_addr(&s_bar), it & 1, abort_p, p.status);
+      const uint32_t sbuf = tmem + lane_off + (it % Cfg::NBUF) * Cfg::S_BUF;
+      const bool got_s =
+          mbar_wait(smem_addr(&s_bar[it % Cfg::NBUF]), (it / Cfg::NBUF) & 1, abort_p, p.status);
       const int kbase = j * BN + g * SCOLS;
       const int kmax = p.causal ? min(p.T - 1, qrow) : p.T - 1;  // last valid key
-      // 16-column TMEM accesses, the big and small halves of a 3xTF32 score
-      // loaded together.  In 1xTF32 with head sizes up to 64 the row's scores
-      // also stay in registers between the max and the exponent passes (TMEM
-      // is read once); otherwise those registers are needed elsewhere.
-      constexpr bool KEEP_S = !SPLIT3 && DHP <= 64;
-      float sv[KEEP_S ? SCOLS : 1];
+      // Scores of this thread's row and columns, key c0 + i of a step in
+      // va[i] (+ vb[i] for 3xTF32) or, for 1xTF32, keys c0 + i and c0 + W + i.
+      // Both passes read them from TMEM; the steps stay rolled so one step's
+      // registers are free before the next step loads.
+      auto load_s = [&](int c0, uint32_t (&va)[W], uint32_t (&vb)[W]) {
+        const uint32_t col = g * SCOLS + c0;
+        if (SPLIT3)
+          tmem_ld_pair<W>(sbuf + Cfg::S_BIG + col, va, sbuf + Cfg::S_SMALL + col, vb);
+        else
+          tmem_ld_pair<W>(sbuf + Cfg::S_BIG + col, va, sbuf + Cfg::S_BIG + col + W, vb);
+      };
       float tmax = -INFINITY;
       if (got_s) {
         tc_fence_after();
+#pragma unroll 1
+        for (int c0 = 0; c0 < SCOLS; c0 += SSTEP) {
+          uint32_t va[W], vb[W];
+          load_s(c0, va, vb);
 #pragma unroll
-        for (int c = 0; c < SCOLS / 16; ++c) {
-          uint32_t sb[16], ss[16];
-          const uint32_t col = g * SCOLS + c * 16;
-          if (SPLIT3)
-            tmem_ld16x2(tmem + lane_off + Cfg::S_BIG + col, sb,
-                        tmem + lane_off + Cfg::S_SMALL + col, ss);
-          else
-            tmem_ld16(tmem + lane_off + Cfg::S_BIG + col, sb);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const float v = __uint_as_float(sb[i]) + (SPLIT3 ? __uint_as_float(ss[i]) : 0.f);
-            if constexpr (KEEP_S) sv[c * 16 + i] = v;
-            if (kbase + c * 16 + i <= kmax) tmax = fmaxf(tmax, v);
+          for (int i = 0; i < W; ++i) {
+            if (SPLIT3) {
+              const float v = __uint_as_float(va[i]) + __uint_as_float(vb[i]);
+              if (kbase + c0 + i <= kmax) tmax = fmaxf(tmax, v);
+            } else {
+              const float v0 = __uint_as_float(va[i]), v1 = __uint_as_float(vb[i]);
+              if (kbase + c0 + i <= kmax) tmax = fmaxf(tmax, v0);
+              if (kbase + c0 + W + i <= kmax) tmax = fmaxf(tmax, v1);
+            }
           }
         }
       } else {
@@ -611,32 +696,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmax = fmaxf(tmax, red[g ^ 1][r]);
       const float m_new = fmaxf(m, tmax);
       float lsum = 0.f;
+      // P = 2^(s - m_new) (0 past the last valid key), split into tf32 hi and
+      // the fp32 remainder for 3xTF32.
+      auto p_of = [&](float v, int key, float& lo) {
+        const float pv = key <= kmax ? fast_exp2(v - m_new) : 0.f;
+        lsum += pv;
+        const float hi = tf32_round(pv);
+        lo = pv - hi;
+        return hi;
+      };
+#pragma unroll 1
+      for (int c0 = 0; c0 < SCOLS; c0 += SSTEP) {
+        uint32_t va[W], vb[W];
+        const uint32_t col = g * SCOLS + c0;
+        load_s(c0, va, vb);
 #pragma unroll
-      for (int c = 0; c < SCOLS / 16; ++c) {
-        uint32_t sb[16], ss[16];
-        const uint32_t col = g * SCOLS + c * 16;
-        if constexpr (!KEEP_S) {
-          if (SPLIT3)
-            tmem_ld16x2(tmem + lane_off + Cfg::S_BIG + col, sb,
-                        tmem + lane_off + Cfg::S_SMALL + col, ss);
-          else
-            tmem_ld16(tmem + lane_off + Cfg::S_BIG + col, sb);
+        for (int i = 0; i < W; ++i) {
+          float lo;
+          if (SPLIT3) {
+            const float v = __uint_as_float(va[i]) + __uint_as_float(vb[i]);
+            va[i] = __float_as_uint(p_of(v, kbase + c0 + i, lo));
+            vb[i] = __float_as_uint(lo);
+          } else {
+            const float v0 = __uint_as_float(va[i]), v1 = __uint_as_float(vb[i]);
+            va[i] = __float_as_uint(p_of(v0, kbase + c0 + i, lo));
+            vb[i] = __float_as_uint(p_of(v1, kbase + c0 + W + i, lo));
+          }
         }
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float v;
-          if constexpr (KEEP_S)
-            v = sv[c * 16 + i];
-          else
-            v = __uint_as_float(sb[i]) + (SPLIT3 ? __uint_as_float(ss[i]) : 0.f);
-          const float pv = (kbase + c * 16 + i <= kmax) ? fast_exp2(v - m_new) : 0.f;
-          lsum += pv;
-          const float hi = tf32_round(pv);
-          sb[i] = __float_as_uint(hi);
-          ss[i] = __float_as_uint(pv - hi);
+        if (SPLIT3) {
+          tmem_st_w<W>(sbuf + Cfg::S_BIG + col, va);
+          tmem_st_w<W>(sbuf + Cfg::S_SMALL + col, vb);
+        } else {
+          tmem_st_w<W>(sbuf + Cfg::S_BIG + col, va);
+          tmem_st_w<W>(sbuf + Cfg::S_BIG + col + W, vb);
         }
-        tmem_st16(tmem + lane_off + Cfg::S_BIG + col, sb);
-        if (SPLIT3) tmem_st16(tmem + lane_off + Cfg::S_SMALL + col, ss);
       }
       tmem_wait_st();
       tc_fence_before();
@@ -645,28 +738,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
       l = l * alpha + lsum;
       m = m_new;
-      if (!mbar_wait(smem_addr(&pv_bar), it & 1, abort_p, p.status)) {
+      // o holds the P.V tiles up to it - 2 (DEFER) or it - 1, relative to the
+      // running max of that tile; alpha_prev / alpha bring it to the next.
+      if (DEFER && pending && !drain_pv(it - 1, alpha_prev)) {
         record_fail(it + 1);  // acted on at the next exchange (or after the loop)
+        pending = false;
         continue;
       }
-      tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < 2 * CH0; ++c) {
-        if (2 * c_lo + c >= 2 * c_hi) break;
-        uint32_t vb[16], vs[16];
-        const uint32_t col = c_lo * 32 + c * 16;
-        if (SPLIT3)
-          tmem_ld16x2(tmem + lane_off + Cfg::PV_BIG + col, vb,
-                      tmem + lane_off + Cfg::PV_SMALL + col, vs);
-        else
-          tmem_ld16(tmem + lane_off + Cfg::PV_BIG + col, vb);
-#pragma unroll
-        for (int i = 0; i < 16; ++i)
-          o[c * 16 + i] = fmaf(o[c * 16 + i], alpha,
-                               __uint_as_float(vb[i]) + (SPLIT3 ? __uint_as_float(vs[i]) : 0.f));
+      if (DEFER) {
+        alpha_prev = alpha;
+        pending = true;
+      } else if (!drain_pv(it, alpha)) {
+        record_fail(it + 1);
       }
-      tc_fence_before();
     }
+    // The last P.V tile of the deferred schedule (only on the normal exit).
+    if (DEFER && pending && it == j1 - j0 && !drain_pv(it - 1, alpha_prev)) softmax_failed = 1;
     // Rows are owned one per thread pair, so the output tile is staged in the
     // (now idle) shared-memory rings and written with TMA stores (or row by
     // row when the output view does not allow TMA); split tiles are staged

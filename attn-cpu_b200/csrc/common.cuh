@@ -321,6 +321,28 @@ __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16
       : "memory");
 }
 
+// Width-generic forms (16 or 32 columns per access) for code templated on
+// how many registers it can spend on one load.
+template <int W>
+__device__ __forceinline__ void tmem_ld_pair(uint32_t ta, uint32_t (&a)[W], uint32_t tb,
+                                             uint32_t (&b)[W]) {
+  static_assert(W == 16 || W == 32, "16 or 32 columns");
+  if constexpr (W == 32) tmem_ld32x2(ta, a, tb, b);
+  else tmem_ld16x2(ta, a, tb, b);
+}
+template <int W>
+__device__ __forceinline__ void tmem_ld_one(uint32_t ta, uint32_t (&a)[W]) {
+  static_assert(W == 16 || W == 32, "16 or 32 columns");
+  if constexpr (W == 32) tmem_ld32(ta, a);
+  else tmem_ld16(ta, a);
+}
+template <int W>
+__device__ __forceinline__ void tmem_st_w(uint32_t ta, const uint32_t (&a)[W]) {
+  static_assert(W == 16 || W == 32, "16 or 32 columns");
+  if constexpr (W == 32) tmem_st32(ta, a);
+  else tmem_st16(ta, a);
+}
+
 // Shared-memory matrix descriptor for a K-major tile stored with the 128-byte
 // swizzle: rows of 128 bytes (32 fp32), 8-row groups 1024 bytes apart.  The
 // tile base must be 1024-byte aligned; stepping K by 8 tf32 elements inside the
