@@ -472,7 +472,7 @@ def cpu_sample(w: str, budget_s: float):
     import oracle
 
     kind = "reference" if oracle.ref_available() else "port"
-    cores = os.cpu_count() or 1
+    cores = int(os.environ.get("OMP_NUM_THREADS") or os.cpu_count() or 1)
     c = WORKLOADS[w]
     rng = np.random.default_rng(0)
     if w == "prefill":
@@ -529,7 +529,10 @@ def run_reference_arm(args):
     if rank != 0:
         return
     w = args.workload
-    os.environ.setdefault("OMP_NUM_THREADS", str(os.cpu_count() or 1))
+    # All host threads for the reference's OpenMP code: torchrun sets
+    # OMP_NUM_THREADS=1 for its workers, and rank 0 runs alone here.  Set
+    # before the compiled reference (and its OpenMP runtime) is loaded.
+    os.environ["OMP_NUM_THREADS"] = str(len(os.sched_getaffinity(0)) or os.cpu_count() or 1)
     os.environ.setdefault("OMP_PROC_BIND", "close")
     per = max(1.0, args.cpu_seconds / max(1, args.steps))
     vals = []
