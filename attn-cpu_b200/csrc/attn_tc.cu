@@ -48,26 +48,38 @@ constexpr int kMaxSplits = 8;  // key splits of a query tile: one portable clust
 // Fused form: V slices split by warp 0 (the rest by the eight softmax warps).
 constexpr int kVSlicesWarp0 = 2;
 
-template <int DHP, bool SPLIT3>
+// QRES: the CTA's Q tile is loaded once and stays in shared memory, and the
+// S ring carries K slices only (deeper for the same bytes).  Used by the
+// multi-tile 1xTF32 form; 3xTF32 needs the bytes for its lo parts.
+template <int DHP, bool SPLIT3, bool QRESIDENT = false>
 struct AttnCfg {
+  static constexpr bool QRES = QRESIDENT;
   static constexpr int NKB = DHP / BK;       // K slices of the S product
   static constexpr int NPART = SPLIT3 ? 2 : 1;
   static constexpr int QBOX = BM * BK * 4;   // 16 KB
   static constexpr int KBOX = BN * BK * 4;   // 16 KB
   static constexpr int VBOX = DHP * BK * 4;  // 32 keys of V^T
-  // Two rings: Q+K slices for the S product, V^T slices for the PV product,
-  // so all of a tile's V slices can be in flight while S and the softmax run.
-  static constexpr int S_STAGE = NPART * (QBOX + KBOX);
-  // S stage: Q hi | K hi | K lo | Q lo, so that K hi and K lo form one
+  static constexpr int BUDGET = 225 * 1024;
+  // Resident Q: hi slices kb at kb * QBOX, lo slices at (NKB + kb) * QBOX.
+  static constexpr int Q_BYTES = QRES ? NPART * NKB * QBOX : 0;
+  // Two rings: Q+K (or K) slices for the S product, V^T slices for the PV
+  // product, so all of a tile's V slices can be in flight while S and the
+  // softmax run.
+  static constexpr int S_STAGE = QRES ? NPART * KBOX : NPART * (QBOX + KBOX);
+  // S stage: [Q hi |] K hi | K lo [| Q lo], so that K hi and K lo form one
   // 256-row B operand ([Qh.Kh | Qh.Kl] in a single N = 256 MMA).
-  static constexpr int OFF_KH = QBOX;
-  static constexpr int OFF_KL = QBOX + KBOX;
+  static constexpr int OFF_KH = QRES ? 0 : QBOX;
+  static constexpr int OFF_KL = OFF_KH + KBOX;
   static constexpr int OFF_QL = QBOX + 2 * KBOX;
-  static constexpr int S_STAGES = SPLIT3 ? 2 : 4;
   static constexpr int V_STAGE = NPART * VBOX;
-  static constexpr int V_STAGES_FIT = (225 * 1024 - S_STAGES * S_STAGE) / V_STAGE;
-  static constexpr int V_STAGES = V_STAGES_FIT < 4 ? V_STAGES_FIT : 4;
-  static constexpr int RING_BYTES = S_STAGES * S_STAGE + V_STAGES * V_STAGE;
+  static constexpr int S_STAGES_FIT = (BUDGET - Q_BYTES - 4 * V_STAGE) / S_STAGE;
+  static constexpr int S_STAGES = !QRES ? (SPLIT3 ? 2 : 4) : (S_STAGES_FIT < 8 ? S_STAGES_FIT : 8);
+  static constexpr int V_STAGES_FIT = (BUDGET - Q_BYTES - S_STAGES * S_STAGE) / V_STAGE;
+  static constexpr int V_CAP = QRES ? 8 : 4;
+  static constexpr int V_STAGES = V_STAGES_FIT < V_CAP ? V_STAGES_FIT : V_CAP;
+  static constexpr int S_RING = Q_BYTES;                          // offset of the S ring
+  static constexpr int V_RING = S_RING + S_STAGES * S_STAGE;      // offset of the V ring
+  static constexpr int RING_BYTES = V_RING + V_STAGES * V_STAGE;
   static constexpr int SMEM = RING_BYTES + 1024;
   // Fused form: raw V rows of the tile's key slices staged past the rings.
   static constexpr int SMEM_FUSED = RING_BYTES + (BN / BK) * VBOX + 1024;
@@ -91,8 +103,9 @@ struct AttnCfg {
   static constexpr int PV_SMALL = DHP;
   static constexpr int TMEM_COLS = 512;
   static_assert(DHP % 32 == 0 && DHP <= 128, "head size padded to 32..128");
-  static_assert(V_STAGES >= 2, "V ring needs two stages");
-  static_assert(BM * (DHP + 1) * 4 <= S_STAGES * S_STAGE, "output staging fits the S ring");
+  static_assert(V_STAGES >= 2 && S_STAGES >= 2, "rings need two stages");
+  static_assert(!QRES || !SPLIT3, "resident Q is a 1xTF32 layout");
+  static_assert(BM * (DHP + 1) * 4 <= RING_BYTES, "output staging fits the rings");
   static_assert(RECV + BM * OP * 4 <= RING_BYTES, "merge staging fits the rings");
   static_assert(NBUF * (S_BUF + PV_BUF) <= TMEM_COLS, "TMEM budget");
 };
@@ -192,7 +205,7 @@ __device__ __forceinline__ void fused_split_v_slice(uint8_t* ring, int vb, int l
                                                     int gstep) {
   using Cfg = AttnCfg<DHP, SPLIT3>;
   const uint8_t* raw = ring + Cfg::RING_BYTES + vb * Cfg::VBOX;
-  uint8_t* st = ring + Cfg::S_STAGES * Cfg::S_STAGE + vb * Cfg::V_STAGE;
+  uint8_t* st = ring + Cfg::V_RING + vb * Cfg::V_STAGE;
 #pragma unroll 4
   for (int gi = gi0; gi < DHP / 4; gi += gstep) {
     const int bx = gi >> 3, c = gi & 7;
@@ -222,11 +235,11 @@ __device__ __forceinline__ void fused_split_v_slice(uint8_t* ring, int vb, int l
 // stores them; the 256 threads of warps 2-9 take (row, 4 columns) items, so
 // consecutive threads write consecutive output columns.  Nothing is stored
 // when any split reported a failed wait.
-template <int DHP, bool SPLIT3>
+template <int DHP, bool SPLIT3, bool QRES>
 __device__ __forceinline__ void cluster_merge(uint32_t base, uint32_t recv_bar,
                                               const AttnParams& p, int qt, int h,
                                               volatile int* abort_p) {
-  using Cfg = AttnCfg<DHP, SPLIT3>;
+  using Cfg = AttnCfg<DHP, SPLIT3, QRES>;
   constexpr int C4 = DHP / 4;
   const int ns = p.nsplit;
   const int me = (int)cluster_ctarank();
@@ -308,7 +321,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                    const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
                    const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
                    const __grid_constant__ CUtensorMap tmO, const AttnParams p) {
-  using Cfg = AttnCfg<DHP, SPLIT3>;
+  using Cfg = AttnCfg<DHP, SPLIT3, !SPLIT3 && !FUSED>;
   constexpr int SST = Cfg::S_STAGES, VST = Cfg::V_STAGES;
   static_assert(!FUSED || (Cfg::NKB <= SST && BN / BK <= VST && Cfg::SMEM_FUSED <= 227 * 1024),
                 "fused form: one stage per slice of the single key tile");
@@ -325,7 +338,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t sfull[SST], sempty[SST], vfull[VST], vempty[VST];
-  __shared__ __align__(8) uint64_t s_bar[2], p_bar, pv_bar[2], final_bar, recv_bar;
+  __shared__ __align__(8) uint64_t s_bar[2], p_bar, pv_bar[2], final_bar, recv_bar, q_bar;
   __shared__ __align__(8) uint64_t rbar[FUSED ? 8 : 1];  // fused: raw Q/K (per slice), V slices
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
@@ -334,8 +347,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, split = blockIdx.y, h = blockIdx.z;
   const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
-  auto s_addr = [&](int st) { return base + st * Cfg::S_STAGE; };
-  auto v_addr = [&](int st) { return base + SST * Cfg::S_STAGE + st * Cfg::V_STAGE; };
+  auto s_addr = [&](int st) { return base + Cfg::S_RING + st * Cfg::S_STAGE; };
+  auto v_addr = [&](int st) { return base + Cfg::V_RING + st * Cfg::V_STAGE; };
 
   // Key tiles of this CTA.
   int n_kv = (p.T + BN - 1) / BN;
@@ -366,6 +379,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_addr(&p_bar), 8);  // one arrival per softmax warp
     mbar_init(smem_addr(&final_bar), 1);
     mbar_init(smem_addr(&recv_bar), 1);
+    mbar_init(smem_addr(&q_bar), 1);
     if (FUSED)
       for (int i = 0; i < 8; ++i) mbar_init(smem_addr(&rbar[i]), 1);
     fence_barrier_init();
@@ -382,7 +396,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   grid_dep_wait();  // packed operands (or, fused, the raw ones) come from earlier kernels
 
   if (warp == 0) {
-    if (FUSED && j0 < j1) {
+    if constexpr (FUSED) if (j0 < j1) {
       // ----------------------------------------------- raw loads (fused form)
       // Lane 0 loads the only key tile's Q/K slices into the S stages' hi
       // slots and its V rows (32 keys x 32 columns per box) into the staging
@@ -424,6 +438,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmQh);
       tma_prefetch_desc(&tmKh);
       tma_prefetch_desc(&tmVh);
+      const bool load_q = Cfg::QRES && j0 < j1;
+      if (load_q) {
+        // The CTA's Q tile, once: hi slices kb at base + kb * QBOX.
+        const uint32_t qb = smem_addr(&q_bar);
+        mbar_arrive_expect_tx(qb, Cfg::Q_BYTES);
+        for (int kb = 0; kb < Cfg::NKB; ++kb)
+          tma_load_3d(base + kb * Cfg::QBOX, &tmQh, qb, kb * BK, qt * BM, h);
+      }
       Ring<SST> rs;
       Ring<VST> rv;
       bool ok = true;
@@ -435,7 +457,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t fb = smem_addr(&sfull[rs.stage]), sa = s_addr(rs.stage);
           mbar_arrive_expect_tx(fb, Cfg::S_STAGE);
-          tma_load_3d(sa, &tmQh, fb, kb * BK, qt * BM, h);
+          if (!Cfg::QRES) tma_load_3d(sa, &tmQh, fb, kb * BK, qt * BM, h);
           tma_load_3d(sa + Cfg::OFF_KH, &tmKh, fb, kb * BK, j * BN, h);
           if (SPLIT3) {
             tma_load_3d(sa + Cfg::OFF_QL, &tmQl, fb, kb * BK, qt * BM, h);
@@ -458,6 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           rv.advance();
         }
       }
+      if (load_q) drain_wait(smem_addr(&q_bar), 0, p.status);
       // Copies still in flight (only possible after an abort) land before exit.
       for (int i = 0; i < SST; ++i)
         if (rs.issued_mask & (1u << i))
@@ -472,16 +495,22 @@ __global__ void __launch_bounds__(kThreads, 1)
       Ring<SST> rs;
       Ring<VST> rv;
       // S(j0 + it) into S buffer it % NBUF.
+      bool q_ready = !Cfg::QRES;
       auto issue_s = [&](int it) {
         const uint32_t sbuf = tmem + (it % Cfg::NBUF) * Cfg::S_BUF;
+        if (!q_ready) {
+          if (!mbar_wait(smem_addr(&q_bar), 0, abort_p, p.status)) return false;
+          q_ready = true;
+        }
         for (int kb = 0; kb < Cfg::NKB; ++kb) {
           if (!mbar_wait(smem_addr(&sfull[rs.stage]), rs.phase, abort_p, p.status)) return false;
           tc_fence_after();
           const uint32_t sa = s_addr(rs.stage);
+          const uint32_t qa = Cfg::QRES ? base + kb * Cfg::QBOX : sa;
 #pragma unroll
           for (int kk = 0; kk < BK / 8; ++kk) {
             const uint32_t acc = (kb | kk) != 0 ? 1u : 0u;
-            const uint64_t qh = sdesc_kmajor_sw128(sa + kk * 32);
+            const uint64_t qh = sdesc_kmajor_sw128(qa + kk * 32);
             const uint64_t kh = sdesc_kmajor_sw128(sa + Cfg::OFF_KH + kk * 32);
             if (SPLIT3) {
               // [S_BIG | S_SMALL] (+)= Qh . [Kh | Kl]^T, then S_SMALL += Ql . Kh^T.
@@ -587,7 +616,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       fail_slot[slot & 1] = 1;
       softmax_failed = 1;
     };
-    if (FUSED && j0 < j1) {
+    if constexpr (FUSED) if (j0 < j1) {
       bool conv = fused_split_qk<DHP, SPLIT3>(ring, rbar, sfull, threadIdx.x - 64, p.qscale,
                                               abort_p, p.status);
       const int nvb = min(BN / BK, (p.T - j0 * BN + BK - 1) / BK);
@@ -855,7 +884,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   // are done reading it.  Every thread passes both barriers.
   if (p.nsplit > 1) {
     cluster_sync_all();
-    if (warp >= 2) cluster_merge<DHP, SPLIT3>(base, smem_addr(&recv_bar), p, qt, h, abort_p);
+    if (warp >= 2)
+      cluster_merge<DHP, SPLIT3, Cfg::QRES>(base, smem_addr(&recv_bar), p, qt, h, abort_p);
     cluster_sync_all();
   }
 
@@ -870,7 +900,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 template <int DHP, bool SPLIT3, bool FUSED>
 void launch_attn(const CUtensorMap* maps, const AttnParams& prm, int qtiles, cudaStream_t s) {
-  using Cfg = AttnCfg<DHP, SPLIT3>;
+  using Cfg = AttnCfg<DHP, SPLIT3, !SPLIT3 && !FUSED>;
   static std::atomic<uint64_t> configured{0};
   int dev = 0;
   ATTNB_CUDA(cudaGetDevice(&dev));
