@@ -89,6 +89,7 @@ struct AttnCfg {
   // of the tile behind them.
   static constexpr int OP = DHP + 4;
   static constexpr int RECV = BM * OP * 4;
+  static constexpr int WTS = 2 * BM * OP * 4;  // per-row split weights, [64][8] floats
   // TMEM: NBUF S buffers ([big | small] key columns each), then NBUF P.V
   // accumulators ([big | small] head columns).  Two of each when they fit
   // (1xTF32): S(j+1) then runs during the softmax of tile j, and PV(j) is
@@ -106,7 +107,7 @@ struct AttnCfg {
   static_assert(V_STAGES >= 2 && S_STAGES >= 2, "rings need two stages");
   static_assert(!QRES || !SPLIT3, "resident Q is a 1xTF32 layout");
   static_assert(BM * (DHP + 1) * 4 <= RING_BYTES, "output staging fits the rings");
-  static_assert(RECV + BM * OP * 4 <= RING_BYTES, "merge staging fits the rings");
+  static_assert(WTS + 64 * 8 * 4 <= RING_BYTES, "merge staging fits the rings");
   static_assert(NBUF * (S_BUF + PV_BUF) <= TMEM_COLS, "TMEM budget");
 };
 
@@ -238,7 +239,7 @@ __device__ __forceinline__ void fused_split_v_slice(uint8_t* ring, int vb, int l
 template <int DHP, bool SPLIT3, bool QRES>
 __device__ __forceinline__ void cluster_merge(uint32_t base, uint32_t recv_bar,
                                               const AttnParams& p, int qt, int h,
-                                              volatile int* abort_p) {
+                                              volatile int* abort_p, int* merge_fail) {
   using Cfg = AttnCfg<DHP, SPLIT3, QRES>;
   constexpr int C4 = DHP / 4;
   const int ns = p.nsplit;
@@ -260,7 +261,10 @@ __device__ __forceinline__ void cluster_merge(uint32_t base, uint32_t recv_bar,
       static_cast<const uint8_t*>(__cvta_shared_to_generic(base)));
   const float* recv = own + Cfg::RECV / 4;
   // Every split's rows carry its validity flag (the first row's suffices).
-  bool valid = mbar_wait(recv_bar, 0, abort_p, p.status);
+  // The decision is shared by all 256 threads (they meet at barriers below).
+  if (!mbar_wait(recv_bar, 0, abort_p, p.status)) *merge_fail = 1;
+  named_bar_sync(1, 256);
+  bool valid = *merge_fail == 0;
   for (int s = 0; valid && s < ns; ++s) {
     const float* first = s == me ? own : recv + (s < me ? s : s - 1) * rows_per * Cfg::OP;
     valid = first[DHP + 2] != 0.f;
@@ -277,34 +281,47 @@ __device__ __forceinline__ void cluster_merge(uint32_t base, uint32_t recv_bar,
   const int vrows = min(nrows, p.L - qt * BM - row0);  // rows inside the output
   const bool vec = p.osD == 1 && (p.osT & 3) == 0 && (p.osH & 3) == 0 &&
                    (reinterpret_cast<uintptr_t>(p.O) & 15u) == 0;
+  auto row_of = [&](int s, int lr) {
+    return s == me ? own + (row0 + lr) * Cfg::OP
+                   : recv + ((s < me ? s : s - 1) * rows_per + lr) * Cfg::OP;
+  };
+  // Per row, once: the weight of each split, 2^(m_s - m_*) / sum_s 2^(m_s - m_*) l_s
+  // (rows_per <= 64 rows of kMaxSplits floats, behind the receive area).
+  float(*wts)[kMaxSplits] = reinterpret_cast<float(*)[kMaxSplits]>(
+      static_cast<uint8_t*>(__cvta_shared_to_generic(base)) + Cfg::WTS);
+  for (int lr = threadIdx.x - 64; lr < vrows; lr += 256) {
+    float mstar = -INFINITY;
+    for (int s = 0; s < ns; ++s) mstar = fmaxf(mstar, row_of(s, lr)[DHP]);
+    float w[kMaxSplits], lsum = 0.f;
+#pragma unroll
+    for (int s = 0; s < kMaxSplits; ++s) {
+      if (s >= ns) break;
+      const float2 ml = *reinterpret_cast<const float2*>(row_of(s, lr) + DHP);
+      w[s] = ml.x == -INFINITY ? 0.f : fast_exp2(ml.x - mstar);
+      lsum = fmaf(w[s], ml.y, lsum);
+    }
+    const float inv = 1.f / lsum;
+#pragma unroll
+    for (int s = 0; s < kMaxSplits; ++s)
+      if (s < ns) wts[lr][s] = w[s] * inv;
+  }
+  named_bar_sync(1, 256);
   for (int item = threadIdx.x - 64; item < vrows * C4; item += 256) {
     const int lr = item / C4, d = (item % C4) * 4;
-    auto row_of = [&](int s) {
-      return s == me ? own + (row0 + lr) * Cfg::OP
-                     : recv + ((s < me ? s : s - 1) * rows_per + lr) * Cfg::OP;
-    };
-    float mstar = -INFINITY;
-    for (int s = 0; s < ns; ++s) mstar = fmaxf(mstar, row_of(s)[DHP]);
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float lsum = 0.f;
     for (int s = 0; s < ns; ++s) {
-      const float* rs = row_of(s);
-      const float2 ml = *reinterpret_cast<const float2*>(rs + DHP);
-      const float w = ml.x == -INFINITY ? 0.f : fast_exp2(ml.x - mstar);
-      const float4 v = *reinterpret_cast<const float4*>(rs + d);
-      lsum = fmaf(w, ml.y, lsum);
+      const float w = wts[lr][s];
+      const float4 v = *reinterpret_cast<const float4*>(row_of(s, lr) + d);
       acc.x = fmaf(w, v.x, acc.x);
       acc.y = fmaf(w, v.y, acc.y);
       acc.z = fmaf(w, v.z, acc.z);
       acc.w = fmaf(w, v.w, acc.w);
     }
-    const float inv = 1.f / lsum;
     float* orow = p.O + h * p.osH + (int64_t)(qt * BM + row0 + lr) * p.osT;
     if (vec && d + 3 < p.Dh) {
-      *reinterpret_cast<float4*>(orow + d) =
-          make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+      *reinterpret_cast<float4*>(orow + d) = acc;
     } else {
-      const float v[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
+      const float v[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
       for (int k = 0; k < 4; ++k)
         if (d + k < p.Dh) orow[(int64_t)(d + k) * p.osD] = v[k];
@@ -343,6 +360,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   __shared__ int softmax_failed;  // any softmax thread saw a wait fail
+  __shared__ int merge_fail;      // a split-merge wait failed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, split = blockIdx.y, h = blockIdx.z;
@@ -362,6 +380,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     abort_flag = 0;
     softmax_failed = 0;
+    merge_fail = 0;
     // Full barriers: one TMA arrival with a byte count, or in the fused form
     // (whose stages are each filled once) one arrival per splitting warp.
     for (int i = 0; i < SST; ++i) {
@@ -885,7 +904,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (p.nsplit > 1) {
     cluster_sync_all();
     if (warp >= 2)
-      cluster_merge<DHP, SPLIT3, Cfg::QRES>(base, smem_addr(&recv_bar), p, qt, h, abort_p);
+      cluster_merge<DHP, SPLIT3, Cfg::QRES>(base, smem_addr(&recv_bar), p, qt, h, abort_p,
+                                            &merge_fail);
     cluster_sync_all();
   }
 
