@@ -346,6 +346,289 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// K1f: one tile per CTA, operand split fused in.
+//
+// When the 128 x BN output tiles number at most the SM count, the packing pass
+// and the L2 traffic of the packed copies (hi and lo, re-read by every tile of
+// a row or column) cost as much as the MMAs.  This form TMA-loads the raw fp32
+// slices -- A as [128 rows x 32 k]; B as [BN rows x 32 k] when K-major, or as
+// (BN/32) boxes of [32 k x 32 columns] staged and transposed when N-major --
+// and the four epilogue warps split them into the tf32 hi / fp32 lo operand
+// slots while the MMAs run: eight warps (2-9), the four epilogue warps among
+// them.  In 3xTF32 every 256-K chunk gets its own TMEM accumulator pair (at
+// most 512 / (2 BN) chunks), drained once at the end, so those warps have
+// nothing else to do during the loop.
+constexpr int kFusedThreads = 320;
+// hi = tf32 round-to-nearest of x (exact as a tf32 operand), lo = x - hi
+// (exact in fp32).
+__device__ __forceinline__ void split4(float4 x, float4& hi, float4& lo) {
+  hi = make_float4(tf32_round(x.x), tf32_round(x.y), tf32_round(x.z), tf32_round(x.w));
+  lo = make_float4(x.x - hi.x, x.y - hi.y, x.z - hi.z, x.w - hi.w);
+}
+
+template <int BN, bool SPLIT3, bool B_KMAJOR>
+struct FusedCfg {
+  static constexpr int NPART = SPLIT3 ? 2 : 1;
+  static constexpr int A_BYTES = BM * BK * 4;  // 16 KB
+  static constexpr int B_BYTES = BN * BK * 4;
+  static constexpr int RAW_B = B_KMAJOR ? 0 : BK * BN * 4;  // N-major B staging
+  static constexpr int OFF_A_LO = A_BYTES;
+  static constexpr int OFF_B_HI = NPART * A_BYTES;
+  static constexpr int OFF_B_LO = OFF_B_HI + B_BYTES;  // follows B_hi: one [B_hi | B_lo] operand
+  static constexpr int OFF_RAW = NPART * (A_BYTES + B_BYTES);
+  static constexpr int STAGE_BYTES = OFF_RAW + RAW_B;
+  static constexpr int STAGES_FIT = (200 * 1024) / STAGE_BYTES;
+  static constexpr int STAGES = STAGES_FIT < 6 ? STAGES_FIT : 6;
+  static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;
+  static constexpr int SLOT_COLS = NPART * BN;  // one chunk's [big | small] accumulators
+  static constexpr int MAX_CHUNKS = SPLIT3 ? 512 / SLOT_COLS : 1;
+  static constexpr int TMEM_COLS = SPLIT3 ? 512 : (BN < 32 ? 32 : BN);
+  static_assert(STAGES >= 2, "pipeline needs two stages");
+};
+
+template <int BN, bool SPLIT3, bool B_KMAJOR>
+__global__ void __launch_bounds__(kFusedThreads, 1)
+    gemm_fused_kernel(const __grid_constant__ CUtensorMap tmA,
+                      const __grid_constant__ CUtensorMap tmB, int M, int N, int K,
+                      float* __restrict__ C, int64_t ldc, float alpha, float beta,
+                      const float* __restrict__ bias, int* status) {
+  using Cfg = FusedCfg<BN, SPLIT3, B_KMAJOR>;
+  constexpr int STAGES = Cfg::STAGES;
+  constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+  constexpr uint32_t IDESC2 = idesc_tf32(BM, 2 * BN);  // A_hi . [B_hi | B_lo]
+  static_assert(!SPLIT3 || 2 * BN <= 256, "double-width MMA: N <= 256");
+  static_assert(Cfg::MAX_CHUNKS * Cfg::SLOT_COLS <= Cfg::TMEM_COLS, "chunk slots fit TMEM");
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[STAGES], conv_bar[STAGES], empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t tfull_bar, final_bar;
+  __shared__ uint32_t tmem_slot;
+  __shared__ int abort_flag;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
+  uint8_t* sbase = smem_raw + (base - smem_addr(smem_raw));
+  auto stage_addr = [&](int s) { return base + s * Cfg::STAGE_BYTES; };
+  const int tiles_m = (M + BM - 1) / BM, tiles_n = (N + BN - 1) / BN;
+  int tm, tn;
+  tile_coords(blockIdx.x, tiles_m, tiles_n, tm, tn);
+  const int nkb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    abort_flag = 0;
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_addr(&full_bar[s]), 1);
+      mbar_init(smem_addr(&conv_bar[s]), 8);  // one arrival per converting warp
+      mbar_init(smem_addr(&empty_bar[s]), 1);
+    }
+    mbar_init(smem_addr(&tfull_bar), 1);
+    mbar_init(smem_addr(&final_bar), 1);
+    fence_barrier_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_addr(&tmem_slot), Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_slot;
+  volatile int* abort_p = &abort_flag;
+  grid_dep_wait();  // the operands may come from the kernel before this one
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ------------------------------------------------- producer (raw fp32)
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      int stage = 0;
+      uint32_t phase = 0, issued_mask = 0, issued_parity = 0;
+      for (int kb = 0; kb < nkb; ++kb) {
+        if (!mbar_wait(smem_addr(&empty_bar[stage]), phase ^ 1u, abort_p, status)) break;
+        const uint32_t fb = smem_addr(&full_bar[stage]), sa = stage_addr(stage);
+        mbar_arrive_expect_tx(fb, Cfg::A_BYTES + (B_KMAJOR ? Cfg::B_BYTES : Cfg::RAW_B));
+        tma_load_2d(sa, &tmA, fb, kb * BK, tm * BM);
+        if (B_KMAJOR) {
+          tma_load_2d(sa + Cfg::OFF_B_HI, &tmB, fb, kb * BK, tn * BN);
+        } else {
+#pragma unroll
+          for (int bx = 0; bx < BN / 32; ++bx)
+            tma_load_2d(sa + Cfg::OFF_RAW + bx * 4096, &tmB, fb, tn * BN + bx * 32, kb * BK);
+        }
+        issued_mask |= 1u << stage;
+        issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      // Copies still in flight (only possible after an abort) land before exit.
+      for (int s = 0; s < STAGES; ++s)
+        if (issued_mask & (1u << s))
+          mbar_drain(smem_addr(&full_bar[s]), (issued_parity >> s) & 1u, status);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---------------------------------------------------------- MMA issuer
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = 0; ok && kb < nkb; ++kb) {
+        if (!mbar_wait(smem_addr(&conv_bar[stage]), phase, abort_p, status)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sa = stage_addr(stage);
+        // 3xTF32: chunk kb / KB_CHUNK accumulates into its own slot.
+        const int c = SPLIT3 ? kb / KB_CHUNK : 0;
+        const bool first = SPLIT3 ? (kb % KB_CHUNK) == 0 : kb == 0;
+        const uint32_t d_big = tmem + c * Cfg::SLOT_COLS, d_small = d_big + BN;
+#pragma unroll
+        for (int kk = 0; kk < BK / 8; ++kk) {
+          const uint32_t acc = (!first || kk != 0) ? 1u : 0u;
+          const uint64_t a_hi = sdesc_kmajor_sw128(sa + kk * 32);
+          const uint64_t b_hi = sdesc_kmajor_sw128(sa + Cfg::OFF_B_HI + kk * 32);
+          if (SPLIT3) {
+            const uint64_t a_lo = sdesc_kmajor_sw128(sa + Cfg::OFF_A_LO + kk * 32);
+            mma_tf32(d_big, a_hi, b_hi, IDESC2, acc);
+            mma_tf32(d_small, a_lo, b_hi, IDESC, 1u);
+          } else {
+            mma_tf32(d_big, a_hi, b_hi, IDESC, acc);
+          }
+        }
+        mma_commit(smem_addr(&empty_bar[stage]));
+        if (++stage == STAGES) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (ok) mma_commit(smem_addr(&tfull_bar));
+      // Every MMA issued above has finished before TMEM is released.
+      mma_commit(smem_addr(&final_bar));
+      mbar_drain(smem_addr(&final_bar), 0, status);
+    }
+  } else {
+    // ------------------------------------- operand split, then epilogue
+    const int t = threadIdx.x - 64, cw = warp - 2;  // 0..255, converting warp 0..7
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int kb = 0; kb < nkb; ++kb) {
+      // Lanes of a warp pass the same __syncwarp whatever their waits returned.
+      if (ok && !mbar_wait(smem_addr(&full_bar[stage]), phase, abort_p, status)) ok = false;
+      if (ok) {
+        uint8_t* st = sbase + stage * Cfg::STAGE_BYTES;
+        // A (and a K-major B) in place: hi over the raw value, lo beside it.
+#pragma unroll 4
+        for (int i = t; i < Cfg::A_BYTES / 16; i += 256) {
+          float4* x = reinterpret_cast<float4*>(st + i * 16);
+          float4 hi, lo;
+          split4(*x, hi, lo);
+          *x = hi;
+          if (SPLIT3) *reinterpret_cast<float4*>(st + Cfg::OFF_A_LO + i * 16) = lo;
+        }
+        if (B_KMAJOR) {
+#pragma unroll 4
+          for (int i = t; i < Cfg::B_BYTES / 16; i += 256) {
+            float4* x = reinterpret_cast<float4*>(st + Cfg::OFF_B_HI + i * 16);
+            float4 hi, lo;
+            split4(*x, hi, lo);
+            *x = hi;
+            if (SPLIT3) *reinterpret_cast<float4*>(st + Cfg::OFF_B_LO + i * 16) = lo;
+          }
+        } else {
+          // N-major B: lane = k; a 16-byte read of four columns of row k of a
+          // staged box, four 4-byte writes down the K-major rows of B.
+          for (int gi = cw; gi < BN / 4; gi += 8) {
+            const int bx = gi >> 3, c = gi & 7;
+            const float4 x = *reinterpret_cast<const float4*>(
+                st + Cfg::OFF_RAW + bx * 4096 + lane * 128 + ((c ^ (lane & 7)) << 4));
+            float4 hi, lo;
+            split4(x, hi, lo);
+            const float hv[4] = {hi.x, hi.y, hi.z, hi.w};
+            const float lv[4] = {lo.x, lo.y, lo.z, lo.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const int n = gi * 4 + i;
+              const uint32_t off = n * 128 + (((lane >> 2) ^ (n & 7)) << 4) + (lane & 3) * 4;
+              *reinterpret_cast<float*>(st + Cfg::OFF_B_HI + off) = hv[i];
+              if (SPLIT3) *reinterpret_cast<float*>(st + Cfg::OFF_B_LO + off) = lv[i];
+            }
+          }
+        }
+        fence_proxy_async_smem();
+      }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(smem_addr(&conv_bar[stage]));
+      if (++stage == STAGES) {
+        stage = 0;
+        phase ^= 1u;
+      }
+    }
+    // Epilogue (warps 2-5): row = TMEM lane; the chunks' big + small sums
+    // (3xTF32) added in fp32 registers in chunk order.
+    if (warp < 6 && ok && mbar_wait(smem_addr(&tfull_bar), 0, abort_p, status)) {
+      tc_fence_after();
+      const int quarter = warp & 3;
+      const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+      const int row = tm * BM + quarter * 32 + lane;
+      float* crow = C + (int64_t)row * ldc;
+      const bool c_vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+      const int nchunks = SPLIT3 ? (nkb + KB_CHUNK - 1) / KB_CHUNK : 1;
+#pragma unroll 1
+      for (int j = 0; j < BN / 32; ++j) {
+        float acc[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) acc[i] = 0.f;
+        for (int c = 0; c < nchunks; ++c) {
+          const uint32_t tb = tmem + lane_off + c * Cfg::SLOT_COLS + j * 32;
+          uint32_t rb[32], rs[32];
+          if (SPLIT3) {
+            tmem_ld32x2(tb, rb, tb + BN, rs);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] += __uint_as_float(rb[i]) + __uint_as_float(rs[i]);
+          } else {
+            tmem_ld32(tb, rb);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) acc[i] = __uint_as_float(rb[i]);
+          }
+        }
+        store32(crow, row, tn * BN + j * 32, acc, M, N, alpha, beta, bias, c_vec);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, Cfg::TMEM_COLS);
+  }
+}
+
+template <int BN, bool SPLIT3, bool B_KMAJOR>
+void launch_fused(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, int K, float* C,
+                  int64_t ldc, float alpha, float beta, const float* bias, int* status,
+                  cudaStream_t s) {
+  using Cfg = FusedCfg<BN, SPLIT3, B_KMAJOR>;
+  static std::atomic<uint64_t> configured{0};  // one bit per device
+  int dev = 0;
+  ATTNB_CUDA(cudaGetDevice(&dev));
+  const uint64_t bit = 1ull << (dev & 63);
+  if (!(configured.load() & bit)) {
+    ATTNB_CUDA(cudaFuncSetAttribute(gemm_fused_kernel<BN, SPLIT3, B_KMAJOR>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    configured.fetch_or(bit);
+  }
+  const int tiles = ((M + BM - 1) / BM) * ((N + BN - 1) / BN);
+  ATTNB_CUDA(launch_pdl(gemm_fused_kernel<BN, SPLIT3, B_KMAJOR>, dim3(tiles),
+                        dim3(kFusedThreads), Cfg::SMEM, s, ta, tb, M, N, K, C, ldc, alpha, beta,
+                        bias, status));
+}
+
 // C = beta * C (alpha == 0 path of the reference, src/gemm.cpp:328-336).
 __global__ void scale_c_kernel(float* C, int64_t ldc, int M, int N, float beta) {
   const int64_t n = (int64_t)M * N;
@@ -428,6 +711,29 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
       scale_c_kernel<<<blocks, 256, 0, s>>>(C, ldc, p.M, p.N, beta);
     }
     return;
+  }
+  // 1xTF32, one 128x64 tile per CTA, aligned rows: the raw operands go
+  // straight into the kernel (no packing pass).  3xTF32 stays on the packed
+  // path: its split stages (hi and lo of A and B, plus the B staging) leave
+  // only three in flight, and the fused form measured no faster there.
+  {
+    const int tiles64 = ((p.M + BM - 1) / BM) * ((p.N + 63) / 64);
+    auto aligned = [](const float* x, int64_t ld) {
+      return (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && ld % 4 == 0;
+    };
+    if (!p.split3 && a_kmajor && pick_bn(p.M, p.N, false, num_sms) == 64 &&
+        tiles64 <= num_sms && aligned(A, lda) && aligned(B, ldb)) {
+      const CUtensorMap ta = make_tmap_2d(A, p.M, p.K, lda, BM, BK);
+      const CUtensorMap tb = b_kmajor ? make_tmap_2d(B, p.N, p.K, ldb, 64, BK)
+                                      : make_tmap_2d(B, p.K, p.N, ldb, BK, 32);
+      ProfScope prof("gemm_tc", s);
+      const auto go = [&](auto launch) {
+        launch(ta, tb, p.M, p.N, p.K, C, ldc, alpha, beta, bias, status, s);
+      };
+      if (b_kmajor) go(launch_fused<64, false, true>);
+      else go(launch_fused<64, false, false>);
+      return;
+    }
   }
   char* w = static_cast<char*>(ws);
   float* a_hi = reinterpret_cast<float*>(w + p.off_a_hi);
