@@ -4,7 +4,9 @@
 Same functions, argument names and defaults as the reference module:
 ``mha_block_dense``, ``gemm``, ``gemm_jit``; plus ``attn_step_dense`` and
 ``attn_block_dense``, which the reference's tests call but its module never
-exported.  Every function takes and returns NumPy float32 arrays (inputs are
+exported, and ``KVCache`` (a device-resident K/V cache for multi-step decode:
+``append(k, v)``, ``step(q, k_new=None, v_new=None)``, ``truncate(n)``), which
+the reference does not have.  Every function takes and returns NumPy float32 arrays (inputs are
 force-cast to C-contiguous float32) and raises ``ValueError`` for shape
 problems and ``RuntimeError`` otherwise, like the reference's bindings.
 
@@ -19,6 +21,7 @@ from __future__ import annotations
 import numpy as np
 
 from ._attn_cpu import (  # noqa: F401  (ImportError here means the extension is not built)
+    KVCache,
     attn_block_dense as _attn_block_dense,
     attn_step_dense as _attn_step_dense,
     gemm as _gemm,
@@ -70,4 +73,4 @@ def attn_block_dense(Q: np.ndarray, K: np.ndarray, V: np.ndarray, causal: bool =
 
 
 __all__ = ["mha_block_dense", "gemm", "gemm_jit", "attn_step_dense", "attn_block_dense",
-           "version"]
+           "KVCache", "version"]

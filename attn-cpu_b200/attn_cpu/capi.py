@@ -28,6 +28,9 @@ EXPORTED = [
     "attnb_attn_step_dense", "attnb_attn_step_dense_dev", "attnb_attn_step_dense_noalloc",
     "attnb_attn_block_dense", "attnb_attn_block_dense_dev",
     "attnb_mha_block_dense", "attnb_mha_block_dense_dev",
+    "attnb_kv_cache_create", "attnb_kv_cache_destroy", "attnb_kv_cache_length",
+    "attnb_kv_cache_truncate", "attnb_kv_cache_append", "attnb_kv_cache_step",
+    "attnb_kv_cache_step_dev",
 ]
 
 
@@ -75,6 +78,13 @@ def lib() -> ctypes.CDLL:
         L.attnb_attn_block_dense_dev.argtypes = [T, T, T, T, i, i, vp]
         L.attnb_mha_block_dense.argtypes = [vp, i, i, vp, vp, vp, vp, i, i, vp, i]
         L.attnb_mha_block_dense_dev.argtypes = [vp, i, i, i, vp, vp, vp, vp, i, i, vp, i, vp]
+        L.attnb_kv_cache_create.argtypes = [i, i, i, ctypes.POINTER(vp)]
+        L.attnb_kv_cache_destroy.argtypes = [vp]
+        L.attnb_kv_cache_length.argtypes = [vp, ctypes.POINTER(i)]
+        L.attnb_kv_cache_truncate.argtypes = [vp, i]
+        L.attnb_kv_cache_append.argtypes = [vp, vp, vp, i, vp]
+        L.attnb_kv_cache_step.argtypes = [vp, vp, vp, vp, vp]
+        L.attnb_kv_cache_step_dev.argtypes = [vp, vp, vp, vp, vp, vp]
         for name in EXPORTED:
             if name not in ("attnb_last_error", "attnb_version"):
                 getattr(L, name).restype = ctypes.c_int
@@ -168,3 +178,47 @@ def profile_read(kernel: str) -> tuple[float, int]:
 
 def stream_status(stream=None) -> None:
     check(lib().attnb_stream_status(_stream(stream)))
+
+
+class KVCacheDev:
+    """The resident K/V cache (attnb_kv_cache_*) driven with CUDA tensors.
+
+    K and V stay on the device current at construction, [H, capacity, Dh];
+    ``append`` and ``step`` enqueue on ``stream`` (default: torch's current
+    stream) and return without synchronising."""
+
+    def __init__(self, H: int, Dh: int, capacity: int):
+        self._h = ctypes.c_void_p()
+        check(lib().attnb_kv_cache_create(H, Dh, capacity, ctypes.byref(self._h)))
+        self.H, self.Dh = H, Dh
+
+    def __len__(self) -> int:
+        n = ctypes.c_int()
+        check(lib().attnb_kv_cache_length(self._h, ctypes.byref(n)))
+        return n.value
+
+    def truncate(self, length: int) -> None:
+        check(lib().attnb_kv_cache_truncate(self._h, length))
+
+    def append(self, k, v, stream=None) -> None:
+        """k, v: [H, n, Dh] contiguous float32 tensors (CUDA or CPU)."""
+        check(lib().attnb_kv_cache_append(self._h, k.data_ptr(), v.data_ptr(), k.shape[1],
+                                          _stream(stream)))
+
+    def step(self, q, o, k_new=None, v_new=None, stream=None) -> None:
+        """o[H, Dh] = attention of q[H, Dh] over the cache, after appending k_new, v_new."""
+        kp = k_new.data_ptr() if k_new is not None else None
+        vp_ = v_new.data_ptr() if v_new is not None else None
+        check(lib().attnb_kv_cache_step_dev(self._h, q.data_ptr(), kp, vp_, o.data_ptr(),
+                                            _stream(stream)))
+
+    def close(self) -> None:
+        if self._h:
+            check(lib().attnb_kv_cache_destroy(self._h))
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown: the library may be gone
+            pass

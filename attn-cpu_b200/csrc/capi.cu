@@ -4,6 +4,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstring>
+#include <memory>
 #include <string>
 #include <vector>
 
@@ -383,6 +384,169 @@ int attnb_attn_step_dense(const attnb_tensor* Q, const attnb_tensor* K, const at
       decode_launch(p, q, k, v, mview(&dO, 1), ws, s);
       ATTNB_CUDA(cudaMemcpyAsync(O->data + so.lo, base + oo, so.count() * 4,
                                  cudaMemcpyDeviceToHost, s));
+      finish_host_call(c);
+    });
+  });
+}
+
+// --------------------------------------------------------- resident KV cache
+}  // extern "C"
+
+// K and V of every head, [H, capacity, Dh] each, on the device that was
+// current at creation; `length` tokens are valid.  The length is host-side
+// state, advanced when an append is enqueued.
+struct attnb_kv_cache {
+  int device, H, Dh, capacity, length;
+  float* k;
+  float* v;
+};
+
+namespace {
+
+attnb_kv_cache* checked_cache(attnb_kv_cache* kc) {
+  if (!kc) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null KV cache");
+  int dev = -1;
+  ATTNB_CUDA(cudaGetDevice(&dev));
+  if (dev != kc->device)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "KV cache belongs to device " + std::to_string(kc->device) +
+                                         ", current device is " + std::to_string(dev));
+  return kc;
+}
+
+// Copies n tokens of k and v ([H, n, Dh], rows contiguous; host or device
+// memory) behind the valid ones: one 2-D copy per tensor (H rows of n * Dh).
+void cache_append(attnb_kv_cache* kc, const float* k, const float* v, int n, cudaStream_t s) {
+  if (n < 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "n must be non-negative");
+  if (n == 0) return;
+  if (!k || !v) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+  if (n > kc->capacity - kc->length)
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "KV cache capacity exceeded (" + std::to_string(kc->length) +
+                                         " + " + std::to_string(n) + " > " +
+                                         std::to_string(kc->capacity) + ")");
+  const size_t pitch = (size_t)kc->capacity * kc->Dh * sizeof(float);
+  const size_t width = (size_t)n * kc->Dh * sizeof(float);
+  const size_t off = (size_t)kc->length * kc->Dh;
+  ATTNB_CUDA(cudaMemcpy2DAsync(kc->k + off, pitch, k, width, width, kc->H, cudaMemcpyDefault, s));
+  ATTNB_CUDA(cudaMemcpy2DAsync(kc->v + off, pitch, v, width, width, kc->H, cudaMemcpyDefault, s));
+  kc->length += n;
+}
+
+// Device views of the valid part of the cache.
+void cache_views(const attnb_kv_cache* kc, attnb_tensor& K, attnb_tensor& V) {
+  const int64_t sH = (int64_t)kc->capacity * kc->Dh;
+  K = attnb_tensor{kc->k, kc->H, kc->length, kc->Dh, sH, kc->Dh, 1};
+  V = attnb_tensor{kc->v, kc->H, kc->length, kc->Dh, sH, kc->Dh, 1};
+}
+
+}  // namespace
+
+extern "C" {
+
+int attnb_kv_cache_create(int H, int Dh, int capacity, attnb_kv_cache** cache) {
+  return guarded([&] {
+    if (!cache) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    *cache = nullptr;
+    if (H <= 0 || Dh <= 0 || capacity <= 0)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "H, Dh and capacity must be positive");
+    DeviceCtx& c = current_ctx();
+    auto kc = std::make_unique<attnb_kv_cache>();
+    kc->device = c.device;
+    kc->H = H;
+    kc->Dh = Dh;
+    kc->capacity = capacity;
+    kc->length = 0;
+    kc->k = kc->v = nullptr;
+    const size_t bytes = (size_t)H * capacity * Dh * sizeof(float);
+    ATTNB_CUDA(cudaMalloc(&kc->k, bytes));
+    const cudaError_t e = cudaMalloc(&kc->v, bytes);
+    if (e != cudaSuccess) {
+      cudaFree(kc->k);
+      ATTNB_CUDA(e);
+    }
+    *cache = kc.release();
+  });
+}
+
+int attnb_kv_cache_destroy(attnb_kv_cache* cache) {
+  return guarded([&] {
+    if (!cache) return;
+    int prev = -1;
+    ATTNB_CUDA(cudaGetDevice(&prev));
+    ATTNB_CUDA(cudaSetDevice(cache->device));
+    // Work still queued on the cache's buffers finishes before they are freed.
+    ATTNB_CUDA(cudaDeviceSynchronize());
+    ATTNB_CUDA(cudaFree(cache->k));
+    ATTNB_CUDA(cudaFree(cache->v));
+    ATTNB_CUDA(cudaSetDevice(prev));
+    delete cache;
+  });
+}
+
+int attnb_kv_cache_length(const attnb_kv_cache* cache, int* length) {
+  return guarded([&] {
+    if (!cache || !length) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    *length = cache->length;
+  });
+}
+
+int attnb_kv_cache_truncate(attnb_kv_cache* cache, int length) {
+  return guarded([&] {
+    if (!cache) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null KV cache");
+    if (length < 0 || length > cache->length)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "length must be in [0, current length]");
+    cache->length = length;
+  });
+}
+
+int attnb_kv_cache_append(attnb_kv_cache* cache, const float* k, const float* v, int n,
+                          void* stream) {
+  return guarded([&] { cache_append(checked_cache(cache), k, v, n, as_stream(stream)); });
+}
+
+int attnb_kv_cache_step_dev(attnb_kv_cache* cache, const float* q, const float* k_new,
+                            const float* v_new, float* o, void* stream) {
+  return guarded([&] {
+    attnb_kv_cache* kc = checked_cache(cache);
+    if (!q || !o) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    if ((k_new == nullptr) != (v_new == nullptr))
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "k_new and v_new are given together");
+    cudaStream_t s = as_stream(stream);
+    if (k_new) cache_append(kc, k_new, v_new, 1, s);
+    if (kc->length == 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "K/V T must be positive and equal");
+    attnb_tensor Q{q, kc->H, 1, kc->Dh, kc->Dh, 0, 1}, K, V;
+    attnb_mtensor O{o, kc->H, 1, kc->Dh, kc->Dh, 0, 1};
+    cache_views(kc, K, V);
+    step_dev(&Q, &K, &V, &O, current_ctx(), s, nullptr, 0);
+  });
+}
+
+int attnb_kv_cache_step(attnb_kv_cache* cache, const float* q, const float* k_new,
+                        const float* v_new, float* o) {
+  return guarded([&] {
+    attnb_kv_cache* kc = checked_cache(cache);
+    if (!q || !o) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    if ((k_new == nullptr) != (v_new == nullptr))
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "k_new and v_new are given together");
+    if (!k_new && kc->length == 0)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "K/V T must be positive and equal");
+    with_host_ctx([&](DeviceCtx& c) {
+      cudaStream_t s = c.stream;
+      const size_t hd = (size_t)kc->H * kc->Dh;
+      Carver cv;
+      const size_t oq = cv.take(hd * 4), oo = cv.take(hd * 4);
+      char* base = static_cast<char*>(c.io.ensure(cv.take(0), s));
+      float* dq = reinterpret_cast<float*>(base + oq);
+      float* dout = reinterpret_cast<float*>(base + oo);
+      if (k_new) cache_append(kc, k_new, v_new, 1, s);
+      ATTNB_CUDA(cudaMemcpyAsync(dq, q, hd * 4, cudaMemcpyHostToDevice, s));
+      attnb_tensor Q{dq, kc->H, 1, kc->Dh, kc->Dh, 0, 1}, K, V;
+      attnb_mtensor O{dout, kc->H, 1, kc->Dh, kc->Dh, 0, 1};
+      cache_views(kc, K, V);
+      const View3 qv = view(&Q, 1), kv = view(&K, K.T), vv = view(&V, V.T);
+      const DecodePlan p = decode_plan(qv, kv, vv, c.num_sms);
+      void* ws = c.scratch_host_path.ensure(decode_workspace_bytes(p, kc->H, kc->Dh) + 256, s);
+      decode_launch(p, qv, kv, vv, mview(&O, 1), ws, s);
+      ATTNB_CUDA(cudaMemcpyAsync(o, dout, hd * 4, cudaMemcpyDeviceToHost, s));
       finish_host_call(c);
     });
   });

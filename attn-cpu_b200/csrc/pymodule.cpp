@@ -149,6 +149,80 @@ py::array_t<float> attn_block_dense_py(farray Q, farray K, farray V, bool causal
   return O;
 }
 
+// Resident K/V cache for multi-step decode (attnb_kv_cache_*): K and V stay on
+// the device between steps; a step moves only the new token and the query in
+// and the output row out.
+class KVCache {
+ public:
+  KVCache(int H, int Dh, int capacity) : H_(H), Dh_(Dh) {
+    rethrow(attnb_kv_cache_create(H, Dh, capacity, &c_));
+  }
+  ~KVCache() {
+    if (c_) attnb_kv_cache_destroy(c_);
+  }
+  KVCache(const KVCache&) = delete;
+  KVCache& operator=(const KVCache&) = delete;
+
+  int length() const {
+    int n = 0;
+    rethrow(attnb_kv_cache_length(c_, &n));
+    return n;
+  }
+  void truncate(int n) { rethrow(attnb_kv_cache_truncate(c_, n)); }
+
+  // k, v: [H, n, Dh]; returns once they are copied.
+  void append(farray k, farray v) {
+    if (k.ndim() != 3 || v.ndim() != 3) throw std::invalid_argument("k and v must be [H,n,Dh]");
+    if (k.shape(0) != H_ || k.shape(2) != Dh_ || v.shape(0) != H_ || v.shape(1) != k.shape(1) ||
+        v.shape(2) != Dh_)
+      throw std::invalid_argument("k and v must both be [H,n,Dh] with the cache's H and Dh");
+    const float *pk = k.data(), *pv = v.data();
+    const int n = (int)k.shape(1);
+    int rc;
+    {
+      py::gil_scoped_release nogil;
+      rc = attnb_kv_cache_append(c_, pk, pv, n, nullptr);
+      if (rc == ATTNB_OK) rc = attnb_stream_status(nullptr);  // the host arrays are read
+    }
+    rethrow(rc);
+  }
+
+  // q: [H, Dh]; k_new / v_new: [H, Dh] (both or neither) appended first.
+  py::array_t<float> step(farray q, py::object k_new, py::object v_new) {
+    auto row = [&](const farray& x, const char* what) {
+      if (x.ndim() != 2 || x.shape(0) != H_ || x.shape(1) != Dh_)
+        throw std::invalid_argument(std::string(what) + " must be [H,Dh] with the cache's H and Dh");
+    };
+    row(q, "q");
+    if (k_new.is_none() != v_new.is_none())
+      throw std::invalid_argument("k_new and v_new are given together");
+    farray kn, vn;
+    const float *pk = nullptr, *pv = nullptr;
+    if (!k_new.is_none()) {
+      kn = k_new.cast<farray>();
+      vn = v_new.cast<farray>();
+      row(kn, "k_new");
+      row(vn, "v_new");
+      pk = kn.data();
+      pv = vn.data();
+    }
+    py::array_t<float> O = result_array({H_, Dh_});
+    const float* pq = q.data();
+    float* po = O.mutable_data();
+    int rc;
+    {
+      py::gil_scoped_release nogil;
+      rc = attnb_kv_cache_step(c_, pq, pk, pv, po);
+    }
+    rethrow(rc);
+    return O;
+  }
+
+ private:
+  attnb_kv_cache* c_ = nullptr;
+  int H_, Dh_;
+};
+
 }  // namespace
 
 PYBIND11_MODULE(_attn_cpu, m) {
@@ -169,4 +243,16 @@ PYBIND11_MODULE(_attn_cpu, m) {
         py::arg("causal") = false, py::arg("precision") = -1,
         "Prefill: Q:[H,L,Dh], K,V:[H,T,Dh] -> O:[H,L,Dh]");
   m.def("version", &attnb_version);
+  py::class_<KVCache>(m, "KVCache",
+                      "Resident K/V cache on the current device for multi-step decode")
+      .def(py::init<int, int, int>(), py::arg("H"), py::arg("Dh"), py::arg("capacity"))
+      .def("__len__", &KVCache::length)
+      .def("truncate", &KVCache::truncate, py::arg("length"),
+           "Drop tokens from the end: keep the first `length`.")
+      .def("append", &KVCache::append, py::arg("k"), py::arg("v"),
+           "Append k, v: [H, n, Dh] behind the valid tokens.")
+      .def("step", &KVCache::step, py::arg("q"), py::arg("k_new") = py::none(),
+           py::arg("v_new") = py::none(),
+           "Append k_new, v_new ([H, Dh]) if given, then O[H, Dh] = attention of q over the "
+           "cache (the function of attn_step_dense).");
 }

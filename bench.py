@@ -19,7 +19,9 @@ Keys beyond the base contract:
   cpu_baseline the reference's own CPU code (oracle/_ref, compiled from its
                sources) timed on this host on a bounded sample (rank 0, N=1);
   also         the other measured configs (decode GB/s, SGEMM TFLOP/s,
-               attention block TFLOP/s) with their own rooflines (N=1 only).
+               attention block TFLOP/s) with their own rooflines (N=1 only);
+  e2e_resident (decode) the decode step through attn_cpu.KVCache, K/V kept on
+               the device: each step moves q and the new token in, o out.
 
 `--impl reference` times the reference's CPU implementation of the headline
 path on this host's cores (all threads) and prints its own line.
@@ -459,9 +461,54 @@ def measure(w: str, rank: int, world: int, steps: int, warmup: int, precision, p
         res["e2e"] = {"value": round(world * work / (e_ms * 1e-3) / scale, 4),
                       "unit": WORKLOADS[w]["unit"], "ms_per_step": round(e_ms, 4),
                       "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h}
+        if w == "decode":
+            res["e2e_resident"] = decode_resident_e2e(rank, world, steps, warmup, work, scale)
     del run, e2e
     torch.cuda.empty_cache()
     return res
+
+
+def decode_resident_e2e(rank: int, world: int, steps: int, warmup: int, work: float,
+                        scale: float) -> dict:
+    """The decode workload through the resident K/V cache (attn_cpu.KVCache):
+    the cache holds T - 1 tokens on the device, and each step (a host call)
+    appends the new token's k and v, attends with q and returns o, so only
+    q, k_new, v_new go in and o comes out.  The cache is truncated back to
+    T - 1 tokens before each step, so every step attends over the same T."""
+    import numpy as np
+    import torch
+
+    import attn_cpu
+
+    c = WORKLOADS["decode"]
+    H, T, Dh = c["H"], c["T"], c["Dh"]
+    rng = np.random.default_rng(2000 + rank)
+    pin = lambda a: torch.from_numpy(a).pin_memory().numpy()
+    K = pin(rng.standard_normal((H, T, Dh), dtype=np.float32))
+    V = pin(rng.standard_normal((H, T, Dh), dtype=np.float32))
+    q = pin(rng.standard_normal((H, Dh), dtype=np.float32))
+    kn, vn = pin(np.ascontiguousarray(K[:, -1])), pin(np.ascontiguousarray(V[:, -1]))
+    cache = attn_cpu.KVCache(H, Dh, T)
+    cache.append(K[:, :T - 1], V[:, :T - 1])
+
+    def step():
+        cache.truncate(T - 1)
+        return cache.step(q, kn, vn)
+
+    for _ in range(max(1, warmup)):
+        step()
+    barrier(world)
+    ts = []
+    for _ in range(steps):
+        t = time.perf_counter()
+        step()
+        ts.append(time.perf_counter() - t)
+    e_ms = max_over_ranks(1e3 * sum(ts) / len(ts), world)
+    del cache
+    return {"value": round(world * work / (e_ms * 1e-3) / scale, 4),
+            "unit": WORKLOADS["decode"]["unit"], "ms_per_step": round(e_ms, 4),
+            "h2d_bytes_per_step": 3 * H * Dh * 4, "d2h_bytes_per_step": H * Dh * 4,
+            "api": "attn_cpu.KVCache.step (K/V resident on the device)"}
 
 
 # ----------------------------------------------------- CPU (reference) runs
@@ -616,6 +663,8 @@ def main():
                 "e2e": head.get("e2e"), "roofline": head["roofline"],
                 "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
                 "cpu_baseline": cpu, "also": also}
+        if head.get("e2e_resident"):
+            line["e2e_resident"] = head["e2e_resident"]
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist

@@ -148,6 +148,37 @@ ATTNB_API int attnb_attn_step_dense_noalloc(const attnb_tensor* Q, const attnb_t
                                             const attnb_tensor* V, attnb_mtensor* O,
                                             void* stream);
 
+/* ------------------------------------------------- resident KV cache */
+/* Multi-step decode with K and V kept on the device between steps, for the
+ * host<->device residency the reference's boundary cannot offer (its
+ * attn::attn_step_dense, src/attn_dense.cpp:21-73, takes the whole cache
+ * from host memory on every call).  A cache holds K and V as [H, capacity,
+ * Dh] fp32 on the device that is current when it is created; calls must be
+ * made with that device current.  `length` tokens are valid, advanced when
+ * an append is enqueued: calls that use one cache from several streams must
+ * be ordered by the caller.
+ *   append: k and v are [H, n, Dh] with contiguous rows, in host or device
+ *     memory; more than capacity - length tokens is ATTNB_ERR_INVALID_ARGUMENT.
+ *   truncate: drops tokens from the end (0 <= length <= current length).
+ *   step: optionally appends one token (k_new, v_new: [H, Dh], both or
+ *     neither), then O[h,:] = softmax(Q[h,:] . K[h]^T / sqrt(Dh)) . V[h] over
+ *     the valid tokens -- the function of attnb_attn_step_dense.
+ *     attnb_kv_cache_step takes host pointers and returns when O is written;
+ *     attnb_kv_cache_step_dev takes device pointers (k_new / v_new may also
+ *     be host memory) and enqueues on `stream`.
+ * destroy synchronises the cache's device before freeing it. */
+typedef struct attnb_kv_cache attnb_kv_cache;
+ATTNB_API int attnb_kv_cache_create(int H, int Dh, int capacity, attnb_kv_cache** cache);
+ATTNB_API int attnb_kv_cache_destroy(attnb_kv_cache* cache);
+ATTNB_API int attnb_kv_cache_length(const attnb_kv_cache* cache, int* length);
+ATTNB_API int attnb_kv_cache_truncate(attnb_kv_cache* cache, int length);
+ATTNB_API int attnb_kv_cache_append(attnb_kv_cache* cache, const float* k, const float* v, int n,
+                                    void* stream);
+ATTNB_API int attnb_kv_cache_step(attnb_kv_cache* cache, const float* q, const float* k_new,
+                                  const float* v_new, float* o);
+ATTNB_API int attnb_kv_cache_step_dev(attnb_kv_cache* cache, const float* q, const float* k_new,
+                                      const float* v_new, float* o, void* stream);
+
 /* Prefill with given Q/K/V: Q [H,L,Dh], K/V [H,T,Dh] -> O [H,L,Dh]; causal
  * needs L == T.  Replaces attn::attn_block_dense (include/attn.h:40-44;
  * src/attn_block.cpp:104-241). */
