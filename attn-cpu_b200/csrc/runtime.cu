@@ -74,6 +74,18 @@ DeviceCtx& current_ctx() {
   return ref;
 }
 
+void ensure_copy_streams(DeviceCtx& c) {
+  if (c.ev_out) return;
+  ATTNB_CUDA(cudaStreamCreateWithFlags(&c.h2d, cudaStreamNonBlocking));
+  ATTNB_CUDA(cudaStreamCreateWithFlags(&c.d2h, cudaStreamNonBlocking));
+  for (int g = 0; g < DeviceCtx::kMaxGroups; ++g) {
+    ATTNB_CUDA(cudaEventCreateWithFlags(&c.ev_in[g], cudaEventDisableTiming));
+    ATTNB_CUDA(cudaEventCreateWithFlags(&c.ev_k[g], cudaEventDisableTiming));
+  }
+  ATTNB_CUDA(cudaEventCreateWithFlags(&c.ev_start, cudaEventDisableTiming));
+  ATTNB_CUDA(cudaEventCreateWithFlags(&c.ev_out, cudaEventDisableTiming));  // last: the guard
+}
+
 void* dev_scratch(DeviceCtx& c, size_t bytes, cudaStream_t stream) {
   if (bytes == 0) return nullptr;
   std::lock_guard<std::mutex> g(c.scratch_mu);

@@ -45,7 +45,17 @@ struct DeviceCtx {
   DeviceBuffer scratch_host_path; // kernel scratch for host-pointer calls
   std::mutex scratch_mu;
   DeviceBuffer scratch_dev_path;  // kernel scratch for _dev calls (per device)
+  // Host-pointer calls that overlap their copies in, kernels and copies out
+  // over groups of rows use a copy-in and a copy-out stream besides `stream`,
+  // and one event per group and stage (ensure_copy_streams, under `mu`).
+  static constexpr int kMaxGroups = 8;
+  cudaStream_t h2d = nullptr, d2h = nullptr;
+  cudaEvent_t ev_start = nullptr, ev_out = nullptr;
+  cudaEvent_t ev_in[kMaxGroups] = {}, ev_k[kMaxGroups] = {};
 };
+
+// Creates ctx's copy streams and events on first use (hold ctx.mu).
+void ensure_copy_streams(DeviceCtx& c);
 
 // Context of the current CUDA device (created on first use).
 DeviceCtx& current_ctx();
