@@ -31,6 +31,8 @@
 #include <algorithm>
 #include <atomic>
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -110,34 +112,6 @@ struct AttnCfg {
   static_assert(WTS + 64 * 8 * 4 <= RING_BYTES, "merge staging fits the rings");
   static_assert(NBUF * (S_BUF + PV_BUF) <= TMEM_COLS, "TMEM budget");
 };
-
-// Position in a ring of N stages (stage index and the phase parity to wait on).
-template <int N>
-struct Ring {
-  int stage = 0;
-  uint32_t phase = 0;
-  uint32_t issued_mask = 0, issued_parity = 0;
-  __device__ __forceinline__ void note_issue() {
-    issued_mask |= 1u << stage;
-    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
-  }
-  __device__ __forceinline__ void advance() {
-    if (++stage == N) {
-      stage = 0;
-      phase ^= 1u;
-    }
-  }
-};
-
-__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* status) {
-  const uint64_t t0 = globaltimer();
-  while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > ATTNB_WAIT_LIMIT_NS) {
-      raise_timeout(status);
-      return;
-    }
-  }
-}
 
 struct AttnParams {
   int L, T, H, Dh, causal, nsplit, tiles_per_split, qtiles;
@@ -989,6 +963,11 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
   p.tiles_per_split = (n_kv + ns - 1) / ns;
   p.nsplit = (n_kv + p.tiles_per_split - 1) / p.tiles_per_split;
   p.fusable = p.tiles_per_split == 1 && p.dhp <= 64;
+  static const bool pairs_on = [] {
+    const char* e = std::getenv("ATTNB_ATTN_PAIRS");
+    return !(e && std::strcmp(e, "0") == 0);
+  }();
+  p.pairs = pairs_on && !p.split3 && p.nsplit == 1 && p.qtiles >= 2 && n_kv >= 2;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -1061,6 +1040,13 @@ void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View
   const bool o_tma = O.sD == 1 && (reinterpret_cast<uintptr_t>(O.data) & 15u) == 0 &&
                      (O.sT % 4) == 0 && (O.sH % 4) == 0 && O.sT > 0 && O.sH > 0;
   if (o_tma) maps[6] = make_tmap_3d(O.data, p.H, p.L, p.Dh, O.sT, O.sH, BM, 32);
+  if (p.pairs) {
+    const AttnPPArgs a{p.L, p.T, p.H, p.Dh, causal ? 1 : 0, p.qtiles, o_tma ? 1 : 0,
+                       O.data, O.sH, O.sT, O.sD, status};
+    ProfScope prof("attn_tc", s);
+    attn_pp_launch(p.dhp, maps[0], maps[2], maps[4], maps[6], a, s);
+    return;
+  }
   AttnParams prm{};
   prm.L = p.L;
   prm.T = p.T;

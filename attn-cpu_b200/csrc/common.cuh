@@ -80,6 +80,37 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
   return mbar_wait_limit(bar, parity, abort_flag, status, ATTNB_WAIT_LIMIT_NS);
 }
 
+// Position in a ring of N stages (stage index and the phase parity to wait on).
+template <int N>
+struct Ring {
+  int stage = 0;
+  uint32_t phase = 0;
+  uint32_t issued_mask = 0, issued_parity = 0;
+  __device__ __forceinline__ void note_issue() {
+    issued_mask |= 1u << stage;
+    issued_parity = (issued_parity & ~(1u << stage)) | (phase << stage);
+  }
+  __device__ __forceinline__ void advance() {
+    if (++stage == N) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  }
+};
+
+// Waits for a phase that is certain to complete (a copy or MMA already issued)
+// before the CTA may exit; if the limit expires it raises the status word and
+// returns.
+__device__ __forceinline__ void drain_wait(uint32_t bar, uint32_t parity, int* status) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer() - t0 > ATTNB_WAIT_LIMIT_NS) {
+      raise_timeout(status);
+      return;
+    }
+  }
+}
+
 // Programmatic dependent launch: wait until the grid this one was launched
 // behind (see launch_pdl) has finished and its writes are visible.
 __device__ __forceinline__ void grid_dep_wait() {
@@ -89,6 +120,12 @@ __device__ __forceinline__ void grid_dep_wait() {
 // Barrier among the `nthreads` threads (a multiple of 32) that use barrier `id`.
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Arrive at barrier `id` without waiting (the other side waits with
+// named_bar_sync; `nthreads` counts both sides).
+__device__ __forceinline__ void named_bar_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
 // ------------------------------------------------------- thread-block cluster

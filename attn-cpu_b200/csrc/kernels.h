@@ -1,6 +1,7 @@
 // kernels.h -- host-side launch interface of the device kernels.  Everything
 // here takes device pointers and a stream; validation happens in capi.cu.
 #pragma once
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
 #include <stdint.h>
@@ -48,6 +49,9 @@ struct AttnTcPlan {
   // One key tile per CTA and dhp <= 64: when the views allow TMA reads, the
   // kernel loads and splits the raw operands itself (no packing launch).
   bool fusable;
+  // 1xTF32 with at least two query tiles and two key tiles: K3p (attn_pp.cu),
+  // two query tiles per CTA.  ATTNB_ATTN_PAIRS=0 keeps K3.
+  bool pairs;
   size_t off_q, off_k, off_v, ws_bytes;
 };
 // Head sizes the tensor-core kernel takes (padded to a multiple of 32, <= 128).
@@ -57,6 +61,18 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
 void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View3& V,
                  const MView3& O, bool causal, void* ws, int* status, int num_sms,
                  cudaStream_t s);
+
+// K3p: 1xTF32 prefill, two query tiles per CTA (attn_pp.cu).  Maps as built by
+// attn_tc_run for the packed operands: Q [H, L, dhp] box 128 x 32, K [H, T, dhp]
+// box 128 x 32, V^T [H, dhp, tp] box dhp x 32, and O box 128 x 32 (o_tma).
+struct AttnPPArgs {
+  int L, T, H, Dh, causal, qtiles, o_tma;
+  float* O;
+  int64_t osH, osT, osD;
+  int* status;
+};
+void attn_pp_launch(int dhp, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
+                    const CUtensorMap& o, const AttnPPArgs& a, cudaStream_t s);
 
 // ------------------------------------------------ operand packing (K2)
 // One packing job: a strided 3-D source src[h][r][c] (r < R, c < C), times
