@@ -104,7 +104,9 @@ def load_peaks() -> dict:
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region.
+    A timed region shorter than the 100 ms sampling period is bracketed: entry
+    waits for a first sample and exit for one more."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -125,7 +127,9 @@ class ClockSampler:
             self.t.start()
         except OSError:
             self.proc = None
-        time.sleep(0.15)
+        t0 = time.time()
+        while self.proc is not None and not self.lines and time.time() - t0 < 3.0:
+            time.sleep(0.01)
         return self
 
     def _read(self):
@@ -134,7 +138,9 @@ class ClockSampler:
 
     def __exit__(self, *a):
         if self.proc is not None:
-            time.sleep(0.15)
+            n0, t0 = len(self.lines), time.time()
+            while len(self.lines) <= n0 and time.time() - t0 < 1.0:
+                time.sleep(0.01)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
