@@ -5,14 +5,17 @@
 // laid out for long key ranges in 1xTF32:
 //
 //   CTA = two 128-row query tiles A and B of one head (query tiles 2x, 2x+1).
-//   Each K / V^T tile streamed by warp 0 serves both, so every byte read from
-//   L2 feeds twice the tensor-core work of K3.  The two tiles run as
-//   independent chains, each issued by one thread of its own warp (1 and 2;
-//   two threads of one warp would wait in lockstep):
+//   Each K / V^T tile streamed into shared memory serves both, so every byte
+//   read from L2 feeds twice the tensor-core work of K3.  Warp 0 streams Q
+//   and K, warp 3 V^T, each through its own ring.  The two tiles run as
+//   chains, each issued by one thread of its own warp (1 and 2; two threads
+//   of one warp would wait in lockstep):
 //       S_c(j) = Q_c . K_j^T  ->  softmax_c(j) writes P over S_c  ->  O_c += P . V_j
-//   so the tensor core works on one tile's products while the other tile's
-//   softmax runs.  TMEM: S_A, S_B (128 columns each), O_A, O_B (<= 128 each).
-//   Warp 0 streams Q and K, warp 3 V^T, each through its own ring.
+//   With rings that hold a whole K and V tile (head size <= 96) the two
+//   softmaxes take turns, so the tensor core works on one tile's products
+//   while the other tile's softmax runs; at head size 128 the rings are
+//   shorter than a tile and the chains run in step.  TMEM: S_A, S_B (128
+//   columns each), O_A, O_B (<= 128 each).
 //   Warps 4-7 (tile A) and 8-11 (tile B) own one query row per thread and hold
 //   the whole 128-key row of S in registers: one TMEM load, the row max, the
 //   exponentials and one TMEM store per tile, with no exchange between warps.

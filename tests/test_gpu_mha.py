@@ -75,3 +75,17 @@ def test_mha_block_config_batched_dev(cuda):
         ref = oracle.mha_block(x[b].cpu().numpy(), Wi.cpu().numpy(), bi.cpu().numpy(),
                                Wo.cpu().numpy(), bo.cpu().numpy(), H, False)
         assert rel_err(y[b].cpu().numpy(), ref) < TOL_3XTF32
+
+
+def test_mha_tf32_two_query_tile_kernel(cuda):
+    """TF32 block with 16 heads x 1280 rows: 160 (head, query tile) pairs, so the
+    attention takes the two-query-tile kernel, on the head-strided projections."""
+    import attn_cpu
+
+    rng = np.random.default_rng(21)
+    T, D, H = 1280, 1024, 16
+    x = rng.standard_normal((T, D), dtype=np.float32)
+    Wi, bi, Wo, bo = _weights(D, rng)
+    ref = oracle.mha_block(x, Wi, bi, Wo, bo, H, False)
+    y = attn_cpu.mha_block_dense(x, Wi, bi, Wo, bo, H, False, precision="tf32")
+    assert rel_err(y, ref) < TOL_TF32
