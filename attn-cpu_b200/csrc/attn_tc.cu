@@ -967,7 +967,14 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
     const char* e = std::getenv("ATTNB_ATTN_PAIRS");
     return !(e && std::strcmp(e, "0") == 0);
   }();
-  p.pairs = pairs_on && !p.split3 && p.nsplit == 1 && p.qtiles >= 2 && n_kv >= 2;
+  // K3p takes about 1.5x K3's time per key tile (it serves two query tiles),
+  // measured at head sizes 32-128; both hold one CTA per SM.  It pays when it
+  // needs fewer waves of CTAs by more than that: e.g. 160 (head, query tile)
+  // pairs take two waves of K3 and one of K3p, 128 pairs one wave of either.
+  const int waves_k3 = (pairs + num_sms - 1) / num_sms;
+  const int waves_pp = (H * ((p.qtiles + 1) / 2) + num_sms - 1) / num_sms;
+  p.pairs = pairs_on && !p.split3 && p.nsplit == 1 && p.qtiles >= 2 && n_kv >= 2 &&
+            waves_pp * 1.45 < waves_k3;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;

@@ -1,9 +1,10 @@
 """1xTF32 prefill with two query tiles per CTA (K3p, attn_pp.cu) against the
-oracle: the shapes below have enough (head, query tile) pairs that the key
-range is not split, so TF32 calls take K3p.  Ragged L and T, odd query-tile
-counts (the second tile of the last CTA is empty), causal masks, padded head
-sizes, an output view that rules out TMA stores, and the same calls with
-K3p turned off (ATTNB_ATTN_PAIRS=0) in a child process."""
+oracle.  The shapes below have 150-192 (head, query tile) pairs: the key range
+is not split, and K3p needs one wave of CTAs where K3 needs two, so TF32 calls
+take K3p.  Ragged L and T, odd query-tile counts (the second tile of the last
+CTA is empty), causal masks, padded head sizes, an output view that rules out
+TMA stores, and the same calls with K3p turned off (ATTNB_ATTN_PAIRS=0) in a
+child process."""
 from __future__ import annotations
 
 import json
@@ -25,9 +26,9 @@ SHAPES = [
     (50, 384, 512, 32, False),    # three query tiles per head: odd
     (24, 896, 640, 96, False),    # seven query tiles per head
     (20, 1024, 700, 128, False),
-    (4, 640, 640, 96, True),
-    (3, 300, 300, 128, True),     # three query tiles, causal
-    (2, 1000, 1000, 16, True),    # head size padded to 32
+    (24, 1024, 1024, 64, True),
+    (50, 384, 384, 128, True),    # three query tiles, causal
+    (40, 500, 500, 16, True),     # head size padded to 32, ragged
 ]
 
 
