@@ -316,11 +316,14 @@ void mha_dev(const float* x, int batch, int T, int D, const float* W_in, const f
   const size_t off_qkv = cv.take((size_t)rows * 3 * D * sizeof(float));
   const size_t off_ctx = cv.take((size_t)rows * D * sizeof(float));
   const size_t off_g = cv.take(0);
-  // The projections and the attention run one after the other on the stream
-  // and share one scratch region.
+  // The projections and the attention run one after the other and share one
+  // scratch region.  Several sequences' attention runs side by side on the
+  // fork streams, each fork with its own slice of that region.
+  const int nf = std::min(batch, ForkStreams::kForks);
+  const size_t attn_ws =
+      (block_scratch_bytes(H, T, T, Dh, causal != 0, prec, c.num_sms) + 255) & ~size_t(255);
   const size_t g_bytes =
-      std::max({p_in.ws_bytes, gemm_workspace_bound(rows, D, D, prec),
-                block_scratch_bytes(H, T, T, Dh, causal != 0, prec, c.num_sms)});
+      std::max({p_in.ws_bytes, gemm_workspace_bound(rows, D, D, prec), nf * attn_ws});
   char* w = static_cast<char*>(dev_scratch(c, off_g + g_bytes, s));
   float* qkv = reinterpret_cast<float*>(w + off_qkv);
   float* ctx = reinterpret_cast<float*>(w + off_ctx);
@@ -328,13 +331,36 @@ void mha_dev(const float* x, int batch, int T, int D, const float* W_in, const f
   // 1) [Q|K|V] = x . W_in^T + b_in   (src/attn_dispatch.cpp:63-95)
   gemm_run(p_in, x, D, true, W_in, D, true, qkv, 3 * D, 1.f, 0.f, b_in, gws, c.status, c.num_sms, s);
   // 2) per-sequence attention over the head-strided projections (:98-107)
-  for (int b = 0; b < batch; ++b) {
+  auto attend = [&](int b, cudaStream_t st, void* ws) {
     const float* base = qkv + (size_t)b * T * 3 * D;
     attnb_tensor q{base, H, T, Dh, Dh, 3 * D, 1};
     attnb_tensor k{base + D, H, T, Dh, Dh, 3 * D, 1};
     attnb_tensor v{base + 2 * D, H, T, Dh, Dh, 3 * D, 1};
     attnb_mtensor o{ctx + (size_t)b * T * D, H, T, Dh, Dh, D, 1};
-    block_dev(&q, &k, &v, &o, causal, prec, c, s, gws);
+    block_dev(&q, &k, &v, &o, causal, prec, c, st, ws);
+  };
+  if (nf == 1) {
+    attend(0, s, gws);
+  } else {
+    // Sequence b runs on fork b % nf, after the projection; the output
+    // projection waits for every fork.
+    ForkStreams& f = fork_streams(c);
+    std::lock_guard<std::mutex> g(f.mu);
+    try {
+      ATTNB_CUDA(cudaEventRecord(f.fork, s));
+      for (int i = 0; i < nf; ++i) ATTNB_CUDA(cudaStreamWaitEvent(f.s[i], f.fork, 0));
+      for (int b = 0; b < batch; ++b)
+        attend(b, f.s[b % nf], static_cast<char*>(gws) + (b % nf) * attn_ws);
+      for (int i = 0; i < nf; ++i) {
+        ATTNB_CUDA(cudaEventRecord(f.join[i], f.s[i]));
+        ATTNB_CUDA(cudaStreamWaitEvent(s, f.join[i], 0));
+      }
+    } catch (...) {
+      // Nothing queued on a fork may still use the scratch after an error.
+      for (int i = 0; i < nf; ++i) cudaStreamSynchronize(f.s[i]);
+      cudaGetLastError();
+      throw;
+    }
   }
   // 3) y = ctx . W_out^T + b_out   (:110-127)
   const GemmPlan p_out = gemm_plan(rows, D, D, prec);

@@ -86,6 +86,21 @@ void ensure_copy_streams(DeviceCtx& c) {
   ATTNB_CUDA(cudaEventCreateWithFlags(&c.ev_out, cudaEventDisableTiming));  // last: the guard
 }
 
+ForkStreams& fork_streams(DeviceCtx& c) {
+  static std::mutex create_mu;
+  std::lock_guard<std::mutex> g(create_mu);
+  if (!c.forks) {
+    auto f = std::make_unique<ForkStreams>();
+    for (int i = 0; i < ForkStreams::kForks; ++i) {
+      ATTNB_CUDA(cudaStreamCreateWithFlags(&f->s[i], cudaStreamNonBlocking));
+      ATTNB_CUDA(cudaEventCreateWithFlags(&f->join[i], cudaEventDisableTiming));
+    }
+    ATTNB_CUDA(cudaEventCreateWithFlags(&f->fork, cudaEventDisableTiming));
+    c.forks = f.release();  // lives as long as the context
+  }
+  return *c.forks;
+}
+
 void* dev_scratch(DeviceCtx& c, size_t bytes, cudaStream_t stream) {
   if (bytes == 0) return nullptr;
   std::lock_guard<std::mutex> g(c.scratch_mu);

@@ -52,10 +52,23 @@ struct DeviceCtx {
   cudaStream_t h2d = nullptr, d2h = nullptr;
   cudaEvent_t ev_start = nullptr, ev_out = nullptr;
   cudaEvent_t ev_in[kMaxGroups] = {}, ev_k[kMaxGroups] = {};
+  struct ForkStreams* forks = nullptr;
 };
 
 // Creates ctx's copy streams and events on first use (hold ctx.mu).
 void ensure_copy_streams(DeviceCtx& c);
+
+// Streams that the batched MHA runs its per-sequence attention on, side by
+// side (the tail of one sequence's CTAs overlaps the next one's), and the
+// events that fork them from and join them back to the caller's stream.
+struct ForkStreams {
+  static constexpr int kForks = 4;
+  std::mutex mu;  // held while a call enqueues on them
+  cudaStream_t s[kForks] = {};
+  cudaEvent_t fork = nullptr, join[kForks] = {};
+};
+// ctx's fork streams, created on first use (hold the returned object's mu).
+ForkStreams& fork_streams(DeviceCtx& c);
 
 // Context of the current CUDA device (created on first use).
 DeviceCtx& current_ctx();
