@@ -975,6 +975,25 @@ AttnTcPlan attn_tc_plan(int H, int L, int T, int Dh, bool causal, int precision,
   const int waves_pp = (H * ((p.qtiles + 1) / 2) + num_sms - 1) / num_sms;
   p.pairs = pairs_on && !p.split3 && p.nsplit == 1 && p.qtiles >= 2 && n_kv >= 2 &&
             waves_pp * 1.45 < waves_k3;
+  static const bool cta_pairs_on = [] {
+    const char* e = std::getenv("ATTNB_ATTN_CTA_PAIRS");
+    return !(e && std::strcmp(e, "0") == 0);
+  }();
+  // K3q runs a key tile per CTA in about 4.8 K cycles (one query tile per
+  // CTA); K3p in 9.0 K (two), K3 in 7.0 K (one), measured at head size 128 on
+  // full waves.  K3q is taken when its waves of CTAs, so weighted, beat the
+  // other two by 10 % or more, it fills at least one wave, and the key range
+  // is long (eight tiles or more): with fewer CTAs or fewer tiles it
+  // measured slower than the per-tile figure says.
+  if (!p.split3 && !causal && p.nsplit == 1 && p.qtiles >= 2 && n_kv >= 8 && p.dhp == 128) {
+    const int ctas_q = H * ((p.qtiles + 1) / 2) * 2;
+    const double t_q = 4.8 * ((ctas_q + num_sms - 1) / num_sms);
+    const double t_pp = 9.0 * waves_pp, t_k3 = 7.0 * waves_k3;
+    p.cta_pairs = cta_pairs_on && ctas_q >= num_sms && t_q <= 0.9 * std::min(t_pp, t_k3);
+  } else {
+    p.cta_pairs = false;
+  }
+  if (p.cta_pairs) p.pairs = false;
   size_t off = 0;
   auto take = [&](size_t bytes) {
     const size_t o = off;
@@ -1047,9 +1066,21 @@ void attn_tc_run(const AttnTcPlan& p, const View3& Q, const View3& K, const View
   const bool o_tma = O.sD == 1 && (reinterpret_cast<uintptr_t>(O.data) & 15u) == 0 &&
                      (O.sT % 4) == 0 && (O.sH % 4) == 0 && O.sT > 0 && O.sH > 0;
   if (o_tma) maps[6] = make_tmap_3d(O.data, p.H, p.L, p.Dh, O.sT, O.sH, BM, 32);
-  if (p.pairs) {
+  if (p.pairs || p.cta_pairs) {
     const AttnPPArgs a{p.L, p.T, p.H, p.Dh, causal ? 1 : 0, p.qtiles, o_tma ? 1 : 0,
                        O.data, O.sH, O.sT, O.sD, status};
+    if (p.cta_pairs) {
+      // Each CTA of a pair loads 64 keys of every K tile and dhp/2 rows of V^T.
+      const float* kh = reinterpret_cast<const float*>(w + p.off_k);
+      const float* vh = reinterpret_cast<const float*>(w + p.off_v);
+      const CUtensorMap k_half =
+          make_tmap_3d(kh, p.H, p.T, p.dhp, p.dhp, (uint64_t)p.T * p.dhp, BN / 2, BK);
+      const CUtensorMap v_half =
+          make_tmap_3d(vh, p.H, p.dhp, p.tp, p.tp, (uint64_t)p.dhp * p.tp, p.dhp / 2, BK);
+      ProfScope prof("attn_tc", s);
+      attn_pair_launch(p.dhp, maps[0], k_half, v_half, maps[6], a, s);
+      return;
+    }
     ProfScope prof("attn_tc", s);
     attn_pp_launch(p.dhp, maps[0], maps[2], maps[4], maps[6], a, s);
     return;

@@ -52,6 +52,9 @@ struct AttnTcPlan {
   // 1xTF32 with at least two query tiles and two key tiles: K3p (attn_pp.cu),
   // two query tiles per CTA.  ATTNB_ATTN_PAIRS=0 keeps K3.
   bool pairs;
+  // 1xTF32, non-causal, head size 128: K3q (attn_pair.cu) on CTA pairs.
+  // ATTNB_ATTN_CTA_PAIRS=0 turns it off.
+  bool cta_pairs;
   size_t off_q, off_k, off_v, ws_bytes;
 };
 // Head sizes the tensor-core kernel takes (padded to a multiple of 32, <= 128).
@@ -73,6 +76,13 @@ struct AttnPPArgs {
 };
 void attn_pp_launch(int dhp, const CUtensorMap& q, const CUtensorMap& k, const CUtensorMap& v,
                     const CUtensorMap& o, const AttnPPArgs& a, cudaStream_t s);
+
+// K3q: 1xTF32 prefill on CTA pairs (attn_pair.cu), head size 128.  Maps: Q as
+// for K3p, K [H, T, dhp] box 64 x 32, V^T [H, dhp, tp] box dhp/2 x 32, O box
+// 128 x 32 (o_tma).
+void attn_pair_launch(int dhp, const CUtensorMap& q, const CUtensorMap& k_half,
+                      const CUtensorMap& v_half, const CUtensorMap& o, const AttnPPArgs& a,
+                      cudaStream_t s);
 
 // ------------------------------------------------ operand packing (K2)
 // One packing job: a strided 3-D source src[h][r][c] (r < R, c < C), times
