@@ -19,7 +19,7 @@
 //   allocation (both CTAs) and, on rank 0, the MMA issuer.  Warps 2-5: one
 //   query row per thread, the whole 128-key row of S in registers (as in
 //   K3p); P overwrites S in TMEM and is read by the P.V product from there.
-//   Rank 0's product commits arrive on both CTAs' barriers (multicast); the
+//   Rank 0's product commits arrive on both CTAs' barriers at once; the
 //   softmax warps of both CTAs arrive on rank 0's P barrier.
 //
 //   O stays in TMEM; the max m used for P moves only when a row's tile max
@@ -152,7 +152,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
     wg_fail = 0;
     for (int i = 0; i < KST; ++i) {
       mbar_init(smem_addr(&kfull[i]), 1);   // rank 0: expect_tx for both halves
-      mbar_init(smem_addr(&kempty[i]), 1);  // a product commit (multicast)
+      mbar_init(smem_addr(&kempty[i]), 1);  // a product commit (both CTAs)
     }
     for (int i = 0; i < VST; ++i) {
       mbar_init(smem_addr(&vfull[i]), 1);
