@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
       if (ok) ok = issue_s(0);
       if (ok && n > 1) ok = issue_s(1);
       for (int j = 0; ok && j < n; ++j) {
-        if (!mbar_wait(smem_addr(&p_bar[j & 1]), (j >> 1) & 1, abort_p, p.status)) break;
+        if (!mbar_wait_cluster(smem_addr(&p_bar[j & 1]), (j >> 1) & 1, abort_p, p.status)) break;
         tc_fence_after();
         const uint32_t sbuf = tmem + (j & 1) * BN;
         const int nvb = slices_of(j);

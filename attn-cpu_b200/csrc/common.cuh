@@ -57,6 +57,19 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// Same, with cluster-scope acquire: for barriers that the other CTA of a
+// cluster arrives on after writing its own shared memory or TMEM.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
 // Wait until the phase with the given parity has completed.  Returns false
 // (and leaves the abort flag set) when the limit expires or another thread of
 // the CTA has already aborted.
@@ -78,6 +91,19 @@ __device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity,
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
                                           int* status) {
   return mbar_wait_limit(bar, parity, abort_flag, status, ATTNB_WAIT_LIMIT_NS);
+}
+__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity,
+                                                  volatile int* abort_flag, int* status) {
+  const uint64_t t0 = globaltimer();
+  while (!mbar_try_wait_cluster(bar, parity)) {
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > ATTNB_WAIT_LIMIT_NS) {
+      *abort_flag = 1;
+      raise_timeout(status);
+      return false;
+    }
+  }
+  return true;
 }
 
 // Position in a ring of N stages (stage index and the phase parity to wait on).
