@@ -10,10 +10,9 @@ here follow the work's natural independence:
 * the MHA block (attn::mha_block_dense, src/attn_dispatch.cpp:17-133): rank r
   owns heads [h0, h1): it projects only its heads' Q/K/V rows of W_in
   (column-parallel QKV), runs their attention, then an all-gather of the
-  per-head context rebuilds ctx [T, D] on every rank, each rank computes the
-  output projection for its own column block of y, and a second all-gather
-  assembles y.  Every output element is summed in the same order as on one
-  GPU;
+  per-head context rebuilds ctx^T [D, T] on every rank, each rank computes
+  its own row block of y^T = W_out ctx^T, and a second all-gather assembles
+  y^T; one transpose (with b_out added) gives y;
 * SGEMM (gemm::sgemm_blocked, src/gemm.cpp:319-415): rank r computes a block
   of C -- a block of rows (A row block x all of B; the all-gather is then
   contiguous) or, as `shard="cols"`, a block of columns (all of A x a column
@@ -93,7 +92,6 @@ class _HeadShard:
     W_in: torch.Tensor   # [3 * (h1-h0) * Dh, D]: this rank's Q, K, V rows
     b_in: torch.Tensor
     W_out: torch.Tensor  # [c1-c0, D]: this rank's rows of W_out (columns of y)
-    b_out: torch.Tensor
     c0: int
     c1: int
 
@@ -102,7 +100,8 @@ class ShardedMHA:
     """mha_block_dense with heads partitioned across the ranks of `group`.
 
     Weights are sliced once at construction (W_in rows of the local heads,
-    W_out rows of the local output columns); `forward(x)` takes x [T, D] or
+    W_out rows of the local output columns; b_out is added whole after the
+    last gather); `forward(x)` takes x [T, D] or
     [B, T, D] (identical on every rank) and returns the full y on every rank.
     """
 
@@ -126,7 +125,8 @@ class ShardedMHA:
         c0, c1 = shard_range(D, rank, world)
         self.shard = _HeadShard(h0, h1, torch.cat(rows, 0).contiguous(),
                                 torch.cat(bias, 0).contiguous(),
-                                W_out[c0:c1].contiguous(), b_out[c0:c1].contiguous(), c0, c1)
+                                W_out[c0:c1].contiguous(), c0, c1)
+        self.b_out = b_out.contiguous()
         self.head_counts = [shard_range(num_heads, r, world)[1] - shard_range(num_heads, r, world)[0]
                             for r in range(world)]
         self.col_counts = [shard_range(D, r, world)[1] - shard_range(D, r, world)[0]
@@ -145,9 +145,9 @@ class ShardedMHA:
         qkv = torch.empty(rows, 3 * hl * Dh, dtype=x.dtype, device=x.device)
         if hl:
             self.ops.linear(x2, s.W_in, s.b_in, qkv)
+        qkv3 = qkv.view(B, T, 3 * hl * Dh)
         # 2) attention of the local heads, per sequence
         ctx_local = torch.empty(B, T, hl * Dh, dtype=x.dtype, device=x.device)
-        qkv3 = qkv.view(B, T, 3 * hl * Dh)
         for b in range(B):
             if not hl:
                 break
@@ -155,17 +155,19 @@ class ShardedMHA:
                 return qkv3[b, :, p * hl * Dh:(p + 1) * hl * Dh].reshape(T, hl, Dh).permute(1, 0, 2)
             o = ctx_local[b].view(T, hl, Dh).permute(1, 0, 2)
             self.ops.attention(heads(0), heads(1), heads(2), o, self.causal)
-        # 3) all-gather the context: [world][B, T, hl_r * Dh] -> ctx [B, T, D]
-        parts = _all_gather_rows(ctx_local.permute(2, 0, 1).reshape(hl * Dh, rows),
-                                 [c * Dh for c in self.head_counts], self.group)
-        ctx = parts.reshape(D, rows).t().contiguous()
-        # 4) local output columns, then all-gather y's column blocks
-        yl = torch.empty(rows, s.c1 - s.c0, dtype=x.dtype, device=x.device)
+        # 3) all-gather the context as ctx^T: [world][hl_r * Dh, B*T] -> [D, B*T]
+        ctxT = _all_gather_rows(ctx_local.view(rows, hl * Dh).t().contiguous(),
+                                [c * Dh for c in self.head_counts], self.group)
+        # 4) this rank's rows of y^T = W_out[c0:c1] ctx^T (read in the gathered
+        #    layout, no transpose), all-gathered into y^T [D, B*T]; the one
+        #    transpose back to y adds b_out.
+        yT = torch.empty(s.c1 - s.c0, rows, dtype=x.dtype, device=x.device)
         if s.c1 > s.c0:
-            self.ops.linear(ctx, s.W_out, s.b_out, yl)
-        yc = _all_gather_rows(yl.t().contiguous(), self.col_counts, self.group)  # [D, rows]
-        y = yc.t().reshape(B, T, D)
-        return y[0] if squeeze else y.contiguous()
+            self.ops.sgemm(s.W_out, ctxT, yT)
+        yT = _all_gather_rows(yT, self.col_counts, self.group)
+        y = torch.empty(B, T, D, dtype=x.dtype, device=x.device)
+        torch.add(yT.t().view(B, T, D), self.b_out, out=y)
+        return y[0] if squeeze else y
 
 
 def gemm_sharded(A: torch.Tensor, B: torch.Tensor, group=None, ops=None,
