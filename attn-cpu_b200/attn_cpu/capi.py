@@ -24,7 +24,7 @@ PREC = {None: -1, "default": -1, "3xtf32": 0, "tf32": 1}
 EXPORTED = [
     "attnb_last_error", "attnb_version", "attnb_stream_status", "attnb_selftest_wait_timeout",
     "attnb_profile_enable", "attnb_profile_read", "attnb_host_alloc", "attnb_host_free",
-    "attnb_sgemm", "attnb_gemm_jit", "attnb_sgemm_dev", "attnb_linear_dev",
+    "attnb_sgemm", "attnb_gemm_jit", "attnb_sgemm_dev", "attnb_gemm_ex_dev", "attnb_linear_dev",
     "attnb_attn_step_dense", "attnb_attn_step_dense_dev", "attnb_attn_step_dense_noalloc",
     "attnb_attn_block_dense", "attnb_attn_block_dense_dev",
     "attnb_mha_block_dense", "attnb_mha_block_dense_dev",
@@ -71,6 +71,7 @@ def lib() -> ctypes.CDLL:
         L.attnb_gemm_jit.argtypes = [vp, i, i, vp, i, vp, f, f, i]
         L.attnb_sgemm_dev.argtypes = [vp, i, vp, i, vp, i, i, i, i, f, f, i, vp]
         L.attnb_linear_dev.argtypes = [vp, i, vp, i, vp, vp, i, i, i, i, i, vp]
+        L.attnb_gemm_ex_dev.argtypes = [i, i, vp, i, vp, i, vp, vp, i, i, i, i, f, f, i, vp]
         L.attnb_attn_step_dense.argtypes = [T, T, T, T]
         L.attnb_attn_step_dense_dev.argtypes = [T, T, T, T, vp]
         L.attnb_attn_step_dense_noalloc.argtypes = [T, T, T, T, vp]
@@ -120,6 +121,25 @@ def sgemm_dev(A, B, C, alpha=1.0, beta=0.0, precision=None, stream=None) -> None
     check(lib().attnb_sgemm_dev(A.data_ptr(), A.stride(0), B.data_ptr(), B.stride(0),
                                 C.data_ptr(), C.stride(0), M, N, K, alpha, beta,
                                 PREC[precision], _stream(stream)))
+
+
+def gemm_ex_dev(A, B, C, trans_a=False, trans_b=False, bias=None, alpha=1.0, beta=0.0,
+                precision=None, stream=None) -> None:
+    """C = alpha * op(A) @ op(B) + beta * C + bias, op(X) = X.T when trans_x.
+    A, B, C: 2-D float32 CUDA tensors with unit column stride (A and B may be
+    column slices: their row pitch is passed as the leading dimension)."""
+    M = A.shape[1] if trans_a else A.shape[0]
+    K = A.shape[0] if trans_a else A.shape[1]
+    N = B.shape[0] if trans_b else B.shape[1]
+    if (B.shape[1] if trans_b else B.shape[0]) != K or tuple(C.shape) != (M, N):
+        raise ValueError("gemm_ex_dev: shapes do not match")
+    if A.stride(1) != 1 or B.stride(1) != 1 or C.stride(1) != 1:
+        raise ValueError("gemm_ex_dev: operands need a unit column stride")
+    check(lib().attnb_gemm_ex_dev(int(trans_a), int(trans_b), A.data_ptr(), A.stride(0),
+                                  B.data_ptr(), B.stride(0),
+                                  bias.data_ptr() if bias is not None else None, C.data_ptr(),
+                                  C.stride(0), M, N, K, alpha, beta, PREC[precision],
+                                  _stream(stream)))
 
 
 def linear_dev(x, W, b, y, precision=None, stream=None) -> None:

@@ -10,9 +10,10 @@ here follow the work's natural independence:
 * the MHA block (attn::mha_block_dense, src/attn_dispatch.cpp:17-133): rank r
   owns heads [h0, h1): it projects only its heads' Q/K/V rows of W_in
   (column-parallel QKV), runs their attention, then an all-gather of the
-  per-head context rebuilds ctx^T [D, T] on every rank, each rank computes
-  its own row block of y^T = W_out ctx^T, and a second all-gather assembles
-  y^T; one transpose (with b_out added) gives y;
+  per-head context rebuilds ctx^T [D, T] on every rank (the attention writes
+  its rows straight into the transposed send buffer), each rank computes a
+  block of y's rows from ctx^T read transposed (y = ctx W_out^T + b_out, the
+  single-GPU product), and a second all-gather of those rows assembles y;
 * SGEMM (gemm::sgemm_blocked, src/gemm.cpp:319-415): rank r computes a block
   of C -- a block of rows (A row block x all of B; the all-gather is then
   contiguous) or, as `shard="cols"`, a block of columns (all of A x a column
@@ -58,6 +59,10 @@ class DeviceOps:
     def sgemm(self, A, B, C):
         self.capi.sgemm_dev(A, B, C, precision=self.precision)
 
+    def gemm_ex(self, A, B, C, trans_a, trans_b, bias):
+        self.capi.gemm_ex_dev(A, B, C, trans_a=trans_a, trans_b=trans_b, bias=bias,
+                              precision=self.precision)
+
 
 def _world(group):
     if not dist.is_available() or not dist.is_initialized():
@@ -91,17 +96,13 @@ class _HeadShard:
     h1: int
     W_in: torch.Tensor   # [3 * (h1-h0) * Dh, D]: this rank's Q, K, V rows
     b_in: torch.Tensor
-    W_out: torch.Tensor  # [c1-c0, D]: this rank's rows of W_out (columns of y)
-    c0: int
-    c1: int
 
 
 class ShardedMHA:
     """mha_block_dense with heads partitioned across the ranks of `group`.
 
-    Weights are sliced once at construction (W_in rows of the local heads,
-    W_out rows of the local output columns; b_out is added whole after the
-    last gather); `forward(x)` takes x [T, D] or
+    W_in is sliced once at construction (the rows of the local heads); every
+    rank keeps all of W_out and b_out for its block of y's rows; `forward(x)` takes x [T, D] or
     [B, T, D] (identical on every rank) and returns the full y on every rank.
     """
 
@@ -122,15 +123,12 @@ class ShardedMHA:
         Dh = self.Dh
         rows = [W_in[p * D + h0 * Dh:p * D + h1 * Dh] for p in range(3)]
         bias = [b_in[p * D + h0 * Dh:p * D + h1 * Dh] for p in range(3)]
-        c0, c1 = shard_range(D, rank, world)
         self.shard = _HeadShard(h0, h1, torch.cat(rows, 0).contiguous(),
-                                torch.cat(bias, 0).contiguous(),
-                                W_out[c0:c1].contiguous(), c0, c1)
+                                torch.cat(bias, 0).contiguous())
+        self.W_out = W_out.contiguous()
         self.b_out = b_out.contiguous()
         self.head_counts = [shard_range(num_heads, r, world)[1] - shard_range(num_heads, r, world)[0]
                             for r in range(world)]
-        self.col_counts = [shard_range(D, r, world)[1] - shard_range(D, r, world)[0]
-                           for r in range(world)]
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         squeeze = x.dim() == 2
@@ -146,27 +144,27 @@ class ShardedMHA:
         if hl:
             self.ops.linear(x2, s.W_in, s.b_in, qkv)
         qkv3 = qkv.view(B, T, 3 * hl * Dh)
-        # 2) attention of the local heads, per sequence
-        ctx_local = torch.empty(B, T, hl * Dh, dtype=x.dtype, device=x.device)
+        # 2) attention of the local heads, per sequence, written transposed
+        #    into the all-gather's send buffer: ctx_local^T [hl * Dh, B*T]
+        ctxT_local = torch.empty(hl * Dh, rows, dtype=x.dtype, device=x.device)
         for b in range(B):
             if not hl:
                 break
             def heads(p):
                 return qkv3[b, :, p * hl * Dh:(p + 1) * hl * Dh].reshape(T, hl, Dh).permute(1, 0, 2)
-            o = ctx_local[b].view(T, hl, Dh).permute(1, 0, 2)
+            o = ctxT_local[:, b * T:(b + 1) * T].view(hl, Dh, T).permute(0, 2, 1)
             self.ops.attention(heads(0), heads(1), heads(2), o, self.causal)
-        # 3) all-gather the context as ctx^T: [world][hl_r * Dh, B*T] -> [D, B*T]
-        ctxT = _all_gather_rows(ctx_local.view(rows, hl * Dh).t().contiguous(),
-                                [c * Dh for c in self.head_counts], self.group)
-        # 4) this rank's rows of y^T = W_out[c0:c1] ctx^T (read in the gathered
-        #    layout, no transpose), all-gathered into y^T [D, B*T]; the one
-        #    transpose back to y adds b_out.
-        yT = torch.empty(s.c1 - s.c0, rows, dtype=x.dtype, device=x.device)
-        if s.c1 > s.c0:
-            self.ops.sgemm(s.W_out, ctxT, yT)
-        yT = _all_gather_rows(yT, self.col_counts, self.group)
-        y = torch.empty(B, T, D, dtype=x.dtype, device=x.device)
-        torch.add(yT.t().view(B, T, D), self.b_out, out=y)
+        # 3) all-gather: [world][hl_r * Dh, B*T] -> ctx^T [D, B*T]
+        ctxT = _all_gather_rows(ctxT_local, [c * Dh for c in self.head_counts], self.group)
+        # 4) this rank's rows of y = ctx W_out^T + b_out, reading ctx^T
+        #    transposed, then an all-gather of the row blocks
+        r0, r1 = shard_range(rows, self.rank, self.world)
+        y_rows = torch.empty(r1 - r0, D, dtype=x.dtype, device=x.device)
+        if r1 > r0:
+            self.ops.gemm_ex(ctxT[:, r0:r1], self.W_out, y_rows, True, True, self.b_out)
+        counts = [shard_range(rows, r, self.world)[1] - shard_range(rows, r, self.world)[0]
+                  for r in range(self.world)]
+        y = _all_gather_rows(y_rows, counts, self.group).view(B, T, D)
         return y[0] if squeeze else y
 
 

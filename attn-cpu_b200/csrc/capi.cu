@@ -432,6 +432,27 @@ int attnb_sgemm_dev(const float* A, int lda, const float* B, int ldb, float* C, 
   });
 }
 
+int attnb_gemm_ex_dev(int trans_a, int trans_b, const float* A, int lda, const float* B, int ldb,
+                      const float* bias, float* C, int ldc, int M, int N, int K, float alpha,
+                      float beta, int precision, void* stream) {
+  return guarded([&] {
+    if (M <= 0 || N <= 0 || K <= 0) return;
+    if (!A || !B || !C) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    if ((trans_a != 0 && trans_a != 1) || (trans_b != 0 && trans_b != 1))
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "trans_a and trans_b must be 0 or 1");
+    if (lda < (trans_a ? M : K) || ldb < (trans_b ? K : N) || ldc < N)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "leading dimension smaller than the row length");
+    const int prec = resolve_precision(precision);
+    DeviceCtx& c = current_ctx();
+    cudaStream_t s = as_stream(stream);
+    const GemmPlan p = gemm_plan(M, N, K, prec);
+    void* ws = dev_scratch(c, p.ws_bytes, s);
+    gemm_run(p, A, lda, trans_a == 0, B, ldb, trans_b == 1, C, ldc, alpha, beta, bias, ws,
+             c.status, c.num_sms, s);
+    ATTNB_CUDA(cudaGetLastError());
+  });
+}
+
 int attnb_linear_dev(const float* x, int ldx, const float* W, int ldw, const float* b, float* y,
                      int ldy, int T, int N, int K, int precision, void* stream) {
   return guarded([&] {

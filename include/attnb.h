@@ -119,6 +119,17 @@ ATTNB_API int attnb_sgemm_dev(const float* A, int lda, const float* B, int ldb, 
                     int M, int N, int K, float alpha, float beta, int precision,
                     void* stream);
 
+/* C[M,N] = alpha * op(A) . op(B) + beta * C + bias[N] on device pointers.
+ * op(A) is A stored [M,K] (trans_a = 0, lda >= K) or A^T with A stored [K,M]
+ * (trans_a = 1, lda >= M); op(B) is B stored [K,N] (trans_b = 0, ldb >= N) or
+ * B^T with B stored [N,K] (trans_b = 1, ldb >= K); ldc >= N; bias may be
+ * NULL.  No reference counterpart: the reference's GEMMs take row-major
+ * operands only (include/gemm.h:11-20).  The sharded MHA block uses it to read
+ * the all-gathered context in its transposed layout. */
+ATTNB_API int attnb_gemm_ex_dev(int trans_a, int trans_b, const float* A, int lda, const float* B,
+                      int ldb, const float* bias, float* C, int ldc, int M, int N, int K,
+                      float alpha, float beta, int precision, void* stream);
+
 /* y[T,N] = x[T,K] . W[N,K]^T + b[N] on device pointers (b may be NULL).
  * The projection step of attn::mha_block_dense (src/attn_dispatch.cpp:45-95,
  * include/gemm_16x16.h:7-60, include/pack_16x16.h:9-25); ldx >= K, ldw >= K,

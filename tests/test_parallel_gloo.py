@@ -35,6 +35,14 @@ class CPUOps:
     def sgemm(self, A, B, C):
         C.copy_((A.double() @ B.double()).to(C.dtype))
 
+    def gemm_ex(self, A, B, C, trans_a, trans_b, bias):
+        a = A.double().t() if trans_a else A.double()
+        b = B.double().t() if trans_b else B.double()
+        r = a @ b
+        if bias is not None:
+            r = r + bias.double()
+        C.copy_(r.to(C.dtype))
+
 
 def _free_port() -> int:
     with socket.socket() as s:
