@@ -27,6 +27,7 @@ EXPORTED = [
     "attnb_sgemm", "attnb_gemm_jit", "attnb_sgemm_dev", "attnb_gemm_ex_dev", "attnb_linear_dev",
     "attnb_attn_step_dense", "attnb_attn_step_dense_dev", "attnb_attn_step_dense_noalloc",
     "attnb_attn_block_dense", "attnb_attn_block_dense_dev",
+    "attnb_attn_block_dense_batched_dev",
     "attnb_mha_block_dense", "attnb_mha_block_dense_dev",
     "attnb_kv_cache_create", "attnb_kv_cache_destroy", "attnb_kv_cache_length",
     "attnb_kv_cache_truncate", "attnb_kv_cache_append", "attnb_kv_cache_step",
@@ -77,6 +78,8 @@ def lib() -> ctypes.CDLL:
         L.attnb_attn_step_dense_noalloc.argtypes = [T, T, T, T, vp]
         L.attnb_attn_block_dense.argtypes = [T, T, T, T, i, i]
         L.attnb_attn_block_dense_dev.argtypes = [T, T, T, T, i, i, vp]
+        L.attnb_attn_block_dense_batched_dev.argtypes = [T, T, T, T, i, i64, i64, i64, i64, i, i,
+                                                         vp]
         L.attnb_mha_block_dense.argtypes = [vp, i, i, vp, vp, vp, vp, i, i, vp, i]
         L.attnb_mha_block_dense_dev.argtypes = [vp, i, i, i, vp, vp, vp, vp, i, i, vp, i, vp]
         L.attnb_kv_cache_create.argtypes = [i, i, i, ctypes.POINTER(vp)]
@@ -170,6 +173,22 @@ def attn_block_dense_dev(Q, K, V, O, causal=False, precision=None, stream=None) 
     check(lib().attnb_attn_block_dense_dev(ctypes.byref(q), ctypes.byref(k), ctypes.byref(v),
                                            ctypes.byref(o), int(causal), PREC[precision],
                                            _stream(stream)))
+
+
+def attn_block_dense_batched_dev(Q, K, V, O, causal=False, precision=None, stream=None) -> None:
+    """Prefill for independent sequences: Q, O [B, H, L, Dh] and K, V [B, H, T, Dh]
+    float32 CUDA views (any strides); the sequences run side by side."""
+    if not (Q.dim() == K.dim() == V.dim() == O.dim() == 4):
+        raise ValueError("attn_block_dense_batched_dev: 4-D views [B, H, T, Dh] expected")
+    B = Q.shape[0]
+    if K.shape[0] != B or V.shape[0] != B or O.shape[0] != B:
+        raise ValueError("attn_block_dense_batched_dev: batch sizes differ")
+    if B == 0:
+        return
+    q, k, v, o = tensor3(Q[0]), tensor3(K[0]), tensor3(V[0]), tensor3(O[0])
+    check(lib().attnb_attn_block_dense_batched_dev(
+        ctypes.byref(q), ctypes.byref(k), ctypes.byref(v), ctypes.byref(o), B, Q.stride(0),
+        K.stride(0), V.stride(0), O.stride(0), int(causal), PREC[precision], _stream(stream)))
 
 
 def mha_block_dense_dev(x, W_in, b_in, W_out, b_out, num_heads, y, causal=False,

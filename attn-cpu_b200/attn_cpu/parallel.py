@@ -56,6 +56,10 @@ class DeviceOps:
     def attention(self, q, k, v, o, causal):
         self.capi.attn_block_dense_dev(q, k, v, o, causal=causal, precision=self.precision)
 
+    def attention_batched(self, q, k, v, o, causal):
+        self.capi.attn_block_dense_batched_dev(q, k, v, o, causal=causal,
+                                               precision=self.precision)
+
     def sgemm(self, A, B, C):
         self.capi.sgemm_dev(A, B, C, precision=self.precision)
 
@@ -144,16 +148,15 @@ class ShardedMHA:
         if hl:
             self.ops.linear(x2, s.W_in, s.b_in, qkv)
         qkv3 = qkv.view(B, T, 3 * hl * Dh)
-        # 2) attention of the local heads, per sequence, written transposed
-        #    into the all-gather's send buffer: ctx_local^T [hl * Dh, B*T]
+        # 2) attention of the local heads, all sequences in one call, written
+        #    transposed into the all-gather's send buffer ctx_local^T [hl * Dh, B*T]
         ctxT_local = torch.empty(hl * Dh, rows, dtype=x.dtype, device=x.device)
-        for b in range(B):
-            if not hl:
-                break
-            def heads(p):
-                return qkv3[b, :, p * hl * Dh:(p + 1) * hl * Dh].reshape(T, hl, Dh).permute(1, 0, 2)
-            o = ctxT_local[:, b * T:(b + 1) * T].view(hl, Dh, T).permute(0, 2, 1)
-            self.ops.attention(heads(0), heads(1), heads(2), o, self.causal)
+        if hl:
+            def heads(p):  # [B, hl, T, Dh] view of the Q, K or V columns
+                return qkv3[:, :, p * hl * Dh:(p + 1) * hl * Dh].view(B, T, hl, Dh).permute(
+                    0, 2, 1, 3)
+            o = ctxT_local.view(hl, Dh, B, T).permute(2, 0, 3, 1)
+            self.ops.attention_batched(heads(0), heads(1), heads(2), o, self.causal)
         # 3) all-gather: [world][hl_r * Dh, B*T] -> ctx^T [D, B*T]
         ctxT = _all_gather_rows(ctxT_local, [c * Dh for c in self.head_counts], self.group)
         # 4) this rank's rows of y = ctx W_out^T + b_out, reading ctx^T

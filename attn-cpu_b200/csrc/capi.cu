@@ -304,6 +304,36 @@ void block_host_overlapped(const attnb_tensor* Q, const attnb_tensor* K, const a
   });
 }
 
+// Runs attend(b, stream, scratch) for b in [0, batch): with one fork it runs
+// on s with scratch ws; otherwise sequence b runs on fork b % nf with its own
+// attn_ws-byte slice of ws, the forks start after the work already queued on
+// s, and s waits for all of them.
+template <class F>
+void run_forked(DeviceCtx& c, cudaStream_t s, int batch, int nf, void* ws, size_t attn_ws,
+                F&& attend) {
+  if (nf == 1) {
+    for (int b = 0; b < batch; ++b) attend(b, s, ws);
+    return;
+  }
+  ForkStreams& f = fork_streams(c);
+  std::lock_guard<std::mutex> g(f.mu);
+  try {
+    ATTNB_CUDA(cudaEventRecord(f.fork, s));
+    for (int i = 0; i < nf; ++i) ATTNB_CUDA(cudaStreamWaitEvent(f.s[i], f.fork, 0));
+    for (int b = 0; b < batch; ++b)
+      attend(b, f.s[b % nf], static_cast<char*>(ws) + (b % nf) * attn_ws);
+    for (int i = 0; i < nf; ++i) {
+      ATTNB_CUDA(cudaEventRecord(f.join[i], f.s[i]));
+      ATTNB_CUDA(cudaStreamWaitEvent(s, f.join[i], 0));
+    }
+  } catch (...) {
+    // Nothing queued on a fork may still use the scratch after an error.
+    for (int i = 0; i < nf; ++i) cudaStreamSynchronize(f.s[i]);
+    cudaGetLastError();
+    throw;
+  }
+}
+
 // -------------------------------------------------------------------- MHA
 void mha_dev(const float* x, int batch, int T, int D, const float* W_in, const float* b_in,
              const float* W_out, const float* b_out, int H, int causal, float* y, int prec,
@@ -339,29 +369,9 @@ void mha_dev(const float* x, int batch, int T, int D, const float* W_in, const f
     attnb_mtensor o{ctx + (size_t)b * T * D, H, T, Dh, Dh, D, 1};
     block_dev(&q, &k, &v, &o, causal, prec, c, st, ws);
   };
-  if (nf == 1) {
-    attend(0, s, gws);
-  } else {
-    // Sequence b runs on fork b % nf, after the projection; the output
-    // projection waits for every fork.
-    ForkStreams& f = fork_streams(c);
-    std::lock_guard<std::mutex> g(f.mu);
-    try {
-      ATTNB_CUDA(cudaEventRecord(f.fork, s));
-      for (int i = 0; i < nf; ++i) ATTNB_CUDA(cudaStreamWaitEvent(f.s[i], f.fork, 0));
-      for (int b = 0; b < batch; ++b)
-        attend(b, f.s[b % nf], static_cast<char*>(gws) + (b % nf) * attn_ws);
-      for (int i = 0; i < nf; ++i) {
-        ATTNB_CUDA(cudaEventRecord(f.join[i], f.s[i]));
-        ATTNB_CUDA(cudaStreamWaitEvent(s, f.join[i], 0));
-      }
-    } catch (...) {
-      // Nothing queued on a fork may still use the scratch after an error.
-      for (int i = 0; i < nf; ++i) cudaStreamSynchronize(f.s[i]);
-      cudaGetLastError();
-      throw;
-    }
-  }
+  // Sequence b runs on fork b % nf, after the projection; the output
+  // projection waits for every fork.
+  run_forked(c, s, batch, nf, gws, attn_ws, attend);
   // 3) y = ctx . W_out^T + b_out   (:110-127)
   const GemmPlan p_out = gemm_plan(rows, D, D, prec);
   gemm_run(p_out, ctx, D, true, W_out, D, true, y, D, 1.f, 0.f, b_out, gws, c.status, c.num_sms, s);
@@ -735,6 +745,34 @@ int attnb_attn_block_dense_dev(const attnb_tensor* Q, const attnb_tensor* K,
     void* ws = dev_scratch(c, block_scratch_bytes(Q->H, Q->T, K->T, Q->Dh, causal != 0, prec,
                                                   c.num_sms), s);
     block_dev(Q, K, V, O, causal, prec, c, s, ws);
+  });
+}
+
+int attnb_attn_block_dense_batched_dev(const attnb_tensor* Q, const attnb_tensor* K,
+                                       const attnb_tensor* V, attnb_mtensor* O, int batch,
+                                       int64_t q_bs, int64_t k_bs, int64_t v_bs, int64_t o_bs,
+                                       int causal, int precision, void* stream) {
+  return guarded([&] {
+    if (batch < 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "batch must be >= 0");
+    validate_block(Q, K, V, O, causal);
+    if (batch == 0) return;
+    const int prec = resolve_precision(precision);
+    DeviceCtx& c = current_ctx();
+    cudaStream_t s = as_stream(stream);
+    const int nf = std::min(batch, ForkStreams::kForks);
+    const size_t attn_ws =
+        (block_scratch_bytes(Q->H, Q->T, K->T, Q->Dh, causal != 0, prec, c.num_sms) + 255) &
+        ~size_t(255);
+    void* ws = dev_scratch(c, nf * attn_ws, s);
+    run_forked(c, s, batch, nf, ws, attn_ws, [&](int b, cudaStream_t st, void* w) {
+      attnb_tensor q = *Q, k = *K, v = *V;
+      attnb_mtensor o = *O;
+      q.data += b * q_bs;
+      k.data += b * k_bs;
+      v.data += b * v_bs;
+      o.data += b * o_bs;
+      block_dev(&q, &k, &v, &o, causal, prec, c, st, w);
+    });
   });
 }
 

@@ -199,6 +199,16 @@ ATTNB_API int attnb_attn_block_dense(const attnb_tensor* Q, const attnb_tensor* 
 ATTNB_API int attnb_attn_block_dense_dev(const attnb_tensor* Q, const attnb_tensor* K,
                                const attnb_tensor* V, attnb_mtensor* O, int causal,
                                int precision, void* stream);
+/* The same prefill for `batch` independent sequences of equal shape: sequence
+ * b's views are Q, K, V, O with data advanced by b * {q,k,v,o}_bs elements.
+ * The sequences run side by side on internal streams forked from `stream`
+ * and joined back to it.  No reference counterpart: the reference's MHA block
+ * loops over sequences (src/attn_dispatch.cpp:98-107); the sharded MHA block
+ * uses this for its local heads. */
+ATTNB_API int attnb_attn_block_dense_batched_dev(const attnb_tensor* Q, const attnb_tensor* K,
+                                       const attnb_tensor* V, attnb_mtensor* O, int batch,
+                                       int64_t q_bs, int64_t k_bs, int64_t v_bs, int64_t o_bs,
+                                       int causal, int precision, void* stream);
 
 /* Full MHA block, x[T,D] -> y[T,D] with W_in[3D,D], b_in[3D], W_out[D,D],
  * b_out[D] (PyTorch nn.MultiheadAttention packing), H heads.

@@ -32,6 +32,10 @@ class CPUOps:
         vv = v.detach().numpy().astype(np.float32)
         o.copy_(torch.from_numpy(oracle.attn_block(qq, kk, vv, causal)))
 
+    def attention_batched(self, q, k, v, o, causal):
+        for b in range(q.shape[0]):
+            self.attention(q[b], k[b], v[b], o[b], causal)
+
     def sgemm(self, A, B, C):
         C.copy_((A.double() @ B.double()).to(C.dtype))
 
