@@ -188,6 +188,37 @@ def dist_setup(n_gpus: int):
     return rank, world, local
 
 
+def numa_bind(local: int):
+    """Restrict this process to the host cores NVML lists as nearest to GPU
+    `local`, so page-locked buffers (allocated later, first touched by these
+    cores) sit on the GPU's NUMA node and host<->device copies do not cross the
+    socket link.  ATTNB_NUMA_BIND=0 turns it off.  Returns (the affinity to
+    restore or None, a description for the JSON line)."""
+    if os.environ.get("ATTNB_NUMA_BIND", "1") == "0":
+        return None, {"bound": False, "why": "ATTNB_NUMA_BIND=0"}
+    try:
+        import pynvml
+        import torch
+
+        prop = torch.cuda.get_device_properties(local)
+        bus = f"{prop.pci_domain_id:08x}:{prop.pci_bus_id:02x}:{prop.pci_device_id:02x}.0"
+        pynvml.nvmlInit()
+        h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        words = (os.cpu_count() + 63) // 64
+        masks = pynvml.nvmlDeviceGetCpuAffinity(h, words)
+        near = {w * 64 + b for w, m in enumerate(masks) for b in range(64) if (m >> b) & 1}
+        orig = os.sched_getaffinity(0)
+        keep = near & orig
+        if not keep or keep == orig:
+            return None, {"bound": False,
+                          "why": f"all {len(orig)} usable cores are near the GPU" if keep
+                          else "no usable core is near the GPU"}
+        os.sched_setaffinity(0, keep)
+        return orig, {"bound": True, "cores": len(keep), "of": len(orig)}
+    except Exception as e:  # no NVML or no device: leave the affinity alone
+        return None, {"bound": False, "why": type(e).__name__}
+
+
 def barrier(world):
     if world > 1:
         import torch.distributed as dist
@@ -634,7 +665,8 @@ def main():
 
     import torch
 
-    rank, world, _ = dist_setup(args.gpus)
+    rank, world, local = dist_setup(args.gpus)
+    orig_affinity, binding = numa_bind(local)
     peaks = load_peaks()
     prec = args.precision
     head = measure(args.workload, rank, world, args.steps, args.warmup, prec, peaks)
@@ -652,6 +684,8 @@ def main():
         for w in args.sharded.split(","):
             also.append(measure_sharded(w.strip(), world, max(3, min(args.steps, 10)), 3, prec,
                                         peaks))
+    if orig_affinity is not None:
+        os.sched_setaffinity(0, orig_affinity)  # the CPU baseline uses every host core
     cpu = None
     if rank == 0 and world == 1:
         v, unit, cores, kind, sample = cpu_sample(args.workload, args.cpu_seconds)
@@ -669,6 +703,7 @@ def main():
                 "e2e": head.get("e2e"), "roofline": head["roofline"],
                 "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
                 "cpu_baseline": cpu, "also": also}
+        line["host_binding"] = binding
         if head.get("e2e_resident"):
             line["e2e_resident"] = head["e2e_resident"]
         print(json.dumps(line), flush=True)
