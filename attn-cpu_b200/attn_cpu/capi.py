@@ -17,6 +17,7 @@ ERR_INVALID_ARGUMENT = 1
 ERR_RUNTIME = 2
 ERR_CUDA = 3
 ERR_DEVICE_TIMEOUT = 4
+ERR_OUT_OF_MEMORY = 5
 
 PREC = {None: -1, "default": -1, "3xtf32": 0, "tf32": 1}
 
@@ -46,6 +47,10 @@ class AttnbError(RuntimeError):
     def __init__(self, code: int, msg: str):
         super().__init__(f"attnb error {code}: {msg}")
         self.code = code
+
+
+class AttnbOutOfMemory(AttnbError, MemoryError):
+    """ATTNB_ERR_OUT_OF_MEMORY: the device scratch the call needs could not be had."""
 
 
 _lib = None
@@ -98,7 +103,8 @@ def lib() -> ctypes.CDLL:
 
 def check(rc: int) -> None:
     if rc != OK:
-        raise AttnbError(rc, lib().attnb_last_error().decode())
+        cls = AttnbOutOfMemory if rc == ERR_OUT_OF_MEMORY else AttnbError
+        raise cls(rc, lib().attnb_last_error().decode())
 
 
 def _stream(stream=None) -> int:

@@ -6,14 +6,20 @@ parallelism is OpenMP inside one process, src/gemm.cpp:350); the partitions
 here follow the work's natural independence:
 
 * attention (prefill and decode): whole heads per rank -- no exchange inside
-  the attention itself;
+  the attention itself; an all-gather of the per-head outputs assembles O
+  (prefill: attn::attn_block_dense, src/attn_block.cpp:104-241; decode step:
+  attn::attn_step_dense, src/attn_dense.cpp:21-73, with the batch and head
+  axes flattened into one head axis of B*H);
 * the MHA block (attn::mha_block_dense, src/attn_dispatch.cpp:17-133): rank r
   owns heads [h0, h1): it projects only its heads' Q/K/V rows of W_in
-  (column-parallel QKV), runs their attention, then an all-gather of the
-  per-head context rebuilds ctx^T [D, T] on every rank (the attention writes
-  its rows straight into the transposed send buffer), each rank computes a
-  block of y's rows from ctx^T read transposed (y = ctx W_out^T + b_out, the
-  single-GPU product), and a second all-gather of those rows assembles y;
+  (column-parallel QKV) and runs their attention, writing the context
+  transposed, ctx_r^T [hl*Dh, tokens].  Rank s will compute y for a block of
+  tokens, so an all-to-all hands it exactly those columns of every rank's
+  ctx_r^T: stacked in rank order they are ctx^T [D, tokens_s] for its block
+  (1/p of the context per rank, where an all-gather would move all of it).
+  Rank s then computes its rows y = ctx W_out^T + b_out from ctx^T read
+  transposed (the single-GPU product, same summation order), and an
+  all-gather of the row blocks assembles y;
 * SGEMM (gemm::sgemm_blocked, src/gemm.cpp:319-415): rank r computes a block
   of C -- a block of rows (A row block x all of B; the all-gather is then
   contiguous) or, as `shard="cols"`, a block of columns (all of A x a column
@@ -30,6 +36,34 @@ from dataclasses import dataclass
 
 import torch
 import torch.distributed as dist
+
+
+class CommInitError(RuntimeError):
+    """The process group could not be formed: a rank never joined within the
+    time limit, or the rendezvous failed."""
+
+
+def init_distributed(backend: str = "nccl", timeout_s: float = 300.0, device=None, **kwargs):
+    """torch.distributed.init_process_group with a bounded wait.
+
+    Every rank of the job calls this once (RANK / WORLD_SIZE / MASTER_ADDR /
+    MASTER_PORT from the environment unless given in ``kwargs``).  If a rank
+    never arrives, or the rendezvous store cannot be reached, the others raise
+    CommInitError after about ``timeout_s`` seconds instead of waiting for
+    good; the same limit bounds every later collective of the group, so a rank
+    that leaves between steps ends the others' next collective with an error.
+    With ``device`` (a CUDA device) the NCCL communicator is bound to it."""
+    import datetime
+
+    opts = dict(kwargs)
+    opts["timeout"] = datetime.timedelta(seconds=timeout_s)
+    if device is not None:
+        opts["device_id"] = device
+    try:
+        dist.init_process_group(backend, **opts)
+    except (RuntimeError, ValueError, OSError) as e:  # DistStoreError etc. derive from these
+        raise CommInitError(f"process group ({backend}) could not be formed within "
+                            f"{timeout_s:g} s: {e}") from e
 
 
 def shard_range(n: int, rank: int, world: int) -> tuple[int, int]:
@@ -63,6 +97,9 @@ class DeviceOps:
     def sgemm(self, A, B, C):
         self.capi.sgemm_dev(A, B, C, precision=self.precision)
 
+    def decode(self, q, k, v, o):
+        self.capi.attn_step_dense_dev(q, k, v, o)
+
     def gemm_ex(self, A, B, C, trans_a, trans_b, bias):
         self.capi.gemm_ex_dev(A, B, C, trans_a=trans_a, trans_b=trans_b, bias=bias,
                               precision=self.precision)
@@ -92,6 +129,30 @@ def _all_gather_rows(local: torch.Tensor, counts: list[int], group) -> torch.Ten
     out = torch.empty((world * cmax,) + tail, dtype=local.dtype, device=local.device)
     dist.all_gather_into_tensor(out, padded, group=group)
     return torch.cat([out[r * cmax:r * cmax + c] for r, c in enumerate(counts)], 0)
+
+
+def _all_to_all_cols(local: torch.Tensor, row_counts: list[int], group) -> torch.Tensor:
+    """Column exchange: ``local`` [n_me, C] holds this rank's rows (n_r rows on
+    rank r, ``row_counts``) of a matrix whose columns are split into balanced
+    contiguous blocks, block s belonging to rank s.  Returns this rank's
+    column block of the whole matrix, [sum(n_r), C_me]: every rank's rows of
+    that block, stacked in rank order."""
+    rank, world = _world(group)
+    if world == 1:
+        return local
+    n_me, C = local.shape
+    cols = [shard_range(C, s, world) for s in range(world)]
+    widths = [b - a for a, b in cols]
+    if len(set(widths)) == 1:
+        # [n_me, world, w] -> [world, n_me, w]: block s contiguous
+        send = local.view(n_me, world, widths[0]).transpose(0, 1).contiguous().view(-1)
+    else:
+        send = torch.cat([local[:, a:b].reshape(-1) for a, b in cols])
+    w_me = widths[rank]
+    recv = torch.empty(sum(row_counts) * w_me, dtype=local.dtype, device=local.device)
+    dist.all_to_all_single(recv, send, output_split_sizes=[n * w_me for n in row_counts],
+                           input_split_sizes=[n_me * w for w in widths], group=group)
+    return recv.view(sum(row_counts), w_me)
 
 
 @dataclass
@@ -157,14 +218,15 @@ class ShardedMHA:
                     0, 2, 1, 3)
             o = ctxT_local.view(hl, Dh, B, T).permute(2, 0, 3, 1)
             self.ops.attention_batched(heads(0), heads(1), heads(2), o, self.causal)
-        # 3) all-gather: [world][hl_r * Dh, B*T] -> ctx^T [D, B*T]
-        ctxT = _all_gather_rows(ctxT_local, [c * Dh for c in self.head_counts], self.group)
+        # 3) all-to-all: rank s receives columns [r0_s, r1_s) of every rank's
+        #    ctx_r^T, which stacked in rank order are ctx^T [D, r1_s - r0_s]
+        ctxT_mine = _all_to_all_cols(ctxT_local, [c * Dh for c in self.head_counts], self.group)
         # 4) this rank's rows of y = ctx W_out^T + b_out, reading ctx^T
         #    transposed, then an all-gather of the row blocks
         r0, r1 = shard_range(rows, self.rank, self.world)
         y_rows = torch.empty(r1 - r0, D, dtype=x.dtype, device=x.device)
         if r1 > r0:
-            self.ops.gemm_ex(ctxT[:, r0:r1], self.W_out, y_rows, True, True, self.b_out)
+            self.ops.gemm_ex(ctxT_mine, self.W_out, y_rows, True, True, self.b_out)
         counts = [shard_range(rows, r, self.world)[1] - shard_range(rows, r, self.world)[0]
                   for r in range(self.world)]
         y = _all_gather_rows(y_rows, counts, self.group).view(B, T, D)
@@ -209,5 +271,25 @@ def attn_block_sharded(Q, K, V, causal=False, group=None, ops=None) -> torch.Ten
     Ol = torch.empty(h1 - h0, L, Dh, dtype=Q.dtype, device=Q.device)
     if h1 > h0:
         ops.attention(Q[h0:h1], K[h0:h1], V[h0:h1], Ol, causal)
+    counts = [shard_range(H, r, world)[1] - shard_range(H, r, world)[0] for r in range(world)]
+    return _all_gather_rows(Ol, counts, group)
+
+
+def attn_step_sharded(Q, K, V, group=None, ops=None) -> torch.Tensor:
+    """attn_step_dense (one decode step) with heads partitioned across ranks.
+
+    Q [H, Dh] and K / V [H, T, Dh] (batch and heads flattened into H; any
+    strides) are the same views on every rank; rank r reads only its heads
+    [h0, h1) of K and V, computes O [h1 - h0, Dh], and an all-gather returns
+    the full O [H, Dh] on every rank.  The reference's decode step
+    (src/attn_dense.cpp:21-73) treats heads independently, so the partition
+    changes no arithmetic."""
+    ops = ops if ops is not None else DeviceOps()
+    rank, world = _world(group)
+    H, Dh = Q.shape
+    h0, h1 = shard_range(H, rank, world)
+    Ol = torch.empty(h1 - h0, Dh, dtype=Q.dtype, device=Q.device)
+    if h1 > h0:
+        ops.decode(Q[h0:h1], K[h0:h1], V[h0:h1], Ol)
     counts = [shard_range(H, r, world)[1] - shard_range(H, r, world)[0] for r in range(world)]
     return _all_gather_rows(Ol, counts, group)

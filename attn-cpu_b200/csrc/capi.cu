@@ -23,8 +23,12 @@ using namespace attnb;
 
 namespace {
 
+// Runs an entry point's body inside an NVTX range named after the entry point
+// (visible in Nsight timelines; free when no tool is attached) and turns its
+// exceptions into a status code plus the thread's last-error message.
 template <class F>
-int guarded(F&& f) {
+int guarded(const char* name, F&& f) {
+  NvtxRange range(name);
   try {
     f();
     return ATTNB_OK;
@@ -388,7 +392,7 @@ const char* attnb_version(void) { return "attnb 0.1 sm_100a"; }
 int attnb_profile_enable(int on) { return profile_enable(on); }
 
 int attnb_selftest_wait_timeout(int limit_us, void* stream) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     if (limit_us <= 0 || limit_us > 10000000)
       fail(ATTNB_ERR_INVALID_ARGUMENT, "limit_us must be in (0, 1e7]");
     selftest_wait_timeout(current_ctx(), limit_us, as_stream(stream));
@@ -400,7 +404,7 @@ int attnb_profile_read(const char* kernel, double* total_ms, int* launches) {
 }
 
 int attnb_host_alloc(size_t bytes, void** ptr) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     if (!ptr) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
     *ptr = nullptr;
     if (bytes == 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "bytes must be positive");
@@ -409,14 +413,14 @@ int attnb_host_alloc(size_t bytes, void** ptr) {
 }
 
 int attnb_host_free(void* ptr) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     if (!host_pool_free(ptr))
       fail(ATTNB_ERR_INVALID_ARGUMENT, "pointer was not allocated by attnb_host_alloc");
   });
 }
 
 int attnb_stream_status(void* stream) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     DeviceCtx& c = current_ctx();
     if (consume_status(c, as_stream(stream)) != ATTNB_OK)
       fail(ATTNB_ERR_DEVICE_TIMEOUT, "a bounded device wait expired");
@@ -426,7 +430,7 @@ int attnb_stream_status(void* stream) {
 // ------------------------------------------------------------------- SGEMM
 int attnb_sgemm_dev(const float* A, int lda, const float* B, int ldb, float* C, int ldc, int M,
                     int N, int K, float alpha, float beta, int precision, void* stream) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     if (M <= 0 || N <= 0 || K <= 0) return;
     if (!A || !B || !C) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
     if (lda < K || ldb < N || ldc < N)
@@ -445,9 +449,19 @@ int attnb_sgemm_dev(const float* A, int lda, const float* B, int ldb, float* C, 
 int attnb_gemm_ex_dev(int trans_a, int trans_b, const float* A, int lda, const float* B, int ldb,
                       const float* bias, float* C, int ldc, int M, int N, int K, float alpha,
                       float beta, int precision, void* stream) {
-  return guarded([&] {
-    if (M <= 0 || N <= 0 || K <= 0) return;
-    if (!A || !B || !C) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+  return guarded(__func__, [&] {
+    if (K < 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "K must be non-negative");
+    if (M <= 0 || N <= 0) return;
+    if (!C) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    if (K == 0) {
+      // An empty product: C = beta * C + bias.
+      if (ldc < N) fail(ATTNB_ERR_INVALID_ARGUMENT, "leading dimension smaller than the row length");
+      DeviceCtx& c = current_ctx();
+      gemm_scale_bias(C, ldc, M, N, beta, bias, c.num_sms, as_stream(stream));
+      ATTNB_CUDA(cudaGetLastError());
+      return;
+    }
+    if (!A || !B) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
     if ((trans_a != 0 && trans_a != 1) || (trans_b != 0 && trans_b != 1))
       fail(ATTNB_ERR_INVALID_ARGUMENT, "trans_a and trans_b must be 0 or 1");
     if (lda < (trans_a ? M : K) || ldb < (trans_b ? K : N) || ldc < N)
@@ -465,7 +479,7 @@ int attnb_gemm_ex_dev(int trans_a, int trans_b, const float* A, int lda, const f
 
 int attnb_linear_dev(const float* x, int ldx, const float* W, int ldw, const float* b, float* y,
                      int ldy, int T, int N, int K, int precision, void* stream) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     if (T <= 0 || N <= 0 || K <= 0) return;
     if (!x || !W || !y) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
     if (ldx < K || ldw < K || ldy < N)
@@ -482,7 +496,7 @@ int attnb_linear_dev(const float* x, int ldx, const float* W, int ldw, const flo
 
 static int sgemm_host(const float* A, int M, int K, const float* B, int N, float* C, float alpha,
                       float beta, int precision) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     if (M <= 0 || N <= 0 || K <= 0) return;
     if (!A || !B || !C) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
     const int prec = resolve_precision(precision);
@@ -525,7 +539,7 @@ int attnb_gemm_jit(const float* A, int M, int K, const float* B, int N, float* C
 // --------------------------------------------------------------- decode step
 int attnb_attn_step_dense_dev(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
                               attnb_mtensor* O, void* stream) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     validate_step(Q, K, V, O);
     DeviceCtx& c = current_ctx();
     step_dev(Q, K, V, O, c, as_stream(stream), nullptr, 0);
@@ -534,7 +548,7 @@ int attnb_attn_step_dense_dev(const attnb_tensor* Q, const attnb_tensor* K, cons
 
 int attnb_attn_step_dense(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
                           attnb_mtensor* O) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     validate_step(Q, K, V, O);
     with_host_ctx([&](DeviceCtx& c) {
       cudaStream_t s = c.stream;
@@ -624,7 +638,7 @@ void cache_views(const attnb_kv_cache* kc, attnb_tensor& K, attnb_tensor& V) {
 extern "C" {
 
 int attnb_kv_cache_create(int H, int Dh, int capacity, attnb_kv_cache** cache) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     if (!cache) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
     *cache = nullptr;
     if (H <= 0 || Dh <= 0 || capacity <= 0)
@@ -638,18 +652,23 @@ int attnb_kv_cache_create(int H, int Dh, int capacity, attnb_kv_cache** cache) {
     kc->length = 0;
     kc->k = kc->v = nullptr;
     const size_t bytes = (size_t)H * capacity * Dh * sizeof(float);
-    ATTNB_CUDA(cudaMalloc(&kc->k, bytes));
-    const cudaError_t e = cudaMalloc(&kc->v, bytes);
-    if (e != cudaSuccess) {
-      cudaFree(kc->k);
+    auto check_alloc = [&](cudaError_t e) {
+      if (e == cudaSuccess) return;
+      cudaGetLastError();
+      if (kc->k) cudaFree(kc->k);
+      if (e == cudaErrorMemoryAllocation)
+        fail(ATTNB_ERR_OUT_OF_MEMORY, "cudaMalloc of the KV cache (2 x " + std::to_string(bytes) +
+                                          " bytes) failed: out of memory");
       ATTNB_CUDA(e);
-    }
+    };
+    check_alloc(cudaMalloc(&kc->k, bytes));
+    check_alloc(cudaMalloc(&kc->v, bytes));
     *cache = kc.release();
   });
 }
 
 int attnb_kv_cache_destroy(attnb_kv_cache* cache) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     if (!cache) return;
     int prev = -1;
     ATTNB_CUDA(cudaGetDevice(&prev));
@@ -664,14 +683,14 @@ int attnb_kv_cache_destroy(attnb_kv_cache* cache) {
 }
 
 int attnb_kv_cache_length(const attnb_kv_cache* cache, int* length) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     if (!cache || !length) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
     *length = cache->length;
   });
 }
 
 int attnb_kv_cache_truncate(attnb_kv_cache* cache, int length) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     if (!cache) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null KV cache");
     if (length < 0 || length > cache->length)
       fail(ATTNB_ERR_INVALID_ARGUMENT, "length must be in [0, current length]");
@@ -681,12 +700,12 @@ int attnb_kv_cache_truncate(attnb_kv_cache* cache, int length) {
 
 int attnb_kv_cache_append(attnb_kv_cache* cache, const float* k, const float* v, int n,
                           void* stream) {
-  return guarded([&] { cache_append(checked_cache(cache), k, v, n, as_stream(stream)); });
+  return guarded(__func__, [&] { cache_append(checked_cache(cache), k, v, n, as_stream(stream)); });
 }
 
 int attnb_kv_cache_step_dev(attnb_kv_cache* cache, const float* q, const float* k_new,
                             const float* v_new, float* o, void* stream) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     attnb_kv_cache* kc = checked_cache(cache);
     if (!q || !o) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
     if ((k_new == nullptr) != (v_new == nullptr))
@@ -703,7 +722,7 @@ int attnb_kv_cache_step_dev(attnb_kv_cache* cache, const float* q, const float* 
 
 int attnb_kv_cache_step(attnb_kv_cache* cache, const float* q, const float* k_new,
                         const float* v_new, float* o) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     attnb_kv_cache* kc = checked_cache(cache);
     if (!q || !o) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
     if ((k_new == nullptr) != (v_new == nullptr))
@@ -737,7 +756,7 @@ int attnb_kv_cache_step(attnb_kv_cache* cache, const float* q, const float* k_ne
 int attnb_attn_block_dense_dev(const attnb_tensor* Q, const attnb_tensor* K,
                                const attnb_tensor* V, attnb_mtensor* O, int causal, int precision,
                                void* stream) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     validate_block(Q, K, V, O, causal);
     const int prec = resolve_precision(precision);
     DeviceCtx& c = current_ctx();
@@ -752,7 +771,7 @@ int attnb_attn_block_dense_batched_dev(const attnb_tensor* Q, const attnb_tensor
                                        const attnb_tensor* V, attnb_mtensor* O, int batch,
                                        int64_t q_bs, int64_t k_bs, int64_t v_bs, int64_t o_bs,
                                        int causal, int precision, void* stream) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     if (batch < 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "batch must be >= 0");
     validate_block(Q, K, V, O, causal);
     if (batch == 0) return;
@@ -778,7 +797,7 @@ int attnb_attn_block_dense_batched_dev(const attnb_tensor* Q, const attnb_tensor
 
 int attnb_attn_block_dense(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
                            attnb_mtensor* O, int causal, int precision) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     validate_block(Q, K, V, O, causal);
     const int prec = resolve_precision(precision);
     if (Q->T == 0) return;
@@ -823,7 +842,7 @@ int attnb_attn_block_dense(const attnb_tensor* Q, const attnb_tensor* K, const a
 int attnb_mha_block_dense_dev(const float* x, int batch, int T, int D, const float* W_in,
                               const float* b_in, const float* W_out, const float* b_out, int H,
                               int causal, float* y, int precision, void* stream) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     validate_mha(x, T, D, W_in, b_in, W_out, b_out, H, y);
     if (batch < 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "batch must be non-negative");
     const int prec = resolve_precision(precision);
@@ -836,7 +855,7 @@ int attnb_mha_block_dense_dev(const float* x, int batch, int T, int D, const flo
 int attnb_mha_block_dense(const float* x, int T, int D, const float* W_in, const float* b_in,
                           const float* W_out, const float* b_out, int H, int causal, float* y,
                           int precision) {
-  return guarded([&] {
+  return guarded(__func__, [&] {
     validate_mha(x, T, D, W_in, b_in, W_out, b_out, H, y);
     const int prec = resolve_precision(precision);
     if (T == 0) return;

@@ -335,7 +335,10 @@ void decode_launch(const DecodePlan& p, const View3& Q, const View3& K, const Vi
 //     caller;
 //   * the first call on a device looks the array's device address up
 //     (cudaGetSymbolAddress) and caches it, so make that first call before
-//     any stream capture.
+//     any stream capture.  The cache is keyed by the device's current CUDA
+//     context: after the caller destroys and recreates that context (for
+//     example cudaDeviceReset), the next call looks the address up again and
+//     should likewise come before any capture.
 // ===================================================================
 #include <mutex>
 
@@ -352,6 +355,33 @@ static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchB
 std::mutex g_noalloc_mu;
 void* g_noalloc_addr[kNoAllocMaxDevices];
 int g_noalloc_sms[kNoAllocMaxDevices];
+unsigned long long g_noalloc_ctx[kNoAllocMaxDevices];  // context the address belongs to
+
+// Unique id of the calling thread's current CUDA context (driver entry points
+// looked up through the runtime, as for the tensor-map encoder), or 0 when it
+// cannot be read; a context created after a reset gets a new id.
+unsigned long long current_context_id() {
+  using GetCurrentFn = CUresult (*)(CUcontext*);
+  using GetIdFn = CUresult (*)(CUcontext, unsigned long long*);
+  static const std::pair<GetCurrentFn, GetIdFn> fns = [] {
+    void* a = nullptr;
+    void* b = nullptr;
+    cudaDriverEntryPointQueryResult qa, qb;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetCurrent", &a, 12000, cudaEnableDefault, &qa) !=
+            cudaSuccess || qa != cudaDriverEntryPointSuccess)
+      a = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuCtxGetId", &b, 12000, cudaEnableDefault, &qb) !=
+            cudaSuccess || qb != cudaDriverEntryPointSuccess)
+      b = nullptr;
+    cudaGetLastError();
+    return std::make_pair(reinterpret_cast<GetCurrentFn>(a), reinterpret_cast<GetIdFn>(b));
+  }();
+  if (!fns.first || !fns.second) return 0;
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (fns.first(&ctx) != CUDA_SUCCESS || !ctx || fns.second(ctx, &id) != CUDA_SUCCESS) return 0;
+  return id;
+}
 
 // The reference's validate_dense_shapes (include/attn.h:54-83), same messages.
 void noalloc_validate(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
@@ -373,19 +403,23 @@ void noalloc_validate(const attnb_tensor* Q, const attnb_tensor* K, const attnb_
     fail(ATTNB_ERR_INVALID_ARGUMENT, "Zero stride encountered");
 }
 
-// Device address of the fixed scratch and the SM count, looked up once per
-// device with that device current.
+// Device address of the fixed scratch and the SM count, looked up with the
+// device current on its first call, and again whenever the device's current
+// context is no longer the one the address was looked up in.
 void* noalloc_scratch(int dev, int* num_sms) {
   if (dev < 0 || dev >= kNoAllocMaxDevices)
     fail(ATTNB_ERR_RUNTIME, "device index out of range for the fixed decode scratch");
   std::lock_guard<std::mutex> g(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
+  // Make sure the runtime has made the device's context current before its id
+  // is read (the first runtime call of a thread creates it lazily).
+  ATTNB_CUDA(cudaDeviceGetAttribute(num_sms, cudaDevAttrMultiProcessorCount, dev));
+  const unsigned long long ctx = current_context_id();
+  if (!g_noalloc_addr[dev] || ctx == 0 || ctx != g_noalloc_ctx[dev]) {
     void* p = nullptr;
     ATTNB_CUDA(cudaGetSymbolAddress(&p, g_decode_scratch));
-    int sms = 0;
-    ATTNB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    g_noalloc_sms[dev] = sms;
+    g_noalloc_sms[dev] = *num_sms;
     g_noalloc_addr[dev] = p;
+    g_noalloc_ctx[dev] = ctx;
   }
   *num_sms = g_noalloc_sms[dev];
   return g_noalloc_addr[dev];
@@ -399,6 +433,7 @@ extern "C" ATTNB_API int attnb_attn_step_dense_noalloc(const attnb_tensor* Q,
                                                        const attnb_tensor* V, attnb_mtensor* O,
                                                        void* stream) {
   using namespace attnb;
+  NvtxRange range(__func__);
   try {
     noalloc_validate(Q, K, V, O);
     int dev = -1;

@@ -629,14 +629,17 @@ void launch_fused(const CUtensorMap& ta, const CUtensorMap& tb, int M, int N, in
                         bias, status));
 }
 
-// C = beta * C (alpha == 0 path of the reference, src/gemm.cpp:328-336).
-__global__ void scale_c_kernel(float* C, int64_t ldc, int M, int N, float beta) {
+// C = beta * C (+ bias[n]): the alpha == 0 path of the reference
+// (src/gemm.cpp:328-336) and an empty inner dimension.  beta == 0 never reads C.
+__global__ void scale_c_kernel(float* C, int64_t ldc, int M, int N, float beta,
+                               const float* __restrict__ bias) {
   const int64_t n = (int64_t)M * N;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
        i += (int64_t)gridDim.x * blockDim.x) {
     const int64_t r = i / N, c = i % N;
     float* p = C + r * ldc + c;
-    *p = (beta == 0.f) ? 0.f : *p * beta;
+    const float b = bias ? bias[c] : 0.f;
+    *p = (beta == 0.f) ? b : fmaf(*p, beta, b);
   }
 }
 
@@ -705,11 +708,7 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
               const float* bias, void* ws, int* status, int num_sms, cudaStream_t s) {
   if (p.M <= 0 || p.N <= 0 || p.K <= 0) return;
   if (alpha == 0.f && bias == nullptr) {
-    if (beta != 1.f) {
-      const int64_t n = (int64_t)p.M * p.N;
-      const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms * 8);
-      scale_c_kernel<<<blocks, 256, 0, s>>>(C, ldc, p.M, p.N, beta);
-    }
+    if (beta != 1.f) gemm_scale_bias(C, ldc, p.M, p.N, beta, nullptr, num_sms, s);
     return;
   }
   // 1xTF32, one 128x64 tile per CTA, aligned rows: the raw operands go
@@ -771,6 +770,14 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
       launch_gemm<64, false>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias, status,
                              num_sms, s);
   }
+}
+
+void gemm_scale_bias(float* C, int64_t ldc, int M, int N, float beta, const float* bias,
+                     int num_sms, cudaStream_t s) {
+  if (M <= 0 || N <= 0) return;
+  const int64_t n = (int64_t)M * N;
+  const int blocks = (int)std::min<int64_t>((n + 255) / 256, (int64_t)num_sms * 8);
+  scale_c_kernel<<<blocks, 256, 0, s>>>(C, ldc, M, N, beta, bias);
 }
 
 size_t gemm_workspace_bound(int M, int N, int K, int precision) {

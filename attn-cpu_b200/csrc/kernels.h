@@ -153,6 +153,9 @@ struct GemmPlan {
   size_t off_a_hi, off_a_lo, off_b_hi, off_b_lo, ws_bytes;
 };
 GemmPlan gemm_plan(int M, int N, int K, int precision);
+// C[M,N] = beta * C + bias[n] (bias may be null; beta == 0 never reads C).
+void gemm_scale_bias(float* C, int64_t ldc, int M, int N, float beta, const float* bias,
+                     int num_sms, cudaStream_t s);
 // Scratch bytes of a plan of this size.
 size_t gemm_workspace_bound(int M, int N, int K, int precision);
 void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, const float* B,

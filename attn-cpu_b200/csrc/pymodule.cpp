@@ -11,6 +11,7 @@
 #include <pybind11/pybind11.h>
 
 #include <cmath>
+#include <new>
 #include <stdexcept>
 #include <string>
 #include <vector>
@@ -26,6 +27,7 @@ void rethrow(int rc) {
   if (rc == ATTNB_OK) return;
   const std::string msg = attnb_last_error();
   if (rc == ATTNB_ERR_INVALID_ARGUMENT) throw std::invalid_argument(msg);
+  if (rc == ATTNB_ERR_OUT_OF_MEMORY) throw std::bad_alloc();
   throw std::runtime_error(msg);
 }
 

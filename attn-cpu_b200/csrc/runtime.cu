@@ -3,6 +3,9 @@
 
 #include "common.cuh"
 
+#include <nvtx3/nvToolsExt.h>
+
+#include <algorithm>
 #include <cstdlib>
 #include <cstring>
 #include <atomic>
@@ -22,6 +25,9 @@ void check_cuda(cudaError_t e, const char* what, const char* file, int line) {
                            ":" + std::to_string(line) + ")");
 }
 
+NvtxRange::NvtxRange(const char* name) { nvtxRangePushA(name); }
+NvtxRange::~NvtxRange() { nvtxRangePop(); }
+
 int set_last_error(int code, const std::string& msg) {
   t_last_error = msg;
   return code;
@@ -29,17 +35,47 @@ int set_last_error(int code, const std::string& msg) {
 
 const char* last_error_cstr() { return t_last_error.c_str(); }
 
+// ATTNB_DEVICE_ARENA_CAP_MB: most bytes all arenas of the process may hold
+// (0 = no cap).  Read once.
+static size_t arena_cap() {
+  static const size_t cap = [] {
+    const char* e = std::getenv("ATTNB_DEVICE_ARENA_CAP_MB");
+    const long mb = e ? std::atol(e) : 0;
+    return (size_t)(mb > 0 ? mb : 0) << 20;
+  }();
+  return cap;
+}
+static std::atomic<size_t> g_arena_bytes{0};  // bytes held by all arenas
+
 void* DeviceBuffer::ensure(size_t need, cudaStream_t stream) {
   if (need <= bytes && ptr) return ptr;
   size_t grow = need + need / 4 + 4096;
+  const size_t cap = arena_cap();
+  if (cap) {
+    const size_t others = g_arena_bytes.load() - bytes;
+    if (others + need > cap)
+      fail(ATTNB_ERR_OUT_OF_MEMORY,
+           "device scratch of " + std::to_string(need) + " bytes exceeds the arena cap of " +
+               std::to_string(cap >> 20) + " MiB (ATTNB_DEVICE_ARENA_CAP_MB)");
+    grow = std::min(grow, cap - others);
+  }
   if (ptr) {
     ATTNB_CUDA(cudaStreamSynchronize(stream));
     ATTNB_CUDA(cudaFree(ptr));
+    g_arena_bytes -= bytes;
     ptr = nullptr;
     bytes = 0;
   }
-  ATTNB_CUDA(cudaMalloc(&ptr, grow));
+  const cudaError_t e = cudaMalloc(&ptr, grow);
+  if (e == cudaErrorMemoryAllocation) {
+    cudaGetLastError();
+    ptr = nullptr;
+    fail(ATTNB_ERR_OUT_OF_MEMORY, "cudaMalloc of " + std::to_string(grow) +
+                                      " bytes of device scratch failed: out of memory");
+  }
+  ATTNB_CUDA(e);
   bytes = grow;
+  g_arena_bytes += bytes;
   return ptr;
 }
 

@@ -22,6 +22,16 @@ struct Error {
 void check_cuda(cudaError_t e, const char* what, const char* file, int line);
 #define ATTNB_CUDA(call) ::attnb::check_cuda((call), #call, __FILE__, __LINE__)
 
+// An NVTX range around a host entry point: pushed on construction, popped on
+// destruction (a no-op unless a profiling tool is attached).
+class NvtxRange {
+ public:
+  explicit NvtxRange(const char* name);
+  ~NvtxRange();
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+
 // Records `msg` as the calling thread's last error and returns `code`.
 int set_last_error(int code, const std::string& msg);
 

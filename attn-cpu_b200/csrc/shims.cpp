@@ -2,6 +2,7 @@
 // gemm.h) as thin wrappers over the C ABI.  Status codes become the
 // reference's exception types: std::invalid_argument for shape / null /
 // stride problems, std::runtime_error for everything else.
+#include <new>
 #include <stdexcept>
 #include <string>
 
@@ -15,6 +16,7 @@ void rethrow(int rc) {
   if (rc == ATTNB_OK) return;
   const std::string msg = attnb_last_error();
   if (rc == ATTNB_ERR_INVALID_ARGUMENT) throw std::invalid_argument(msg);
+  if (rc == ATTNB_ERR_OUT_OF_MEMORY) throw std::bad_alloc();
   throw std::runtime_error(msg);
 }
 attnb_tensor to_c(const attn::TensorF32& t) {

@@ -176,13 +176,10 @@ def dist_setup(n_gpus: int):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     if world > 1:
-        import datetime
-
-        import torch.distributed as dist
+        from attn_cpu import parallel
 
         torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
-                                device_id=torch.device("cuda", local))
+        parallel.init_distributed("nccl", timeout_s=300.0, device=torch.device("cuda", local))
     else:
         torch.cuda.set_device(0)
     return rank, world, local
@@ -282,8 +279,9 @@ def time_device(run, steps: int, warmup: int, world: int, flush: bool):
 # --------------------------------------------------------- workloads (ours)
 def setup_sharded(w: str, precision):
     """One problem partitioned over all ranks (attn_cpu.parallel) with its
-    NCCL all-gathers: heads for prefill / the attention block, row blocks of
-    C for SGEMM.  Inputs are identical on every rank (same seed)."""
+    NCCL collectives: heads for prefill / decode / the attention block (the
+    block: all-to-all of the context, all-gather of y), row blocks of C for
+    SGEMM.  Inputs are identical on every rank (same seed)."""
     import torch
 
     from attn_cpu import parallel
@@ -295,6 +293,11 @@ def setup_sharded(w: str, precision):
         Q, K, V = (torch.randn(c["H"], c["L"], c["Dh"], device="cuda", generator=g)
                    for _ in range(3))
         return lambda: parallel.attn_block_sharded(Q, K, V, False, ops=ops)
+    if w == "decode":
+        Q = torch.randn(c["H"], c["Dh"], device="cuda", generator=g)
+        K = torch.randn(c["H"], c["T"], c["Dh"], device="cuda", generator=g)
+        V = torch.randn(c["H"], c["T"], c["Dh"], device="cuda", generator=g)
+        return lambda: parallel.attn_step_sharded(Q, K, V, ops=ops)
     if w.startswith("sgemm"):
         A = torch.rand(c["M"], c["K"], device="cuda", generator=g) * 2 - 1
         B = torch.rand(c["K"], c["N"], device="cuda", generator=g) * 2 - 1
@@ -310,8 +313,9 @@ def setup_sharded(w: str, precision):
     raise KeyError(f"{w} has no sharded form")
 
 
-def setup_workload(w: str, rank: int, precision):
-    """Device inputs (seeded per rank) and (run, e2e_run, h2d, d2h, launches)."""
+def setup_workload(w: str, rank: int, precision, host: bool = True):
+    """Device inputs (seeded per rank) and (run, e2e_run, h2d, d2h, launches);
+    with host=False no page-locked host copies are made and e2e_run is None."""
     import numpy as np
     import torch
 
@@ -327,9 +331,11 @@ def setup_workload(w: str, rank: int, precision):
         V = torch.randn(H, T, Dh, device="cuda", generator=g)
         O = torch.empty(H, L, Dh, device="cuda")
         run = lambda: capi.attn_block_dense_dev(Q, K, V, O, False, precision)
-        hQ, hK, hV = (t.cpu().pin_memory() for t in (Q, K, V))
-        nQ, nK, nV = hQ.numpy(), hK.numpy(), hV.numpy()
-        e2e = lambda: attn_cpu.attn_block_dense(nQ, nK, nV, precision=precision)
+        e2e = None
+        if host:
+            hQ, hK, hV = (t.cpu().pin_memory() for t in (Q, K, V))
+            nQ, nK, nV = hQ.numpy(), hK.numpy(), hV.numpy()
+            e2e = lambda: attn_cpu.attn_block_dense(nQ, nK, nV, precision=precision)
         h2d = 4 * (Q.numel() + K.numel() + V.numel())
         d2h = 4 * O.numel()
         # [1,8,512,64]: one launch (each CTA holds one key tile and loads and
@@ -342,9 +348,11 @@ def setup_workload(w: str, rank: int, precision):
         V = torch.randn(H, T, Dh, device="cuda", generator=g)
         O = torch.empty(H, Dh, device="cuda")
         run = lambda: capi.attn_step_dense_dev(Q, K, V, O)
-        hQ, hK, hV = (t.cpu().pin_memory() for t in (Q, K, V))
-        nQ, nK, nV = hQ.numpy(), hK.numpy(), hV.numpy()
-        e2e = lambda: attn_cpu.attn_step_dense(nQ, nK, nV)
+        e2e = None
+        if host:
+            hQ, hK, hV = (t.cpu().pin_memory() for t in (Q, K, V))
+            nQ, nK, nV = hQ.numpy(), hK.numpy(), hV.numpy()
+            e2e = lambda: attn_cpu.attn_step_dense(nQ, nK, nV)
         return run, e2e, 4 * (Q.numel() + K.numel() + V.numel()), 4 * O.numel(), 2  # + merge
     if w.startswith("sgemm"):
         M, N, K = c["M"], c["N"], c["K"]
@@ -352,9 +360,11 @@ def setup_workload(w: str, rank: int, precision):
         B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
         C = torch.empty(M, N, device="cuda")
         run = lambda: capi.sgemm_dev(A, B, C, precision=precision)
-        hA, hB = A.cpu().pin_memory(), B.cpu().pin_memory()
-        nA, nB = hA.numpy(), hB.numpy()
-        e2e = lambda: attn_cpu.gemm(nA, nB, precision=precision)
+        e2e = None
+        if host:
+            hA, hB = A.cpu().pin_memory(), B.cpu().pin_memory()
+            nA, nB = hA.numpy(), hB.numpy()
+            e2e = lambda: attn_cpu.gemm(nA, nB, precision=precision)
         # 1xTF32 at 1024^3: one launch (every CTA holds one tile and splits the
         # raw operands itself); otherwise pack + GEMM.
         one = w == "sgemm" and precision == "tf32"
@@ -368,11 +378,13 @@ def setup_workload(w: str, rank: int, precision):
         bo = torch.zeros(D, device="cuda")
         y = torch.empty_like(x)
         run = lambda: capi.mha_block_dense_dev(x, Wi, bi, Wo, bo, H, y, False, precision)
-        hx = x.cpu().pin_memory()
-        hw = [t.cpu().pin_memory().numpy() for t in (Wi, bi, Wo, bo)]
-        nx = hx.numpy()
-        e2e = lambda: [attn_cpu.mha_block_dense(nx[b], *hw, H, precision=precision)
-                       for b in range(Bt)]
+        e2e = None
+        if host:
+            hx = x.cpu().pin_memory()
+            hw = [t.cpu().pin_memory().numpy() for t in (Wi, bi, Wo, bo)]
+            nx = hx.numpy()
+            e2e = lambda: [attn_cpu.mha_block_dense(nx[b], *hw, H, precision=precision)
+                           for b in range(Bt)]
         # per sequence (e2e calls the host API once per sequence): x_b and all weights
         h2d = 4 * (x.numel() + Bt * (Wi.numel() + bi.numel() + Wo.numel() + bo.numel()))
         return run, e2e, h2d, 4 * y.numel(), 4 + 2 * Bt  # 2 x (pack + GEMM), B x (pack + attn)
@@ -445,27 +457,69 @@ def kernel_time(run, w: str, steps: int, world: int, flush: bool):
     return max_over_ranks(ms / steps, world), n // max(1, steps)
 
 
-def measure_sharded(w: str, world: int, steps: int, warmup: int, precision, peaks):
-    """Strong scaling: one problem over all ranks, collectives inside the step."""
-    run = setup_sharded(w, precision)
-    times = time_device(run, steps, warmup, world, flush=w in ("prefill", "sgemm"))
+def measure_sharded(w: str, rank: int, world: int, steps: int, warmup: int, precision):
+    """Strong scaling: one problem over all ranks, collectives inside the step,
+    beside the same problem on one GPU through the single-GPU entry point
+    (rank 0 alone, the other ranks waiting at a barrier).  Compact entry."""
+    import torch
+
     from attn_cpu import capi
 
+    flush = w in ("prefill", "sgemm")
+    run = setup_sharded(w, precision)
+    times = time_device(run, steps, warmup, world, flush=flush)
     capi.stream_status()
     ms = max_over_ranks(sum(times), world) / steps
-    work = flops_of(w)
-    return {"metric": WORKLOADS[w]["metric"] + " (one problem sharded over all GPUs)",
-            "value": round(work / (ms * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-            "ms_per_step": round(ms, 5), "scaling": "strong", "config": WORKLOADS[w]["desc"],
-            "parallelism": ("heads" if w in ("prefill", "block") else "C row blocks") +
-                           f" x{world} + NCCL all-gather"}
+    del run
+    torch.cuda.empty_cache()
+    ms1 = None
+    if rank == 0:
+        run1 = setup_workload(w, 0, precision, host=False)[0]
+        ms1 = sum(time_device(run1, steps, warmup, 1, flush)) / steps
+        del run1
+        torch.cuda.empty_cache()
+    barrier(world)
+    work = flops_of(w) if w != "decode" else bytes_of(w)
+    scale = 1e12 if WORKLOADS[w]["unit"] == "TFLOP/s" else 1e9
+    value = work / (ms * 1e-3) / scale
+    r = {"w": w, "prec": precision if w != "decode" else "fp32", "scaling": "strong",
+         "v": round(value, 2), "u": WORKLOADS[w]["unit"], "ms": round(ms, 4),
+         "par": {"prefill": "heads", "decode": "heads", "block": "heads+a2a",
+                 "sgemm": "C rows", "sgemm-large": "C rows"}[w] + f" x{world}"}
+    if ms1 is not None:
+        v1 = work / (ms1 * 1e-3) / scale
+        r.update(n1=round(v1, 2), eff=round(value / (world * v1), 3))
+    return r
+
+
+def compact(w: str, res: dict, precision) -> dict:
+    """Short form of a secondary measurement for the `also` list: value and
+    unit, ms per step, the dominant kernel's CUDA-event time per step and its
+    roofline fraction (of the TF32 rate, or of HBM for decode; the dominant
+    kernel of each workload is named in dominant_of), e2e and the SM clock."""
+    rf = res["roofline"]
+    out = {"w": w, "prec": precision if w != "decode" else "fp32", "v": res["value"],
+           "u": res["unit"], "ms": round(res["ms_per_step"], 4),
+           "k_ms": round(rf["kernel_ms_per_step"], 4), "frac": rf["frac"]}
+    if "frac_of_3xtf32_cap" in rf:
+        out["frac3x"] = rf["frac_of_3xtf32_cap"]
+    if res.get("e2e"):
+        out["e2e"] = res["e2e"]["value"]
+    if res.get("e2e_resident"):
+        out["e2e_res"] = res["e2e_resident"]["value"]
+    clk = res.get("clocks") or {}
+    if clk:
+        out["mhz"] = clk.get("sm_mhz")
+        if clk.get("reasons"):
+            out["why"] = clk["reasons"]
+    return out
 
 
 def measure(w: str, rank: int, world: int, steps: int, warmup: int, precision, peaks,
             with_e2e=True):
     import torch
 
-    run, e2e, h2d, d2h, launches = setup_workload(w, rank, precision)
+    run, e2e, h2d, d2h, launches = setup_workload(w, rank, precision, host=with_e2e)
     flush = w in ("prefill", "sgemm")  # the other workloads' inputs exceed L2
     with ClockSampler(int(os.environ.get("LOCAL_RANK", "0"))) as clk:
         t0 = time.perf_counter()
@@ -632,12 +686,20 @@ def run_reference_arm(args):
     line = {"impl": "reference", "metric": WORKLOADS[w]["metric"], "value": round(value, 5),
             "unit": unit, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": WORKLOADS[w]["desc"]},
+            "data": "synthetic", "config": config_of(w, world),
             "cpu_baseline": {"value": round(value, 5), "unit": unit, "cores": cores,
                              "kind": kind, "sample": sample},
             "e2e": {"value": round(value, 5), "unit": unit, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
+
+
+def config_of(w: str, world: int) -> dict:
+    """The `config` of a line: the same dict in both arms."""
+    return {"workload": WORKLOADS[w]["desc"],
+            "l2": "flushed between steps" if w in ("prefill", "sgemm") else
+                  "inputs larger than L2",
+            "parallelism": f"batch-x-heads x{world}", "global_batch": world}
 
 
 # --------------------------------------------------------------------- main
@@ -652,9 +714,10 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0,
                     help="CPU time budget of the reference measurement")
     ap.add_argument("--no-also", action="store_true", help="skip the secondary configs")
-    ap.add_argument("--sharded", default="",
-                    help="with N>1: also time these workloads (comma list of prefill, sgemm, "
-                         "sgemm-large, block) as one problem partitioned over all GPUs")
+    ap.add_argument("--sharded", default="block,sgemm-large,decode",
+                    help="with N>1: also time these workloads (comma list of prefill, decode, "
+                         "sgemm, sgemm-large, block) as one problem partitioned over all GPUs, "
+                         "in both precisions; empty to skip")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
@@ -672,18 +735,21 @@ def main():
     head = measure(args.workload, rank, world, args.steps, args.warmup, prec, peaks)
     also = []
     if world == 1 and not args.no_also:
-        for w in ("decode", "sgemm", "sgemm-large", "prefill-large", "block"):
-            if w == args.workload:
-                continue
+        # The other configs in this run's precision, then the tensor-core
+        # configs at scale in the other precision.
+        other = "tf32" if prec == "3xtf32" else "3xtf32"
+        plan = [(w, prec) for w in ("decode", "sgemm", "sgemm-large", "prefill-large", "block")
+                if w != args.workload]
+        plan += [(w, other) for w in ("sgemm-large", "prefill-large", "block")]
+        for w, pr in plan:
             steps = args.steps if w in ("decode", "sgemm") else max(3, min(args.steps, 5))
-            r = measure(w, rank, world, steps, 3, prec, peaks,
-                        with_e2e=w in ("decode", "sgemm"))
-            r["config"] = WORKLOADS[w]["desc"]
-            also.append(r)
-    if world > 1 and args.sharded:
-        for w in args.sharded.split(","):
-            also.append(measure_sharded(w.strip(), world, max(3, min(args.steps, 10)), 3, prec,
-                                        peaks))
+            r = measure(w, rank, world, steps, 3, pr, peaks,
+                        with_e2e=w in ("decode", "sgemm") and pr == prec)
+            also.append(compact(w, r, pr))
+    if world > 1 and args.sharded and not args.no_also:
+        for w in [x.strip() for x in args.sharded.split(",") if x.strip()]:
+            for pr in ((prec,) if w == "decode" else ("3xtf32", "tf32")):
+                also.append(measure_sharded(w, rank, world, max(3, min(args.steps, 8)), 3, pr))
     if orig_affinity is not None:
         os.sched_setaffinity(0, orig_affinity)  # the CPU baseline uses every host core
     cpu = None
@@ -697,16 +763,14 @@ def main():
                 "ms_per_step": head["ms_per_step"], "higher_is_better": True,
                 "scaling": "weak", "vs_baseline": None, "dtype": "f32",
                 "precision": prec, "data": "synthetic (seeded N(0,1) / U[-1,1])",
-                "config": {"workload": WORKLOADS[args.workload]["desc"],
-                           "l2": head["l2"], "parallelism": f"batch-x-heads x{world}",
-                           "global_batch": world},
+                "config": config_of(args.workload, world),
                 "e2e": head.get("e2e"), "roofline": head["roofline"],
                 "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
                 "cpu_baseline": cpu, "also": also}
         line["host_binding"] = binding
         if head.get("e2e_resident"):
             line["e2e_resident"] = head["e2e_resident"]
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line, separators=(",", ":")), flush=True)
     if world > 1:
         import torch.distributed as dist
 

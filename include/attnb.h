@@ -41,6 +41,17 @@ extern "C" {
 #define ATTNB_ERR_RUNTIME 2          /* unsupported configuration: std::runtime_error */
 #define ATTNB_ERR_CUDA 3             /* a CUDA runtime/driver call failed */
 #define ATTNB_ERR_DEVICE_TIMEOUT 4   /* a bounded in-kernel wait expired */
+#define ATTNB_ERR_OUT_OF_MEMORY 5    /* device memory could not be had: std::bad_alloc */
+
+/* Device memory.  Scratch (packed operands, split partials) and the device
+ * copies of host-pointer calls' data live in per-device arenas that grow on
+ * demand and are reused.  A growth that cudaMalloc refuses, or that would take
+ * the arenas past ATTNB_DEVICE_ARENA_CAP_MB MiB (environment variable, read
+ * once; unset or 0 = no cap), fails the call with ATTNB_ERR_OUT_OF_MEMORY
+ * before any of its work is enqueued; the library stays usable for calls that
+ * fit.  The reference allocates with std::vector, so its allocation failures
+ * are std::bad_alloc (MemoryError in Python), which the shims and the Python
+ * module raise for this code. */
 
 /* Arithmetic used by the tensor-core contractions (SGEMM, projections,
  * prefill attention).  Decode is always plain fp32 FMA on CUDA cores.
@@ -123,7 +134,10 @@ ATTNB_API int attnb_sgemm_dev(const float* A, int lda, const float* B, int ldb, 
  * op(A) is A stored [M,K] (trans_a = 0, lda >= K) or A^T with A stored [K,M]
  * (trans_a = 1, lda >= M); op(B) is B stored [K,N] (trans_b = 0, ldb >= N) or
  * B^T with B stored [N,K] (trans_b = 1, ldb >= K); ldc >= N; bias may be
- * NULL.  No reference counterpart: the reference's GEMMs take row-major
+ * NULL.  M <= 0 or N <= 0 leaves C untouched; K == 0 (an empty product; A and
+ * B are not read and may be NULL) gives C = beta * C + bias, where beta == 0
+ * never reads C; K < 0 is ATTNB_ERR_INVALID_ARGUMENT.
+ * No reference counterpart: the reference's GEMMs take row-major
  * operands only (include/gemm.h:11-20).  The sharded MHA block uses it to read
  * the all-gathered context in its transposed layout. */
 ATTNB_API int attnb_gemm_ex_dev(int trans_a, int trans_b, const float* A, int lda, const float* B,
@@ -154,7 +168,10 @@ ATTNB_API int attnb_attn_step_dense_dev(const attnb_tensor* Q, const attnb_tenso
  * GPU that loads the library until exit; calls needing more are rejected with
  * ATTNB_ERR_INVALID_ARGUMENT.  All calls share that array: calls that overlap
  * on the GPU race.  The first call on a device looks up the array's address;
- * make it before any stream capture.  Allocates nothing. */
+ * make it before any stream capture.  The address is cached per device and
+ * CUDA context: the first call after the caller recreates the device's context
+ * (e.g. cudaDeviceReset) looks it up again, and likewise belongs before any
+ * capture.  Allocates nothing. */
 ATTNB_API int attnb_attn_step_dense_noalloc(const attnb_tensor* Q, const attnb_tensor* K,
                                             const attnb_tensor* V, attnb_mtensor* O,
                                             void* stream);

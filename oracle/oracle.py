@@ -26,13 +26,22 @@ _i64 = ctypes.c_int64
 _ll = ctypes.c_longlong
 
 
+# Source tree of the reference (the directory holding src/ and include/), for
+# building _ref/libattnref.so; unset means the reference part is not built.
+REF_ENV = "ATTNB_REFERENCE_SRC"
+
+
 def build(with_reference: bool | None = None) -> None:
-    """Compile the checkers (the reference part only where its tree exists)."""
+    """Compile the checkers: the restatement always, the reference library when
+    the environment variable ATTNB_REFERENCE_SRC names its source tree."""
     targets = ["port"]
+    ref_dir = os.environ.get(REF_ENV, "")
     if with_reference is None:
-        with_reference = os.path.isdir("/root/reference/src")
+        with_reference = bool(ref_dir) and os.path.isdir(os.path.join(ref_dir, "src"))
     if with_reference:
-        targets.append("ref")
+        if not ref_dir:
+            raise RuntimeError(f"{REF_ENV} must name the reference's source tree")
+        targets += ["ref", f"REF={ref_dir}"]
     subprocess.run(["make", "-s", "-C", HERE] + targets, check=True)
 
 
@@ -118,6 +127,15 @@ def sgemm_rows(A, B, rows, alpha=1.0):
     """alpha * A[rows] . B in float64 (numpy), for sampled checks of large GEMMs."""
     A = np.asarray(A)
     return (alpha * (A[rows].astype(np.float64) @ np.asarray(B, np.float64))).astype(np.float32)
+
+
+def linear_f64(x, W, b=None):
+    """y = x . W^T + b in float64 (numpy BLAS), for the projections of sampled
+    checks at full size, where the scalar restatement would take minutes."""
+    y = np.asarray(x, np.float64) @ np.asarray(W, np.float64).T
+    if b is not None:
+        y += np.asarray(b, np.float64)
+    return y
 
 
 def linear(x, W, b=None):

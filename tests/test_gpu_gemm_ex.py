@@ -61,3 +61,30 @@ def test_gemm_ex_argument_checks(cuda):
     assert L.attnb_gemm_ex_dev(1, 0, p, 3, p, 4, None, p, 4, 4, 4, 4, 1.0, 0.0, -1, None) != 0
     # empty problem: nothing to do
     assert L.attnb_gemm_ex_dev(0, 0, p, 4, p, 4, None, p, 4, 0, 4, 4, 1.0, 0.0, -1, None) == 0
+
+
+@pytest.mark.parametrize("beta", [0.0, 0.5])
+def test_gemm_ex_empty_inner_dimension(cuda, beta):
+    """K == 0: the product is empty, so C = beta * C + bias (beta == 0 does not
+    read C, whatever it holds); A and B are not read and may be NULL."""
+    import torch
+    from attn_cpu import capi
+
+    M, N = 37, 70
+    rng = np.random.default_rng(5)
+    C0 = rng.standard_normal((M, N), dtype=np.float32)
+    bias = rng.standard_normal(N, dtype=np.float32)
+    C = torch.from_numpy(C0).cuda()
+    if beta == 0.0:
+        C.fill_(float("nan"))
+    b = torch.from_numpy(bias).cuda()
+    rc = capi.lib().attnb_gemm_ex_dev(0, 0, None, 0, None, N, b.data_ptr(), C.data_ptr(), N, M,
+                                      N, 0, 1.0, beta, -1,
+                                      torch.cuda.current_stream().cuda_stream)
+    assert rc == capi.OK, capi.lib().attnb_last_error()
+    torch.cuda.synchronize()
+    ref = beta * C0.astype(np.float64) + bias if beta else np.broadcast_to(bias, (M, N))
+    assert np.array_equal(C.cpu().numpy(), ref.astype(np.float32))
+    # K < 0 is rejected
+    assert capi.lib().attnb_gemm_ex_dev(0, 0, None, 0, None, N, None, C.data_ptr(), N, M, N, -1,
+                                        1.0, beta, -1, None) == capi.ERR_INVALID_ARGUMENT

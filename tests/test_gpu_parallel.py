@@ -3,7 +3,6 @@ two ranks, one per GPU, against the oracle.  Skipped on a single-GPU box; the
 same partition logic is covered on CPU gloo ranks by test_parallel_gloo.py."""
 from __future__ import annotations
 
-import datetime
 import os
 import socket
 
@@ -33,9 +32,8 @@ def _worker(rank, world, port, q):
 
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=60),
-                            device_id=torch.device("cuda", rank))
+    parallel.init_distributed("nccl", timeout_s=60.0, device=torch.device("cuda", rank),
+                              rank=rank, world_size=world)
     try:
         errs = {}
         g = torch.Generator(device="cuda").manual_seed(0)
@@ -55,6 +53,13 @@ def _worker(rank, world, port, q):
         for shard in ("rows", "cols"):
             C = parallel.gemm_sharded(A, B, shard=shard)
             errs[shard] = float(np.max(np.abs(C.cpu().numpy() - refC)) / np.max(np.abs(refC)))
+        # decode step, 2 x 5 heads (ragged over 2 ranks), T = 700, Dh = 128
+        Qd = torch.randn(10, 128, device="cuda", generator=g)
+        Kd = torch.randn(10, 700, 128, device="cuda", generator=g)
+        Vd = torch.randn(10, 700, 128, device="cuda", generator=g)
+        Od = parallel.attn_step_sharded(Qd, Kd, Vd)
+        refd = oracle.attn_step(Qd.cpu().numpy(), Kd.cpu().numpy(), Vd.cpu().numpy())
+        errs["decode"] = float(np.max(np.abs(Od.cpu().numpy() - refd)) / np.max(np.abs(refd)))
         torch.cuda.synchronize()
         q.put((rank, errs))
     finally:

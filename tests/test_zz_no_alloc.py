@@ -14,6 +14,7 @@ import ctypes
 import numpy as np
 import pytest
 
+import oracle
 from conftest import TOL_FP32, rel_err
 
 pytestmark = pytest.mark.gpu
@@ -51,6 +52,11 @@ def test_noalloc_matches_dev_entry_point_twice(cuda):
         torch.cuda.synchronize()
         assert torch.isfinite(O_na).all()
         assert rel_err(O_na.cpu().numpy(), O_ref.cpu().numpy()) < TOL_FP32
+        # and against the float64 oracle on sampled heads (first, middle, last)
+        heads = [0, 1, H // 2, H - 1]
+        r = oracle.attn_step(Q[heads].cpu().numpy(), K[heads].cpu().numpy(),
+                             V[heads].cpu().numpy())
+        assert rel_err(O_na[heads].cpu().numpy(), r) < TOL_FP32
 
 
 def test_noalloc_small_and_strided(cuda):
