@@ -45,10 +45,12 @@ constexpr int BM = 128;        // query rows per CTA
 constexpr int BN = 128;        // keys per KV tile
 constexpr int BK = 32;         // fp32 elements per 128-byte swizzle row
 constexpr int kThreads = 320;  // warp 0 TMA, warp 1 MMA, warps 2-9 softmax (two groups)
+// Fused form: two more warps (10 and 11) split the raw V slices as they land,
+// off the softmax warps' path.  Twelve warps still leave 168 registers a
+// thread (three warps per SM sub-partition, as with ten).
+constexpr int kThreadsFused = 384;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr int kMaxSplits = 8;  // key splits of a query tile: one portable cluster
-// Fused form: V slices split by warp 0 (the rest by the eight softmax warps).
-constexpr int kVSlicesWarp0 = 2;
 
 // QRES: the CTA's Q tile is loaded once and stays in shared memory, and the
 // S ring carries K slices only (deeper for the same bytes).  Used by the
@@ -85,13 +87,15 @@ struct AttnCfg {
   static constexpr int SMEM = RING_BYTES + 1024;
   // Fused form: raw V rows of the tile's key slices staged past the rings.
   static constexpr int SMEM_FUSED = RING_BYTES + (BN / BK) * VBOX + 1024;
-  // Split merge: each CTA of a cluster stages its unnormalised rows in its
-  // idle rings as [O (DHP floats) | m | l | valid | spare] (OP floats, a
-  // multiple of 16 bytes) and receives the other splits' rows of its share
-  // of the tile behind them.
+  // Split merge: the CTAs of a cluster push their unnormalised rows to the
+  // CTA that merges them (rows [q * rows_per, ...) to rank q) as [O (DHP
+  // floats) | m | l | valid | spare] (OP floats, a multiple of 16 bytes).
+  // They land in q's receive area at the start of its Q / S region, idle by
+  // then, one block of rows per sending split: at most 127 rows in all.
   static constexpr int OP = DHP + 4;
-  static constexpr int RECV = BM * OP * 4;
-  static constexpr int WTS = 2 * BM * OP * 4;  // per-row split weights, [64][8] floats
+  static constexpr int RECV_MAX = (BM - 1) * OP * 4;
+  // Staging of the rows a CTA sends, at their row positions, behind it.
+  static constexpr int STAGE_END = RECV_MAX + BM * OP * 4;
   // TMEM: NBUF S buffers ([big | small] key columns each), then NBUF P.V
   // accumulators ([big | small] head columns).  Two of each when they fit
   // (1xTF32): S(j+1) then runs during the softmax of tile j, and PV(j) is
@@ -109,7 +113,8 @@ struct AttnCfg {
   static_assert(V_STAGES >= 2 && S_STAGES >= 2, "rings need two stages");
   static_assert(!QRES || !SPLIT3, "resident Q is a 1xTF32 layout");
   static_assert(BM * (DHP + 1) * 4 <= RING_BYTES, "output staging fits the rings");
-  static_assert(WTS + 64 * 8 * 4 <= RING_BYTES, "merge staging fits the rings");
+  static_assert(RECV_MAX <= V_RING, "merge receive area fits the Q / S region");
+  static_assert(STAGE_END <= RING_BYTES, "merge staging fits the rings");
   static_assert(NBUF * (S_BUF + PV_BUF) <= TMEM_COLS, "TMEM budget");
 };
 
@@ -201,113 +206,11 @@ __device__ __forceinline__ void fused_split_v_slice(uint8_t* ring, int vb, int l
   fence_proxy_async_smem();
 }
 
-// Final rows of a split tile.  CTA rank q of the cluster owns rows
-// [q * rows_per, ...), rows_per = ceil(128 / nsplit): every CTA bulk-copies
-// the staged rows each peer owns into that peer's receive area (one copy per
-// peer, signalled on the peer's recv_bar), then combines its own rows with
-// the received ones from local shared memory -- the online-softmax merge
-// m_* = max m_s, O = sum 2^(m_s - m_*) O_s, l likewise -- normalises and
-// stores them; the 256 threads of warps 2-9 take (row, 4 columns) items, so
-// consecutive threads write consecutive output columns.  Nothing is stored
-// when any split reported a failed wait.
-template <int DHP, bool SPLIT3, bool QRES>
-__device__ __forceinline__ void cluster_merge(uint32_t base, uint32_t recv_bar,
-                                              const AttnParams& p, int qt, int h,
-                                              volatile int* abort_p, int* merge_fail) {
-  using Cfg = AttnCfg<DHP, SPLIT3, QRES>;
-  constexpr int C4 = DHP / 4;
-  const int ns = p.nsplit;
-  const int me = (int)cluster_ctarank();
-  const int rows_per = (BM + ns - 1) / ns;
-  const int row0 = me * rows_per;
-  const int nrows = min(rows_per, BM - row0);  // rows this CTA receives and merges
-  if (threadIdx.x == 64) {
-    for (int q = 0; q < ns; ++q) {
-      if (q == me) continue;
-      const int k = me < q ? me : me - 1;  // this CTA's slot in q's receive area
-      const int qrows = min(rows_per, BM - q * rows_per);
-      bulk_copy_to_peer(map_shared_rank(base + Cfg::RECV + k * rows_per * Cfg::OP * 4, q),
-                        base + q * rows_per * Cfg::OP * 4, qrows * Cfg::OP * 4,
-                        map_shared_rank(recv_bar, q));
-    }
-  }
-  const float* own = reinterpret_cast<const float*>(
-      static_cast<const uint8_t*>(__cvta_shared_to_generic(base)));
-  const float* recv = own + Cfg::RECV / 4;
-  // Every split's rows carry its validity flag (the first row's suffices).
-  // The decision is shared by all 256 threads (they meet at barriers below).
-  if (!mbar_wait(recv_bar, 0, abort_p, p.status)) *merge_fail = 1;
-  named_bar_sync(1, 256);
-  bool valid = *merge_fail == 0;
-  for (int s = 0; valid && s < ns; ++s) {
-    const float* first = s == me ? own : recv + (s < me ? s : s - 1) * rows_per * Cfg::OP;
-    valid = first[DHP + 2] != 0.f;
-  }
-  if (!valid) {
-    // Copies that never landed (only after an abort) finish before the exit.
-    if (threadIdx.x == 64) {
-      const uint64_t t0 = globaltimer();
-      while (!mbar_try_wait(recv_bar, 0) && globaltimer() - t0 < ATTNB_WAIT_LIMIT_NS) {
-      }
-    }
-    return;
-  }
-  const int vrows = min(nrows, p.L - qt * BM - row0);  // rows inside the output
-  const bool vec = p.osD == 1 && (p.osT & 3) == 0 && (p.osH & 3) == 0 &&
-                   (reinterpret_cast<uintptr_t>(p.O) & 15u) == 0;
-  auto row_of = [&](int s, int lr) {
-    return s == me ? own + (row0 + lr) * Cfg::OP
-                   : recv + ((s < me ? s : s - 1) * rows_per + lr) * Cfg::OP;
-  };
-  // Per row, once: the weight of each split, 2^(m_s - m_*) / sum_s 2^(m_s - m_*) l_s
-  // (rows_per <= 64 rows of kMaxSplits floats, behind the receive area).
-  float(*wts)[kMaxSplits] = reinterpret_cast<float(*)[kMaxSplits]>(
-      static_cast<uint8_t*>(__cvta_shared_to_generic(base)) + Cfg::WTS);
-  for (int lr = threadIdx.x - 64; lr < vrows; lr += 256) {
-    float mstar = -INFINITY;
-    for (int s = 0; s < ns; ++s) mstar = fmaxf(mstar, row_of(s, lr)[DHP]);
-    float w[kMaxSplits], lsum = 0.f;
-#pragma unroll
-    for (int s = 0; s < kMaxSplits; ++s) {
-      if (s >= ns) break;
-      const float2 ml = *reinterpret_cast<const float2*>(row_of(s, lr) + DHP);
-      w[s] = ml.x == -INFINITY ? 0.f : fast_exp2(ml.x - mstar);
-      lsum = fmaf(w[s], ml.y, lsum);
-    }
-    const float inv = 1.f / lsum;
-#pragma unroll
-    for (int s = 0; s < kMaxSplits; ++s)
-      if (s < ns) wts[lr][s] = w[s] * inv;
-  }
-  named_bar_sync(1, 256);
-  for (int item = threadIdx.x - 64; item < vrows * C4; item += 256) {
-    const int lr = item / C4, d = (item % C4) * 4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s = 0; s < ns; ++s) {
-      const float w = wts[lr][s];
-      const float4 v = *reinterpret_cast<const float4*>(row_of(s, lr) + d);
-      acc.x = fmaf(w, v.x, acc.x);
-      acc.y = fmaf(w, v.y, acc.y);
-      acc.z = fmaf(w, v.z, acc.z);
-      acc.w = fmaf(w, v.w, acc.w);
-    }
-    float* orow = p.O + h * p.osH + (int64_t)(qt * BM + row0 + lr) * p.osT;
-    if (vec && d + 3 < p.Dh) {
-      *reinterpret_cast<float4*>(orow + d) = acc;
-    } else {
-      const float v[4] = {acc.x, acc.y, acc.z, acc.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k)
-        if (d + k < p.Dh) orow[(int64_t)(d + k) * p.osD] = v[k];
-    }
-  }
-}
-
 // FUSED: every CTA owns one key tile, loaded raw by TMA and split in shared
 // memory (Q/K by the softmax warps 2-9 before their softmax, V by warp 0).
 // Otherwise warp 0 streams pre-packed tiles.
 template <int DHP, bool SPLIT3, bool FUSED>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmQh, const __grid_constant__ CUtensorMap tmQl,
                    const __grid_constant__ CUtensorMap tmKh, const __grid_constant__ CUtensorMap tmKl,
                    const __grid_constant__ CUtensorMap tmVh, const __grid_constant__ CUtensorMap tmVl,
@@ -330,11 +233,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t sfull[SST], sempty[SST], vfull[VST], vempty[VST];
   __shared__ __align__(8) uint64_t s_bar[2], p_bar, pv_bar[2], final_bar, recv_bar, q_bar;
+  __shared__ __align__(8) uint64_t ready_bar;  // split merge: peers' Q / S regions are idle
   __shared__ __align__(8) uint64_t rbar[FUSED ? 8 : 1];  // fused: raw Q/K (per slice), V slices
   __shared__ uint32_t tmem_slot;
   __shared__ int abort_flag;
   __shared__ int softmax_failed;  // any softmax thread saw a wait fail
-  __shared__ int merge_fail;      // a split-merge wait failed
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qt = blockIdx.x, split = blockIdx.y, h = blockIdx.z;
@@ -354,7 +257,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     abort_flag = 0;
     softmax_failed = 0;
-    merge_fail = 0;
     // Full barriers: one TMA arrival with a byte count, or in the fused form
     // (whose stages are each filled once) one arrival per splitting warp.
     for (int i = 0; i < SST; ++i) {
@@ -362,7 +264,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_addr(&sempty[i]), 1);
     }
     for (int i = 0; i < VST; ++i) {
-      mbar_init(smem_addr(&vfull[i]), FUSED && i >= kVSlicesWarp0 ? 8 : 1);
+      mbar_init(smem_addr(&vfull[i]), FUSED ? 2 : 1);  // fused: both V-splitting warps
       mbar_init(smem_addr(&vempty[i]), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -372,10 +274,18 @@ __global__ void __launch_bounds__(kThreads, 1)
     mbar_init(smem_addr(&p_bar), 8);  // one arrival per softmax warp
     mbar_init(smem_addr(&final_bar), 1);
     mbar_init(smem_addr(&recv_bar), 1);
+    mbar_init(smem_addr(&ready_bar), p.nsplit > 1 ? p.nsplit - 1 : 1);
     mbar_init(smem_addr(&q_bar), 1);
     if (FUSED)
       for (int i = 0; i < 8; ++i) mbar_init(smem_addr(&rbar[i]), 1);
     fence_barrier_init();
+    if (p.nsplit > 1) {
+      // The other splits' rows of this CTA's share: DHP floats and (m, l,
+      // valid, spare) per row from each of them.
+      const int rows_per = (BM + p.nsplit - 1) / p.nsplit;
+      const int mine = min(rows_per, BM - (int)cluster_ctarank() * rows_per);
+      mbar_arrive_expect_tx(smem_addr(&recv_bar), (p.nsplit - 1) * mine * (DHP * 4 + 16));
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_addr(&tmem_slot), Cfg::TMEM_COLS);
@@ -386,6 +296,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
   volatile int* abort_p = &abort_flag;
+  // Split cluster barrier, first phase: waited on before any access to a
+  // peer's barriers or shared memory.  Every thread arrives and waits twice
+  // (the second phase ends before the exit).
+  if (p.nsplit > 1) cluster_arrive_relaxed();
   grid_dep_wait();  // packed operands (or, fused, the raw ones) come from earlier kernels
 
   if (warp == 0) {
@@ -393,8 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ----------------------------------------------- raw loads (fused form)
       // Lane 0 loads the only key tile's Q/K slices into the S stages' hi
       // slots and its V rows (32 keys x 32 columns per box) into the staging
-      // area; then the warp splits the first V slices while the softmax warps
-      // split Q/K (and, after that, the remaining V slices).
+      // area; the softmax warps split Q/K, warps 10-11 split V.
       const int j = j0;
       const int nvb = min(BN / BK, (p.T - j * BN + BK - 1) / BK);
       if (lane == 0) {
@@ -411,16 +324,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int bx = 0; bx < DHP / 32; ++bx)
             tma_load_3d(va + bx * 4096, &tmVh, rb, bx * 32, j * BN + vb * BK, h);
         }
-      }
-      __syncwarp();
-      uint8_t* ring = smem_raw + (base - smem_addr(smem_raw));
-      bool conv = true;
-      for (int vb = 0; vb < min(nvb, kVSlicesWarp0); ++vb) {
-        if (conv && !mbar_wait(smem_addr(&rbar[Cfg::NKB + vb]), 0, abort_p, p.status))
-          conv = false;
-        if (conv) fused_split_v_slice<DHP, SPLIT3>(ring, vb, lane, 0, 1);
-        __syncwarp();
-        if (conv && lane == 0) mbar_arrive(smem_addr(&vfull[vb]));
       }
       // Every copy lands before the CTA can exit (they are never cancelled).
       if (lane == 0)
@@ -481,6 +384,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int i = 0; i < VST; ++i)
         if (rv.issued_mask & (1u << i))
           drain_wait(smem_addr(&vfull[i]), (rv.issued_parity >> i) & 1u, p.status);
+    }
+    if (p.nsplit > 1) {
+      cluster_wait_acquire();
+      cluster_arrive_release();
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -575,6 +482,31 @@ __global__ void __launch_bounds__(kThreads, 1)
       mma_commit(smem_addr(&final_bar));
       drain_wait(smem_addr(&final_bar), 0, p.status);
     }
+    if (p.nsplit > 1) {
+      cluster_wait_acquire();
+      cluster_arrive_release();
+    }
+  } else if (FUSED && warp >= 10) {
+    // ------------------------------------------- V split (fused form, 2 warps)
+    // Each raw V slice, as it lands, is split and transposed into its V^T
+    // stage by both warps (alternate column groups); each warp's lane 0
+    // arrives on the stage's full barrier.
+    if (j0 < j1) {
+      uint8_t* ring = smem_raw + (base - smem_addr(smem_raw));
+      const int nvb = min(BN / BK, (p.T - j0 * BN + BK - 1) / BK);
+      bool conv = true;
+      for (int vb = 0; vb < nvb; ++vb) {
+        if (conv && !mbar_wait(smem_addr(&rbar[Cfg::NKB + vb]), 0, abort_p, p.status))
+          conv = false;
+        if (conv) fused_split_v_slice<DHP, SPLIT3>(ring, vb, lane, warp - 10, 2);
+        __syncwarp();
+        if (conv && lane == 0) mbar_arrive(smem_addr(&vfull[vb]));
+      }
+    }
+    if (p.nsplit > 1) {
+      cluster_wait_acquire();
+      cluster_arrive_release();
+    }
   } else {
     // ------------------------------------------------ softmax / output (8 warps)
     // Two warpgroups share every query row (TMEM lane): group g (warps 2-5:
@@ -612,14 +544,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if constexpr (FUSED) if (j0 < j1) {
       bool conv = fused_split_qk<DHP, SPLIT3>(ring, rbar, sfull, threadIdx.x - 64, p.qscale,
                                               abort_p, p.status);
-      const int nvb = min(BN / BK, (p.T - j0 * BN + BK - 1) / BK);
-      for (int vb = kVSlicesWarp0; vb < nvb; ++vb) {
-        if (conv && !mbar_wait(smem_addr(&rbar[Cfg::NKB + vb]), 0, abort_p, p.status))
-          conv = false;
-        if (conv) fused_split_v_slice<DHP, SPLIT3>(ring, vb, lane, sw, 8);
-        __syncwarp();
-        if (conv && lane == 0) mbar_arrive(smem_addr(&vfull[vb]));
-      }
       if (!conv) record_fail(0);
     }
     // TMEM accesses: every wait covers two W-column loads -- the big and
@@ -629,6 +553,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int W = DHP > 64 ? 16 : 32;
     constexpr int SSTEP = SPLIT3 ? W : 2 * W;  // S columns per wait
     static_assert(SCOLS % SSTEP == 0, "S columns per group");
+    // Scores kept in registers between the two passes: in the fused form,
+    // whose single tile leaves the output row zero (no registers) until the
+    // P.V product is folded in.  Elsewhere the registers would spill.
+    constexpr bool KEEP = FUSED;
     // The P.V drain updates the output row in place: 16-column loads once
     // that row takes 64 registers.
     constexpr int WD = DHP > 64 ? 16 : 32;
@@ -673,7 +601,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     float alpha_prev = 1.f;
     bool pending = false;  // a P.V tile not yet folded into o
     int it = 0;
-    for (int j = j0; j < j1; ++j, ++it) {
+    // The fused form holds a single key tile: one iteration, which the
+    // compiler can see (the output row is then still zero during the softmax
+    // and takes no registers there).
+    const int j_end = FUSED ? j0 + 1 : j1;
+    for (int j = j0; j < j_end; ++j, ++it) {
       const uint32_t sbuf = tmem + lane_off + (it % Cfg::NBUF) * Cfg::S_BUF;
       const bool got_s =
           mbar_wait(smem_addr(&s_bar[it % Cfg::NBUF]), (it / Cfg::NBUF) & 1, abort_p, p.status);
@@ -690,22 +622,52 @@ __global__ void __launch_bounds__(kThreads, 1)
         else
           tmem_ld_pair<W>(sbuf + Cfg::S_BIG + col, va, sbuf + Cfg::S_BIG + col + W, vb);
       };
+      // Every key of this thread's columns is valid: no masking in this tile.
+      const bool full = kbase + SCOLS - 1 <= kmax;
+      // Head sizes up to 64: the thread's scores (sv[e] is key kbase + e) stay
+      // in registers from the max pass to the exponent pass.
+      float sv[KEEP ? SCOLS : 1];
       float tmax = -INFINITY;
       if (got_s) {
         tc_fence_after();
-#pragma unroll 1
-        for (int c0 = 0; c0 < SCOLS; c0 += SSTEP) {
-          uint32_t va[W], vb[W];
-          load_s(c0, va, vb);
+        if constexpr (KEEP) {
 #pragma unroll
-          for (int i = 0; i < W; ++i) {
-            if (SPLIT3) {
-              const float v = __uint_as_float(va[i]) + __uint_as_float(vb[i]);
-              if (kbase + c0 + i <= kmax) tmax = fmaxf(tmax, v);
-            } else {
-              const float v0 = __uint_as_float(va[i]), v1 = __uint_as_float(vb[i]);
-              if (kbase + c0 + i <= kmax) tmax = fmaxf(tmax, v0);
-              if (kbase + c0 + W + i <= kmax) tmax = fmaxf(tmax, v1);
+          for (int c0 = 0; c0 < SCOLS; c0 += SSTEP) {
+            uint32_t va[W], vb[W];
+            load_s(c0, va, vb);
+#pragma unroll
+            for (int i = 0; i < W; ++i) {
+              if (SPLIT3) {
+                sv[c0 + i] = __uint_as_float(va[i]) + __uint_as_float(vb[i]);
+              } else {
+                sv[c0 + i] = __uint_as_float(va[i]);
+                sv[c0 + W + i] = __uint_as_float(vb[i]);
+              }
+            }
+          }
+          if (full) {
+#pragma unroll
+            for (int e = 0; e < SCOLS; ++e) tmax = fmaxf(tmax, sv[e]);
+          } else {
+#pragma unroll
+            for (int e = 0; e < SCOLS; ++e)
+              if (kbase + e <= kmax) tmax = fmaxf(tmax, sv[e]);
+          }
+        } else {
+#pragma unroll 1
+          for (int c0 = 0; c0 < SCOLS; c0 += SSTEP) {
+            uint32_t va[W], vb[W];
+            load_s(c0, va, vb);
+#pragma unroll
+            for (int i = 0; i < W; ++i) {
+              if (SPLIT3) {
+                const float v = __uint_as_float(va[i]) + __uint_as_float(vb[i]);
+                if (kbase + c0 + i <= kmax) tmax = fmaxf(tmax, v);
+              } else {
+                const float v0 = __uint_as_float(va[i]), v1 = __uint_as_float(vb[i]);
+                if (kbase + c0 + i <= kmax) tmax = fmaxf(tmax, v0);
+                if (kbase + c0 + W + i <= kmax) tmax = fmaxf(tmax, v1);
+              }
             }
           }
         }
@@ -721,26 +683,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       // P = 2^(s - m_new) (0 past the last valid key), split into tf32 hi and
       // the fp32 remainder for 3xTF32.
       auto p_of = [&](float v, int key, float& lo) {
-        const float pv = key <= kmax ? fast_exp2(v - m_new) : 0.f;
+        const float pv = (full || key <= kmax) ? fast_exp2(v - m_new) : 0.f;
         lsum += pv;
         const float hi = tf32_round(pv);
         lo = pv - hi;
         return hi;
       };
-#pragma unroll 1
-      for (int c0 = 0; c0 < SCOLS; c0 += SSTEP) {
-        uint32_t va[W], vb[W];
+      // One step: P of columns c0.. into TMEM, from the scores in va / vb
+      // (or, KEEP, in sv).
+      auto p_step = [&](int c0, uint32_t (&va)[W], uint32_t (&vb)[W]) {
         const uint32_t col = g * SCOLS + c0;
-        load_s(c0, va, vb);
 #pragma unroll
         for (int i = 0; i < W; ++i) {
           float lo;
           if (SPLIT3) {
-            const float v = __uint_as_float(va[i]) + __uint_as_float(vb[i]);
+            const float v =
+                KEEP ? sv[KEEP ? c0 + i : 0] : __uint_as_float(va[i]) + __uint_as_float(vb[i]);
             va[i] = __float_as_uint(p_of(v, kbase + c0 + i, lo));
             vb[i] = __float_as_uint(lo);
           } else {
-            const float v0 = __uint_as_float(va[i]), v1 = __uint_as_float(vb[i]);
+            const float v0 = KEEP ? sv[KEEP ? c0 + i : 0] : __uint_as_float(va[i]);
+            const float v1 = KEEP ? sv[KEEP ? c0 + W + i : 0] : __uint_as_float(vb[i]);
             va[i] = __float_as_uint(p_of(v0, kbase + c0 + i, lo));
             vb[i] = __float_as_uint(p_of(v1, kbase + c0 + W + i, lo));
           }
@@ -751,6 +714,20 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           tmem_st_w<W>(sbuf + Cfg::S_BIG + col, va);
           tmem_st_w<W>(sbuf + Cfg::S_BIG + col + W, vb);
+        }
+      };
+      if constexpr (KEEP) {
+#pragma unroll
+        for (int c0 = 0; c0 < SCOLS; c0 += SSTEP) {
+          uint32_t va[W], vb[W];
+          p_step(c0, va, vb);
+        }
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < SCOLS; c0 += SSTEP) {
+          uint32_t va[W], vb[W];
+          load_s(c0, va, vb);
+          p_step(c0, va, vb);
         }
       }
       tmem_wait_st();
@@ -794,28 +771,132 @@ __global__ void __launch_bounds__(kThreads, 1)
     named_bar_sync(1, 256);
     l += red[g ^ 1][r];
     if (p.nsplit > 1) {
-      // Stage this split's unnormalised rows for the cluster merge after the
-      // role branches (16-byte writes at a 16-byte-aligned pitch: conflict
-      // free), and arm the barrier that receives the other splits' rows.
-      float* so = reinterpret_cast<float*>(ring);
-      if (ok) {
+      // ---------------------------------------------------- split merge
+      // Row r of the tile is merged by cluster rank q = r / rows_per.  Each
+      // split stages the rows other ranks merge (this group's columns; group
+      // 0 adds m, l and its validity) at their row positions past the receive
+      // area, and one thread bulk-copies each rank's block of rows into that
+      // rank's receive area (bytes counted on its recv_bar) once every rank
+      // has reported its Q / S region idle.  The threads of rank q holding
+      // row r then combine it with the received rows -- the online-softmax
+      // merge m* = max m_s, O = sum 2^(m_s - m*) O_s, l likewise -- and store
+      // it.  Nothing is stored for a row when any split reported a failure.
+      const int ns = p.nsplit;
+      const int me = (int)cluster_ctarank();
+      const int rows_per = (BM + ns - 1) / ns;
+      const int q = r / rows_per;
+      float* stage = reinterpret_cast<float*>(ring + Cfg::RECV_MAX);
+      if (q != me) {
+        float* srow = stage + r * Cfg::OP;
 #pragma unroll
         for (int c = 0; c < CH0; ++c) {
           if (c_lo + c >= c_hi) break;
 #pragma unroll
-          for (int q = 0; q < 8; ++q)
-            *reinterpret_cast<float4*>(so + r * Cfg::OP + (c_lo + c) * 32 + q * 4) =
-                make_float4(o[c * 32 + q * 4], o[c * 32 + q * 4 + 1], o[c * 32 + q * 4 + 2],
-                            o[c * 32 + q * 4 + 3]);
+          for (int i = 0; i < 8; ++i)
+            *reinterpret_cast<float4*>(srow + (c_lo + c) * 32 + i * 4) =
+                make_float4(o[c * 32 + i * 4], o[c * 32 + i * 4 + 1], o[c * 32 + i * 4 + 2],
+                            o[c * 32 + i * 4 + 3]);
         }
-        if (g == 0) *reinterpret_cast<float2*>(so + r * Cfg::OP + DHP) = make_float2(m, l);
+        if (g == 0)
+          *reinterpret_cast<float4*>(srow + DHP) = make_float4(m, l, ok ? 1.f : 0.f, 0.f);
+        fence_proxy_async_smem();  // the rows leave by bulk copies (async proxy)
       }
-      if (g == 0) so[r * Cfg::OP + DHP + 2] = ok ? 1.f : 0.f;
-      fence_proxy_async_smem();  // the rows leave by bulk copies (async proxy)
-      if (leader) {
-        const int rows_per = (BM + p.nsplit - 1) / p.nsplit;
-        const int mine = min(rows_per, BM - (int)cluster_ctarank() * rows_per);
-        mbar_arrive_expect_tx(smem_addr(&recv_bar), (p.nsplit - 1) * mine * Cfg::OP * 4);
+      cluster_wait_acquire();  // the peers' barriers are initialised
+      // Every S product of this CTA has completed (the tile loop ran to its
+      // end), so nothing reads the Q / S region any more.
+      if (leader && it == j1 - j0)
+        for (int t = 0; t < ns; ++t)
+          if (t != me) mbar_arrive_remote(map_shared_rank(smem_addr(&ready_bar), t));
+      named_bar_sync(1, 256);  // every staged row is written
+      if (threadIdx.x == 64 && mbar_wait_cluster(smem_addr(&ready_bar), 0, abort_p, p.status)) {
+        for (int t = 0; t < ns; ++t) {
+          if (t == me) continue;
+          const int k = me < t ? me : me - 1;  // this split's block in t's receive area
+          const int trows = min(rows_per, BM - t * rows_per);
+          bulk_copy_to_peer(map_shared_rank(base + k * rows_per * Cfg::OP * 4, t),
+                            base + Cfg::RECV_MAX + t * rows_per * Cfg::OP * 4,
+                            trows * Cfg::OP * 4, map_shared_rank(smem_addr(&recv_bar), t));
+        }
+      }
+      // The rows this CTA merges have all landed (or, after a failure, every
+      // copy that was issued has), so the other ranks' staging is free when
+      // the second phase ends.
+      bool got = true;
+      if (q == me) {
+        got = mbar_wait_cluster(smem_addr(&recv_bar), 0, abort_p, p.status);
+        if (!got) {
+          const uint64_t t0 = globaltimer();
+          while (!mbar_try_wait_cluster(smem_addr(&recv_bar), 0) &&
+                 globaltimer() - t0 < ATTNB_WAIT_LIMIT_NS) {
+          }
+        }
+      }
+      cluster_arrive_release();
+      if (q == me) {
+        const int lr = r - me * rows_per;
+        const float* recv = reinterpret_cast<const float*>(ring);
+        // Compact loops: this code runs once per CTA, so its instruction
+        // fetches are on the critical path.
+        bool valid = got && ok;
+        float mstar = m;
+#pragma unroll 1
+        for (int t = 0; t < ns - 1; ++t) {
+          const float* row = recv + (t * rows_per + lr) * Cfg::OP;
+          valid = valid && row[DHP + 2] != 0.f;
+          mstar = fmaxf(mstar, row[DHP]);
+        }
+        const int qrow = qt * BM + r;
+        if (valid && qrow < p.L) {
+          // This row's merged values of this group's columns, written over o.
+          const float wme = m == -INFINITY ? 0.f : fast_exp2(m - mstar);
+          float lsum = wme * l;
+#pragma unroll
+          for (int e = 0; e < CH0 * 32; ++e) o[e] *= wme;
+#pragma unroll 1
+          for (int t = 0; t < ns - 1; ++t) {
+            const float* row = recv + (t * rows_per + lr) * Cfg::OP;
+            const float w = row[DHP] == -INFINITY ? 0.f : fast_exp2(row[DHP] - mstar);
+            lsum = fmaf(w, row[DHP + 1], lsum);
+#pragma unroll
+            for (int c = 0; c < CH0; ++c) {
+              if (c_lo + c >= c_hi) break;
+#pragma unroll
+              for (int i = 0; i < 8; ++i) {
+                const float4 v = *reinterpret_cast<const float4*>(row + (c_lo + c) * 32 + i * 4);
+                o[c * 32 + i * 4] = fmaf(w, v.x, o[c * 32 + i * 4]);
+                o[c * 32 + i * 4 + 1] = fmaf(w, v.y, o[c * 32 + i * 4 + 1]);
+                o[c * 32 + i * 4 + 2] = fmaf(w, v.z, o[c * 32 + i * 4 + 2]);
+                o[c * 32 + i * 4 + 3] = fmaf(w, v.w, o[c * 32 + i * 4 + 3]);
+              }
+            }
+          }
+          const float inv = 1.f / lsum;
+          const bool vec = p.osD == 1 && (p.osT & 3) == 0 && (p.osH & 3) == 0 &&
+                           (reinterpret_cast<uintptr_t>(p.O) & 15u) == 0 &&
+                           c_hi * 32 <= p.Dh;
+          float* orow = p.O + h * p.osH + (int64_t)qrow * p.osT;
+          if (vec) {
+#pragma unroll
+            for (int c = 0; c < CH0; ++c) {
+              if (c_lo + c >= c_hi) break;
+#pragma unroll
+              for (int i = 0; i < 8; ++i)
+                *reinterpret_cast<float4*>(orow + (c_lo + c) * 32 + i * 4) =
+                    make_float4(o[c * 32 + i * 4] * inv, o[c * 32 + i * 4 + 1] * inv,
+                                o[c * 32 + i * 4 + 2] * inv, o[c * 32 + i * 4 + 3] * inv);
+            }
+          } else {
+#pragma unroll
+            for (int c = 0; c < CH0; ++c) {
+              if (c_lo + c >= c_hi) break;
+#pragma unroll
+              for (int i = 0; i < 32; ++i) {
+                const int d = (c_lo + c) * 32 + i;
+                if (d < p.Dh) orow[(int64_t)d * p.osD] = o[c * 32 + i] * inv;
+              }
+            }
+          }
+        }
       }
     }
     const bool write_out = (p.nsplit == 1) && ok;
@@ -869,19 +950,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
-  // ------------------------------------------------------------- split merge
-  // The CTAs of a cluster hold the key splits of one (head, query tile).
-  // After the first barrier every CTA reads the staged rows of all splits
-  // through distributed shared memory and writes its share of the output
-  // rows; the second keeps every CTA's shared memory alive until the others
-  // are done reading it.  Every thread passes both barriers.
-  if (p.nsplit > 1) {
-    cluster_sync_all();
-    if (warp >= 2)
-      cluster_merge<DHP, SPLIT3, Cfg::QRES>(base, smem_addr(&recv_bar), p, qt, h, abort_p,
-                                            &merge_fail);
-    cluster_sync_all();
-  }
+  // Second phase of the split cluster barrier: every CTA's incoming copies
+  // have landed (or been waited for after a failure), so no copy still reads
+  // this CTA's staging or writes its receive area when it exits.
+  if (p.nsplit > 1) cluster_wait_acquire();
 
   tc_fence_before();
   __syncthreads();
@@ -910,11 +982,13 @@ void launch_attn(const CUtensorMap* maps, const AttnParams& prm, int qtiles, cud
   if (prm.nsplit > 1) {
     // The key splits of a (head, query tile) form one cluster (merge through
     // distributed shared memory).
-    ATTNB_CUDA(launch_pdl_cluster(attn_tc_kernel<DHP, SPLIT3, FUSED>, grid, dim3(kThreads), smem,
+    ATTNB_CUDA(launch_pdl_cluster(attn_tc_kernel<DHP, SPLIT3, FUSED>, grid,
+                                  dim3(FUSED ? kThreadsFused : kThreads), smem,
                                   s, dim3(1, prm.nsplit, 1), maps[0], maps[1], maps[2], maps[3],
                                   maps[4], maps[5], maps[6], prm));
   } else {
-    ATTNB_CUDA(launch_pdl(attn_tc_kernel<DHP, SPLIT3, FUSED>, grid, dim3(kThreads), smem, s,
+    ATTNB_CUDA(launch_pdl(attn_tc_kernel<DHP, SPLIT3, FUSED>, grid,
+                          dim3(FUSED ? kThreadsFused : kThreads), smem, s,
                           maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], maps[6], prm));
   }
 }

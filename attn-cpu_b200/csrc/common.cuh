@@ -169,6 +169,40 @@ __device__ __forceinline__ void cluster_sync_all() {
       "barrier.cluster.wait.acquire;" ::: "memory");
 }
 
+// Split cluster barrier: every thread of every CTA in the cluster arrives once
+// and later waits once per phase.  The relaxed arrive follows
+// fence_barrier_init so that peers see this CTA's mbarriers initialised after
+// the matching wait; the release / acquire pair orders shared-memory accesses
+// around the phase.
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_arrive_release() {
+  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait_acquire() {
+  asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+
+// Arrive (release, cluster scope) on an mbarrier of another CTA of the cluster
+// (`bar` is a shared::cluster address from map_shared_rank).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(bar)
+               : "memory");
+}
+
+// Asynchronous 16-byte store into another CTA's shared memory (`dst` and `bar`
+// are shared::cluster addresses from map_shared_rank); its bytes count on the
+// destination CTA's mbarrier `bar` (complete_tx) when they land.
+__device__ __forceinline__ void st_async_v4(uint32_t dst, float a, float b, float c, float d,
+                                            uint32_t bar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, "
+      "[%5];" ::"r"(dst),
+      "f"(a), "f"(b), "f"(c), "f"(d), "r"(bar)
+      : "memory");
+}
+
 // The shared::cluster address of the same shared-memory offset in CTA `rank`.
 __device__ __forceinline__ uint32_t map_shared_rank(uint32_t addr, uint32_t rank) {
   uint32_t r;
@@ -430,11 +464,13 @@ __host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
          | (static_cast<uint32_t>(M >> 4) << 24);    // M / 16
 }
 
-// Round to the nearest tf32 value (low 13 mantissa bits cleared).
+// Round to the nearest tf32 value, ties away from zero (the rounding of
+// cvt.rna.tf32.f32), in two integer operations: adding half a unit of the
+// 10-bit mantissa to the magnitude bits and clearing the low 13 bits rounds
+// the magnitude, a carry into the exponent included.  Exact for every finite
+// value below the largest float; infinities stay infinite.
 __device__ __forceinline__ float tf32_round(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
 
 // 2^x on the special-function unit (PTX ex2.approx.ftz.f32).
