@@ -134,6 +134,7 @@ def test_shard_range_covers_everything():
     (2, ("mha", 1, 17, 48, 3, True)),      # 3 heads over 2 ranks, 17 tokens: ragged
     (3, ("mha", 1, 20, 64, 8, False)),
     (4, ("mha", 2, 16, 32, 2, False)),     # more ranks than heads: two ranks hold none
+    (2, ("mha", 2, 1100, 32, 2, False)),   # 2200 tokens, long sequences
 ])
 def test_sharded_mha_gloo(world, case):
     _run(world, case)
@@ -143,6 +144,7 @@ def test_sharded_mha_gloo(world, case):
     (2, ("gemm", 37, 29, 41, "rows")),
     (2, ("gemm", 37, 29, 41, "cols")),
     (3, ("gemm", 64, 16, 10, "cols")),
+    (3, ("gemm", 3100, 8, 20, "rows")),   # ragged row blocks
 ])
 def test_sharded_gemm_gloo(world, case):
     _run(world, case)
