@@ -254,6 +254,18 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
   const int j0 = split * p.tiles_per_split;
   const int j1 = min(n_kv, j0 + p.tiles_per_split);
 
+  if (threadIdx.x == 32) {
+    // The tensor maps' first use waits for their fetch: start it now (after
+    // an L2 flush it is a DRAM round trip ahead of the first tile's).
+    tma_prefetch_desc(&tmQh);
+    tma_prefetch_desc(&tmKh);
+    tma_prefetch_desc(&tmVh);
+    if (SPLIT3 && !FUSED) {
+      tma_prefetch_desc(&tmQl);
+      tma_prefetch_desc(&tmKl);
+      tma_prefetch_desc(&tmVl);
+    }
+  }
   if (threadIdx.x == 0) {
     abort_flag = 0;
     softmax_failed = 0;
@@ -331,9 +343,6 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
     }
     if (!FUSED && lane == 0) {
       // ------------------------------------------------------------ producer
-      tma_prefetch_desc(&tmQh);
-      tma_prefetch_desc(&tmKh);
-      tma_prefetch_desc(&tmVh);
       const bool load_q = Cfg::QRES && j0 < j1;
       if (load_q) {
         // The CTA's Q tile, once: hi slices kb at base + kb * QBOX.
@@ -387,7 +396,7 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
     }
     if (p.nsplit > 1) {
       cluster_wait_acquire();
-      cluster_arrive_release();
+      cluster_arrive_relaxed();
     }
   } else if (warp == 1) {
     if (lane == 0) {
@@ -484,7 +493,7 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
     }
     if (p.nsplit > 1) {
       cluster_wait_acquire();
-      cluster_arrive_release();
+      cluster_arrive_relaxed();
     }
   } else if (FUSED && warp >= 10) {
     // ------------------------------------------- V split (fused form, 2 warps)
@@ -505,7 +514,7 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
     }
     if (p.nsplit > 1) {
       cluster_wait_acquire();
-      cluster_arrive_release();
+      cluster_arrive_relaxed();
     }
   } else {
     // ------------------------------------------------ softmax / output (8 warps)
@@ -831,7 +840,7 @@ __global__ void __launch_bounds__(FUSED ? kThreadsFused : kThreads, 1)
           }
         }
       }
-      cluster_arrive_release();
+      cluster_arrive_relaxed();
       if (q == me) {
         const int lr = r - me * rows_per;
         const float* recv = reinterpret_cast<const float*>(ring);

@@ -16,10 +16,15 @@
 
 namespace attnb {
 
-// Device status word (one int per device, owned by the host runtime and passed
-// to every kernel that waits): bit 0 = a bounded wait expired.
+// Status word (one int per device, owned by the host runtime and passed to
+// every kernel that waits; page-locked host memory mapped into the device's
+// address space): 1 = a bounded wait expired.  Every writer stores the same
+// value, so a plain store suffices; the fence pushes it to the host.
 __device__ __forceinline__ void raise_timeout(int* status) {
-  if (status) atomicOr(status, 1);
+  if (status) {
+    *reinterpret_cast<volatile int*>(status) = 1;
+    __threadfence_system();
+  }
 }
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -170,15 +175,12 @@ __device__ __forceinline__ void cluster_sync_all() {
 }
 
 // Split cluster barrier: every thread of every CTA in the cluster arrives once
-// and later waits once per phase.  The relaxed arrive follows
-// fence_barrier_init so that peers see this CTA's mbarriers initialised after
-// the matching wait; the release / acquire pair orders shared-memory accesses
-// around the phase.
+// and later waits once per phase.  A relaxed arrive after fence_barrier_init
+// lets peers see this CTA's mbarriers initialised once their wait returns;
+// data that crosses CTAs is ordered by the mbarriers it counts on, not by this
+// barrier.
 __device__ __forceinline__ void cluster_arrive_relaxed() {
   asm volatile("barrier.cluster.arrive.relaxed;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_arrive_release() {
-  asm volatile("barrier.cluster.arrive.release;" ::: "memory");
 }
 __device__ __forceinline__ void cluster_wait_acquire() {
   asm volatile("barrier.cluster.wait.acquire;" ::: "memory");

@@ -47,9 +47,9 @@ struct DeviceCtx {
   int device = -1;
   int num_sms = 0;
   cudaStream_t stream = nullptr;  // used by the host-pointer entry points
-  int* status = nullptr;          // device status word (bit 0: wait time-out)
-  int* status_host = nullptr;     // pinned mirror the status word is read into
-  std::mutex status_mu;           // guards status_host
+  int* status = nullptr;          // status word as kernels see it (1: a wait timed out)
+  int* status_host = nullptr;     // the same word: page-locked host memory, mapped
+  std::mutex status_mu;           // guards reading and clearing it
   std::mutex mu;                  // serialises host-pointer calls on this device
   DeviceBuffer io;                // device copies of host inputs/outputs
   DeviceBuffer scratch_host_path; // kernel scratch for host-pointer calls
