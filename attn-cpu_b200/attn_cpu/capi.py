@@ -25,8 +25,11 @@ PREC = {None: -1, "default": -1, "3xtf32": 0, "tf32": 1}
 EXPORTED = [
     "attnb_last_error", "attnb_version", "attnb_stream_status", "attnb_selftest_wait_timeout",
     "attnb_profile_enable", "attnb_profile_read", "attnb_host_alloc", "attnb_host_free",
-    "attnb_sgemm", "attnb_gemm_jit", "attnb_sgemm_dev", "attnb_gemm_ex_dev", "attnb_linear_dev",
+    "attnb_sgemm", "attnb_gemm_jit", "attnb_sgemm_dev", "attnb_gemm_ex_dev",
+    "attnb_gemm_ex_bcast_dev", "attnb_ipc_alloc", "attnb_ipc_free", "attnb_ipc_export", "attnb_ipc_import", "attnb_ipc_close",
+    "attnb_linear_dev",
     "attnb_attn_step_dense", "attnb_attn_step_dense_dev", "attnb_attn_step_dense_noalloc",
+    "attnb_attn_step_dense_bcast_dev", "attnb_peer_barrier_dev",
     "attnb_attn_block_dense", "attnb_attn_block_dense_dev",
     "attnb_attn_block_dense_batched_dev",
     "attnb_mha_block_dense", "attnb_mha_block_dense_dev",
@@ -78,9 +81,19 @@ def lib() -> ctypes.CDLL:
         L.attnb_sgemm_dev.argtypes = [vp, i, vp, i, vp, i, i, i, i, f, f, i, vp]
         L.attnb_linear_dev.argtypes = [vp, i, vp, i, vp, vp, i, i, i, i, i, vp]
         L.attnb_gemm_ex_dev.argtypes = [i, i, vp, i, vp, i, vp, vp, i, i, i, i, f, f, i, vp]
+        L.attnb_gemm_ex_bcast_dev.argtypes = [i, i, vp, i, vp, i, vp, vp, i,
+                                              ctypes.POINTER(vp), i, i, i, i, f, f, i, vp]
+        L.attnb_ipc_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
+        L.attnb_ipc_free.argtypes = [vp]
+        L.attnb_ipc_export.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint64)]
+        L.attnb_ipc_import.argtypes = [vp, ctypes.c_uint64, ctypes.POINTER(vp)]
+        L.attnb_ipc_close.argtypes = [vp]
         L.attnb_attn_step_dense.argtypes = [T, T, T, T]
         L.attnb_attn_step_dense_dev.argtypes = [T, T, T, T, vp]
         L.attnb_attn_step_dense_noalloc.argtypes = [T, T, T, T, vp]
+        L.attnb_attn_step_dense_bcast_dev.argtypes = [T, T, T, T, ctypes.POINTER(vp), i, vp]
+        L.attnb_peer_barrier_dev.argtypes = [vp, ctypes.POINTER(vp), i, i, ctypes.c_uint64, i,
+                                             vp]
         L.attnb_attn_block_dense.argtypes = [T, T, T, T, i, i]
         L.attnb_attn_block_dense_dev.argtypes = [T, T, T, T, i, i, vp]
         L.attnb_attn_block_dense_batched_dev.argtypes = [T, T, T, T, i, i64, i64, i64, i64, i, i,
@@ -151,6 +164,82 @@ def gemm_ex_dev(A, B, C, trans_a=False, trans_b=False, bias=None, alpha=1.0, bet
                                   _stream(stream)))
 
 
+def gemm_ex_bcast_dev(A, B, C, replicas, trans_a=False, trans_b=False, bias=None, alpha=1.0,
+                      beta=0.0, precision=None, stream=None) -> None:
+    """gemm_ex_dev that also writes C, element for element, into each address
+    in `replicas` (device addresses as ints, same layout and leading dimension
+    as C -- e.g. C's rows in the other GPUs' replicas, from ipc_import)."""
+    M = A.shape[1] if trans_a else A.shape[0]
+    K = A.shape[0] if trans_a else A.shape[1]
+    N = B.shape[0] if trans_b else B.shape[1]
+    if (B.shape[1] if trans_b else B.shape[0]) != K or tuple(C.shape) != (M, N):
+        raise ValueError("gemm_ex_bcast_dev: shapes do not match")
+    if A.stride(1) != 1 or B.stride(1) != 1 or C.stride(1) != 1:
+        raise ValueError("gemm_ex_bcast_dev: operands need a unit column stride")
+    arr = (ctypes.c_void_p * max(1, len(replicas)))(*[int(r) for r in replicas])
+    check(lib().attnb_gemm_ex_bcast_dev(int(trans_a), int(trans_b), A.data_ptr(), A.stride(0),
+                                        B.data_ptr(), B.stride(0),
+                                        bias.data_ptr() if bias is not None else None,
+                                        C.data_ptr(), C.stride(0), arr, len(replicas), M, N, K,
+                                        alpha, beta, PREC[precision], _stream(stream)))
+
+
+IPC_HANDLE_BYTES = 64
+
+
+class _SharedBlock:
+    """A device allocation of its own (attnb_ipc_alloc), exposed through the
+    CUDA array interface so torch can view it; freed when the last view dies."""
+
+    def __init__(self, shape: tuple):
+        n = 1
+        for d in shape:
+            n *= int(d)
+        p = ctypes.c_void_p()
+        check(lib().attnb_ipc_alloc(max(4, 4 * n), ctypes.byref(p)))
+        self.ptr = p.value
+        self.__cuda_array_interface__ = {"shape": tuple(int(d) for d in shape), "typestr": "<f4",
+                                         "data": (self.ptr, False), "version": 3,
+                                         "strides": None}
+
+    def __del__(self):
+        try:
+            lib().attnb_ipc_free(self.ptr)
+        except Exception:  # interpreter shutdown: the library may be gone
+            pass
+
+
+def shared_empty(shape: tuple):
+    """An uninitialised float32 CUDA tensor on the current device in an
+    allocation of its own, exportable with ipc_export."""
+    import torch
+
+    return torch.as_tensor(_SharedBlock(tuple(shape)), device="cuda")
+
+
+def ipc_export(t) -> tuple[bytes, int]:
+    """(handle, byte offset) of the device allocation holding CUDA tensor `t`,
+    for ipc_import in another process of the node."""
+    h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    off = ctypes.c_uint64()
+    check(lib().attnb_ipc_export(t.data_ptr(), h, ctypes.byref(off)))
+    return h.raw, off.value
+
+
+def ipc_import(handle: bytes, offset: int) -> int:
+    """Device address, in the current device's context, of another process's
+    allocation (see ipc_export); release with ipc_close."""
+    if len(handle) != IPC_HANDLE_BYTES:
+        raise ValueError("ipc handle must be 64 bytes")
+    p = ctypes.c_void_p()
+    check(lib().attnb_ipc_import(handle, offset, ctypes.byref(p)))
+    return p.value
+
+
+def ipc_close(ptr: int) -> None:
+    check(lib().attnb_ipc_close(ptr))
+
+
 def linear_dev(x, W, b, y, precision=None, stream=None) -> None:
     """y = x @ W^T + b (b may be None)."""
     T_, K = x.shape
@@ -164,6 +253,26 @@ def attn_step_dense_dev(Q, K, V, O, stream=None) -> None:
     q, k, v, o = tensor3(Q, True), tensor3(K), tensor3(V), tensor3(O, True)
     check(lib().attnb_attn_step_dense_dev(ctypes.byref(q), ctypes.byref(k), ctypes.byref(v),
                                           ctypes.byref(o), _stream(stream)))
+
+
+def attn_step_dense_bcast_dev(Q, K, V, O, replicas, stream=None) -> None:
+    """attn_step_dense_dev that also stores O into each address in `replicas`
+    (device addresses as ints: O's heads in other GPUs' copies)."""
+    q, k, v, o = tensor3(Q, True), tensor3(K), tensor3(V), tensor3(O, True)
+    arr = (ctypes.c_void_p * max(1, len(replicas)))(*[int(r) for r in replicas])
+    check(lib().attnb_attn_step_dense_bcast_dev(ctypes.byref(q), ctypes.byref(k),
+                                                ctypes.byref(v), ctypes.byref(o), arr,
+                                                len(replicas), _stream(stream)))
+
+
+def peer_barrier_dev(flags: int, peer_flags: list, rank: int, epoch: int, limit_us: int = 0,
+                     stream=None) -> None:
+    """Enqueue the peer-memory barrier (attnb_peer_barrier_dev): `flags` is
+    this rank's epoch array, peer_flags[r] rank r's array as mapped here (any
+    value at index `rank`)."""
+    n = len(peer_flags)
+    arr = (ctypes.c_void_p * n)(*[int(p) if p else None for p in peer_flags])
+    check(lib().attnb_peer_barrier_dev(flags, arr, n, rank, epoch, limit_us, _stream(stream)))
 
 
 def attn_step_dense_noalloc(Q, K, V, O, stream=None) -> None:

@@ -18,13 +18,16 @@ here follow the work's natural independence:
   ctx_r^T: stacked in rank order they are ctx^T [D, tokens_s] for its block
   (1/p of the context per rank, where an all-gather would move all of it).
   Rank s then computes its rows y = ctx W_out^T + b_out from ctx^T read
-  transposed (the single-GPU product, same summation order), and an
-  all-gather of the row blocks assembles y;
+  transposed (the single-GPU product, same summation order); on NVLink the
+  out-projection kernel itself stores those rows into every rank's y
+  (peer memory mapped with CUDA IPC), elsewhere an all-gather of the row
+  blocks assembles y;
 * SGEMM (gemm::sgemm_blocked, src/gemm.cpp:319-415): rank r computes a block
   of C -- a block of rows (A row block x all of B; the all-gather is then
   contiguous) or, as `shard="cols"`, a block of columns (all of A x a column
   block of B, read in place through its leading dimension) followed by an
-  all-gather and a permute.
+  all-gather and a permute.  ShardedGemm is the row form without a gather:
+  the GEMM kernel stores its tiles into every rank's C over NVLink.
 
 Local compute goes through an `ops` object whose default calls the B200
 kernels in libattnb (attn_cpu.capi); tests substitute a CPU implementation to
@@ -100,9 +103,18 @@ class DeviceOps:
     def decode(self, q, k, v, o):
         self.capi.attn_step_dense_dev(q, k, v, o)
 
+    def decode_bcast(self, q, k, v, o, replicas):
+        self.capi.attn_step_dense_bcast_dev(q, k, v, o, replicas)
+
     def gemm_ex(self, A, B, C, trans_a, trans_b, bias):
         self.capi.gemm_ex_dev(A, B, C, trans_a=trans_a, trans_b=trans_b, bias=bias,
                               precision=self.precision)
+
+    def gemm_ex_bcast(self, A, B, C, replicas, trans_a, trans_b, bias):
+        """gemm_ex whose kernel also stores C into the replicas (device
+        addresses on other GPUs) as its tiles finish."""
+        self.capi.gemm_ex_bcast_dev(A, B, C, replicas, trans_a=trans_a, trans_b=trans_b,
+                                    bias=bias, precision=self.precision)
 
 
 def _world(group):
@@ -155,6 +167,136 @@ def _all_to_all_cols(local: torch.Tensor, row_counts: list[int], group) -> torch
     return recv.view(sum(row_counts), w_me)
 
 
+def _peer_capable(ops, group) -> bool:
+    """Whether outputs can be broadcast by the kernels' own stores into the
+    other GPUs' memory: the B200 ops and an NCCL group of more than one rank."""
+    if not hasattr(ops, "gemm_ex_bcast"):
+        return False
+    rank, world = _world(group)
+    return world > 1 and dist.get_backend(group) == "nccl"
+
+
+def _fence(group, device) -> None:
+    """A collective on the current stream (an all-reduce of one word): when it
+    completes on a rank, every rank has finished the work it enqueued before
+    it, including kernels that stored into this rank's memory."""
+    t = torch.zeros(1, dtype=torch.int32, device=device)
+    dist.all_reduce(t, group=group)
+
+
+class PeerReplicas:
+    """A float32 buffer of `shape` on every rank of `group`, in a device
+    allocation of its own, with the other ranks' buffers mapped into this
+    process (CUDA IPC over NVLink / NVSwitch): a kernel on this GPU stores into
+    every rank's copy directly.  Collective: every rank constructs it with the
+    same shape, and close() is collective too."""
+
+    def __init__(self, shape, group=None, zero: bool = False):
+        from . import capi
+
+        self.capi = capi
+        self.group = group
+        self.rank, self.world = _world(group)
+        self.local = capi.shared_empty(tuple(shape))
+        if zero:  # ordered before any rank's first store by the gather below
+            self.local.zero_()
+        mine = capi.ipc_export(self.local)
+        entries = [None] * self.world
+        dist.all_gather_object(entries, mine, group=group)
+        self.peers = []  # (rank, base address of that rank's copy), rank order
+        try:
+            for r, (h, off) in enumerate(entries):
+                if r != self.rank:
+                    self.peers.append((r, capi.ipc_import(h, off)))
+        except Exception:
+            for _, p in self.peers:
+                capi.ipc_close(p)
+            raise
+
+    def replicas(self, byte_offset: int) -> list[int]:
+        """Addresses `byte_offset` bytes into every other rank's copy."""
+        return [p + byte_offset for _, p in self.peers]
+
+    def close(self) -> None:
+        """Collective: waits until no rank writes any more, then unmaps."""
+        if self.peers is None:
+            return
+        _fence(self.group, self.local.device)
+        torch.cuda.current_stream().synchronize()
+        for _, p in self.peers:
+            self.capi.ipc_close(p)
+        self.peers = None
+
+
+class PeerGroup:
+    """Cross-GPU barrier over peer memory for the ranks of `group`
+    (attnb_peer_barrier_dev): one small kernel per barrier, a few microseconds,
+    where a collective of the communication library costs tens.  Every rank
+    calls barrier() at the same points of its stream; work enqueued after a
+    barrier on any rank sees every store that any rank enqueued before it
+    (including kernel stores into other ranks' memory).  Waits are bounded: a
+    rank that never arrives shows as ATTNB_ERR_DEVICE_TIMEOUT on the others
+    (capi.stream_status).  Collective construction and close()."""
+
+    def __init__(self, group=None):
+        from . import capi
+
+        self.capi = capi
+        self.rank, self.world = _world(group)
+        # one uint64 epoch per rank (two float32 words each), zeroed
+        self.flags = PeerReplicas((2 * self.world,), group, zero=True)
+        ptrs = [0] * self.world
+        for r, p in self.flags.peers:
+            ptrs[r] = p
+        ptrs[self.rank] = self.flags.local.data_ptr()  # own slot: not read
+        self._ptrs = ptrs
+        self.epoch = 0
+
+    def barrier(self, limit_us: int = 0) -> None:
+        self.epoch += 1
+        self.capi.peer_barrier_dev(self.flags.local.data_ptr(), self._ptrs, self.rank,
+                                   self.epoch, limit_us)
+
+    def close(self) -> None:
+        self.flags.close()
+
+
+class ShardedGemm:
+    """C = A @ B [M, N] with C's rows partitioned across the ranks of `group`
+    and no separate gather: rank r's GEMM kernel stores each finished tile of
+    its rows [m0, m1) into C on every rank, over NVLink, while its other tiles
+    are still being multiplied (attnb_gemm_ex_bcast_dev).  A and B are the
+    same on every rank.  forward() returns this object's C buffer, which the
+    next forward overwrites; it is complete on every rank when forward
+    returns (stream order).  The summation order of every element is that of
+    the single-GPU SGEMM (gemm::sgemm_blocked, src/gemm.cpp:319-415)."""
+
+    def __init__(self, M: int, N: int, group=None, ops=None):
+        self.ops = ops if ops is not None else DeviceOps()
+        self.group = group
+        self.M, self.N = M, N
+        self.rank, self.world = _world(group)
+        self.m0, self.m1 = shard_range(M, self.rank, self.world)
+        self.C = PeerReplicas((M, N), group)
+        self.sync = PeerGroup(group)
+
+    def forward(self, A: torch.Tensor, B: torch.Tensor) -> torch.Tensor:
+        if A.shape[0] != self.M or B.shape[1] != self.N or A.shape[1] != B.shape[0]:
+            raise ValueError("ShardedGemm: A must be [M, K] and B [K, N]")
+        C = self.C.local
+        # No rank may still be reading the previous result when the stores start.
+        self.sync.barrier()
+        if self.m1 > self.m0:
+            self.ops.gemm_ex_bcast(A[self.m0:self.m1], B, C[self.m0:self.m1],
+                                   self.C.replicas(self.m0 * self.N * 4), False, False, None)
+        self.sync.barrier()  # every rank's rows have landed
+        return C
+
+    def close(self) -> None:
+        self.C.close()
+        self.sync.close()
+
+
 @dataclass
 class _HeadShard:
     h0: int
@@ -172,7 +314,7 @@ class ShardedMHA:
     """
 
     def __init__(self, W_in, b_in, W_out, b_out, num_heads: int, causal: bool = False,
-                 group=None, ops=None):
+                 group=None, ops=None, peer_output=None):
         D = W_in.shape[1]
         if W_in.shape != (3 * D, D) or W_out.shape != (D, D):
             raise ValueError("W_in must be [3D, D] and W_out [D, D]")
@@ -194,6 +336,14 @@ class ShardedMHA:
         self.b_out = b_out.contiguous()
         self.head_counts = [shard_range(num_heads, r, world)[1] - shard_range(num_heads, r, world)[0]
                             for r in range(world)]
+        # Peer output: the out-projection kernel stores y's rows into every
+        # rank's y (PeerReplicas per input shape) instead of an all-gather.
+        can = _peer_capable(self.ops, group)
+        if peer_output and not can:
+            raise ValueError("peer_output needs the B200 ops on an NCCL group of >1 rank")
+        self.peer_output = can if peer_output is None else bool(peer_output)
+        self._y = {}  # (B, T) -> PeerReplicas
+        self._sync = PeerGroup(group) if self.peer_output else None
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         squeeze = x.dim() == 2
@@ -224,6 +374,20 @@ class ShardedMHA:
         # 4) this rank's rows of y = ctx W_out^T + b_out, reading ctx^T
         #    transposed, then an all-gather of the row blocks
         r0, r1 = shard_range(rows, self.rank, self.world)
+        if self.peer_output:
+            # The kernel stores y's rows [r0, r1) into every rank's y.  The
+            # all-to-all above already ordered these stores after every rank's
+            # earlier work (no rank still reads the previous y); the fence
+            # after them orders every reader after all ranks' rows.
+            yb = self._y.get((B, T))
+            if yb is None:
+                yb = self._y[(B, T)] = PeerReplicas((rows, D), self.group)
+            if r1 > r0:
+                self.ops.gemm_ex_bcast(ctxT_mine, self.W_out, yb.local[r0:r1],
+                                       yb.replicas(r0 * D * 4), True, True, self.b_out)
+            self._sync.barrier()
+            y = yb.local.view(B, T, D)
+            return y[0] if squeeze else y
         y_rows = torch.empty(r1 - r0, D, dtype=x.dtype, device=x.device)
         if r1 > r0:
             self.ops.gemm_ex(ctxT_mine, self.W_out, y_rows, True, True, self.b_out)
@@ -231,6 +395,15 @@ class ShardedMHA:
                   for r in range(self.world)]
         y = _all_gather_rows(y_rows, counts, self.group).view(B, T, D)
         return y[0] if squeeze else y
+
+    def close(self) -> None:
+        """Collective: releases the peer output buffers."""
+        for yb in self._y.values():
+            yb.close()
+        self._y = {}
+        if self._sync is not None:
+            self._sync.close()
+            self._sync = None
 
 
 def gemm_sharded(A: torch.Tensor, B: torch.Tensor, group=None, ops=None,
@@ -293,3 +466,42 @@ def attn_step_sharded(Q, K, V, group=None, ops=None) -> torch.Tensor:
         ops.decode(Q[h0:h1], K[h0:h1], V[h0:h1], Ol)
     counts = [shard_range(H, r, world)[1] - shard_range(H, r, world)[0] for r in range(world)]
     return _all_gather_rows(Ol, counts, group)
+
+
+class ShardedDecode:
+    """The decode step (attn::attn_step_dense, src/attn_dense.cpp:21-73) with
+    heads partitioned across the ranks of `group` and no separate gather:
+    rank r's kernels read only its heads [h0, h1) of K and V and store their
+    output heads into O on every rank over NVLink
+    (attnb_attn_step_dense_bcast_dev), then one peer-memory barrier
+    (PeerGroup) orders every reader after all ranks' heads.  O is double
+    buffered, so one barrier per step suffices: step() returns an [H, Dh]
+    buffer that stays valid until the step after next.  Q [H, Dh] and K / V
+    [H, T, Dh] (batch and heads flattened into H; any strides) are the same
+    views on every rank."""
+
+    def __init__(self, H: int, Dh: int, group=None, ops=None):
+        self.ops = ops if ops is not None else DeviceOps()
+        self.H, self.Dh = H, Dh
+        self.rank, self.world = _world(group)
+        self.h0, self.h1 = shard_range(H, self.rank, self.world)
+        self.O = [PeerReplicas((H, Dh), group) for _ in range(2)]
+        self.sync = PeerGroup(group)
+        self.n = 0
+
+    def step(self, Q, K, V) -> torch.Tensor:
+        if Q.shape != (self.H, self.Dh) or K.shape[0] != self.H or V.shape[0] != self.H:
+            raise ValueError("ShardedDecode: Q must be [H, Dh] and K, V [H, T, Dh]")
+        ob = self.O[self.n & 1]
+        self.n += 1
+        h0, h1 = self.h0, self.h1
+        if h1 > h0:
+            self.ops.decode_bcast(Q[h0:h1], K[h0:h1], V[h0:h1], ob.local[h0:h1],
+                                  ob.replicas(h0 * self.Dh * 4))
+        self.sync.barrier()
+        return ob.local
+
+    def close(self) -> None:
+        for ob in self.O:
+            ob.close()
+        self.sync.close()

@@ -150,7 +150,7 @@ void finish_host_call(DeviceCtx& c) {
 // ------------------------------------------------------------------ decode
 void step_dev(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* V,
               const attnb_mtensor* O, DeviceCtx& c, cudaStream_t s, void* scratch_override,
-              size_t scratch_bytes) {
+              size_t scratch_bytes, const PeerOut* peers = nullptr) {
   const View3 q = view(Q, 1), k = view(K, K->T), v = view(V, V->T);
   const MView3 o = mview(O, 1);
   const DecodePlan p = decode_plan(q, k, v, c.num_sms);
@@ -158,7 +158,7 @@ void step_dev(const attnb_tensor* Q, const attnb_tensor* K, const attnb_tensor* 
   void* ws = scratch_override;
   if (!ws) ws = dev_scratch(c, need, s);
   else if (need > scratch_bytes) fail(ATTNB_ERR_RUNTIME, "scratch too small");
-  decode_launch(p, q, k, v, o, ws, s);
+  decode_launch(p, q, k, v, o, ws, s, peers);
   ATTNB_CUDA(cudaGetLastError());
 }
 
@@ -477,6 +477,163 @@ int attnb_gemm_ex_dev(int trans_a, int trans_b, const float* A, int lda, const f
   });
 }
 
+int attnb_gemm_ex_bcast_dev(int trans_a, int trans_b, const float* A, int lda, const float* B,
+                            int ldb, const float* bias, float* C, int ldc,
+                            float* const* replicas, int nreplicas, int M, int N, int K,
+                            float alpha, float beta, int precision, void* stream) {
+  return guarded(__func__, [&] {
+    if (nreplicas < 0 || nreplicas > kMaxPeerOut)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "nreplicas must be in [0, 7]");
+    if (nreplicas > 0 && !replicas) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null replica list");
+    PeerOut po{};
+    po.n = nreplicas;
+    for (int i = 0; i < nreplicas; ++i) {
+      if (!replicas[i]) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null replica pointer");
+      // One vector-width decision serves C and every replica.
+      if (((reinterpret_cast<uintptr_t>(replicas[i]) ^ reinterpret_cast<uintptr_t>(C)) & 15u) != 0)
+        fail(ATTNB_ERR_INVALID_ARGUMENT, "replicas must have C's alignment modulo 16 bytes");
+      po.dst[i] = replicas[i];
+    }
+    if (K < 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "K must be non-negative");
+    if (M <= 0 || N <= 0) return;
+    if (!C) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    if (ldc < N) fail(ATTNB_ERR_INVALID_ARGUMENT, "leading dimension smaller than the row length");
+    DeviceCtx& c = current_ctx();
+    cudaStream_t s = as_stream(stream);
+    if (K == 0) {
+      gemm_scale_bias(C, ldc, M, N, beta, bias, c.num_sms, s);
+      for (int i = 0; i < nreplicas; ++i)
+        ATTNB_CUDA(cudaMemcpy2DAsync(po.dst[i], (size_t)ldc * sizeof(float), C,
+                                     (size_t)ldc * sizeof(float), (size_t)N * sizeof(float), M,
+                                     cudaMemcpyDeviceToDevice, s));
+      ATTNB_CUDA(cudaGetLastError());
+      return;
+    }
+    if (!A || !B) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    if ((trans_a != 0 && trans_a != 1) || (trans_b != 0 && trans_b != 1))
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "trans_a and trans_b must be 0 or 1");
+    if (lda < (trans_a ? M : K) || ldb < (trans_b ? K : N))
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "leading dimension smaller than the row length");
+    const int prec = resolve_precision(precision);
+    const GemmPlan p = gemm_plan(M, N, K, prec);
+    void* ws = dev_scratch(c, p.ws_bytes, s);
+    gemm_run(p, A, lda, trans_a == 0, B, ldb, trans_b == 1, C, ldc, alpha, beta, bias, ws,
+             c.status, c.num_sms, s, &po);
+    ATTNB_CUDA(cudaGetLastError());
+  });
+}
+
+// ------------------------------------------------------------ peer memory
+namespace {
+// Device memory of other processes opened in this one.  A handle can be
+// opened once per context, so openings are shared and counted.
+struct IpcOpening {
+  std::string key;  // the handle's bytes
+  int device;
+  void* base;
+  int refs;
+};
+std::mutex g_ipc_mu;
+std::vector<IpcOpening> g_ipc;
+
+using GetAddressRangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+GetAddressRangeFn address_range_fn() {
+  static GetAddressRangeFn fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPointByVersion("cuMemGetAddressRange", &p, 12000, cudaEnableDefault,
+                                         &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      return (GetAddressRangeFn) nullptr;
+    return reinterpret_cast<GetAddressRangeFn>(p);
+  }();
+  if (!fn) fail(ATTNB_ERR_CUDA, "cuMemGetAddressRange is unavailable from the driver");
+  return fn;
+}
+}  // namespace
+
+int attnb_ipc_alloc(size_t bytes, void** dptr) {
+  return guarded(__func__, [&] {
+    if (!dptr || bytes == 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "need a size and an output pointer");
+    *dptr = nullptr;
+    const cudaError_t e = cudaMalloc(dptr, bytes);
+    if (e == cudaErrorMemoryAllocation) {
+      cudaGetLastError();
+      fail(ATTNB_ERR_OUT_OF_MEMORY, "cudaMalloc of a shared buffer failed");
+    }
+    ATTNB_CUDA(e);
+  });
+}
+
+int attnb_ipc_free(void* dptr) {
+  return guarded(__func__, [&] {
+    if (dptr) ATTNB_CUDA(cudaFree(dptr));
+  });
+}
+
+int attnb_ipc_export(const void* dptr, void* handle, uint64_t* offset) {
+  return guarded(__func__, [&] {
+    if (!dptr || !handle || !offset) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null pointer");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    const CUresult r = address_range_fn()(&base, &size, reinterpret_cast<CUdeviceptr>(dptr));
+    if (r != CUDA_SUCCESS)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "not a device allocation of this process");
+    cudaIpcMemHandle_t h;
+    ATTNB_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+    std::memcpy(handle, &h, sizeof(h));
+    *offset = reinterpret_cast<uintptr_t>(dptr) - (uintptr_t)base;
+  });
+}
+
+int attnb_ipc_import(const void* handle, uint64_t offset, void** dptr) {
+  return guarded(__func__, [&] {
+    if (!handle || !dptr) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null pointer");
+    int dev = 0;
+    ATTNB_CUDA(cudaGetDevice(&dev));
+    std::string key(static_cast<const char*>(handle), sizeof(cudaIpcMemHandle_t));
+    std::lock_guard<std::mutex> lk(g_ipc_mu);
+    for (auto& o : g_ipc)
+      if (o.key == key && o.device == dev) {
+        ++o.refs;
+        *dptr = static_cast<char*>(o.base) + offset;
+        return;
+      }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle, sizeof(h));
+    void* base = nullptr;
+    ATTNB_CUDA(cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess));
+    g_ipc.push_back({key, dev, base, 1});
+    *dptr = static_cast<char*>(base) + offset;
+  });
+}
+
+int attnb_ipc_close(void* dptr) {
+  return guarded(__func__, [&] {
+    if (!dptr) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null pointer");
+    std::lock_guard<std::mutex> lk(g_ipc_mu);
+    int dev = 0;
+    ATTNB_CUDA(cudaGetDevice(&dev));
+    for (size_t i = 0; i < g_ipc.size(); ++i) {
+      IpcOpening& o = g_ipc[i];
+      if (o.device != dev) continue;
+      CUdeviceptr base = 0;
+      size_t size = 0;
+      if (address_range_fn()(&base, &size, reinterpret_cast<CUdeviceptr>(o.base)) !=
+          CUDA_SUCCESS)
+        continue;
+      const uintptr_t p = reinterpret_cast<uintptr_t>(dptr);
+      if (p < (uintptr_t)base || p >= (uintptr_t)base + size) continue;
+      if (--o.refs == 0) {
+        ATTNB_CUDA(cudaIpcCloseMemHandle(o.base));
+        g_ipc.erase(g_ipc.begin() + (std::ptrdiff_t)i);
+      }
+      return;
+    }
+    fail(ATTNB_ERR_INVALID_ARGUMENT, "pointer was not opened by attnb_ipc_import");
+  });
+}
+
 int attnb_linear_dev(const float* x, int ldx, const float* W, int ldw, const float* b, float* y,
                      int ldy, int T, int N, int K, int precision, void* stream) {
   return guarded(__func__, [&] {
@@ -543,6 +700,55 @@ int attnb_attn_step_dense_dev(const attnb_tensor* Q, const attnb_tensor* K, cons
     validate_step(Q, K, V, O);
     DeviceCtx& c = current_ctx();
     step_dev(Q, K, V, O, c, as_stream(stream), nullptr, 0);
+  });
+}
+
+int attnb_attn_step_dense_bcast_dev(const attnb_tensor* Q, const attnb_tensor* K,
+                                    const attnb_tensor* V, attnb_mtensor* O,
+                                    float* const* replicas, int nreplicas, void* stream) {
+  return guarded(__func__, [&] {
+    validate_step(Q, K, V, O);
+    if (nreplicas < 0 || nreplicas > kMaxPeerOut)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "nreplicas must be in [0, 7]");
+    if (nreplicas > 0 && !replicas) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null replica list");
+    if (nreplicas > 0 && O->strideDh != 1)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "replicated O needs a unit head-dim stride");
+    PeerOut po{};
+    po.n = nreplicas;
+    for (int i = 0; i < nreplicas; ++i) {
+      if (!replicas[i]) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null replica pointer");
+      po.dst[i] = replicas[i];
+    }
+    DeviceCtx& c = current_ctx();
+    step_dev(Q, K, V, O, c, as_stream(stream), nullptr, 0, &po);
+  });
+}
+
+int attnb_peer_barrier_dev(uint64_t* flags, uint64_t* const* peer_flags, int nranks, int rank,
+                           uint64_t epoch, int limit_us, void* stream) {
+  return guarded(__func__, [&] {
+    if (nranks < 1 || nranks > kMaxRanks)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "nranks must be in [1, 8]");
+    if (rank < 0 || rank >= nranks) fail(ATTNB_ERR_INVALID_ARGUMENT, "rank out of range");
+    if (!flags || (nranks > 1 && !peer_flags)) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null pointer");
+    if (epoch == 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "epochs start at 1");
+    if (limit_us < 0 || limit_us > 10000000)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "limit_us must be in [0, 1e7] (0: the default 2 s)");
+    PeerFlags f{};
+    f.local = flags;
+    f.n = nranks;
+    f.rank = rank;
+    for (int r = 0; r < nranks; ++r) {
+      if (r == rank) continue;
+      if (!peer_flags[r]) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null peer flag array");
+      f.peer[r] = peer_flags[r];
+    }
+    if (nranks == 1) return;
+    DeviceCtx& c = current_ctx();
+    // Default: the 2 s limit of the kernels' other bounded waits.
+    const uint64_t limit_ns = limit_us ? (uint64_t)limit_us * 1000ull : 2000000000ull;
+    peer_barrier(f, epoch, limit_ns, c.status, as_stream(stream));
+    ATTNB_CUDA(cudaGetLastError());
   });
 }
 

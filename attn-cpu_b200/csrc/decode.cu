@@ -228,7 +228,8 @@ __global__ void __launch_bounds__(kThreads) decode_generic_kernel(
 // Merge the nsplit partials of each head.
 __global__ void decode_merge_kernel(const float* __restrict__ part_o,
                                     const float2* __restrict__ part_ml, int nsplit, int Dh,
-                                    float* __restrict__ O, int64_t osH, int64_t osD) {
+                                    float* __restrict__ O, int64_t osH, int64_t osD,
+                                    const PeerOut peers) {
   const int h = blockIdx.x;
   const float2* ml = part_ml + (size_t)h * nsplit;
   float M = -INFINITY;
@@ -240,8 +241,14 @@ __global__ void decode_merge_kernel(const float* __restrict__ part_o,
     float o = 0.f;
     for (int s = 0; s < nsplit; ++s)
       o += fast_exp2(ml[s].x - M) * part_o[((size_t)h * nsplit + s) * Dh + d];
-    O[h * osH + d * osD] = o * invL;
+    const int64_t off = h * osH + d * osD;
+    O[off] = o * invL;
+    // Replicas on other GPUs (the sharded decode step's output heads).
+#pragma unroll
+    for (int p = 0; p < kMaxPeerOut; ++p)
+      if (p < peers.n) peers.dst[p][off] = o * invL;
   }
+  if (peers.n > 0) __threadfence_system();
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -276,7 +283,7 @@ size_t decode_workspace_bytes(const DecodePlan& p, int H, int Dh) {
 }
 
 void decode_launch(const DecodePlan& p, const View3& Q, const View3& K, const View3& V,
-                   const MView3& O, void* ws, cudaStream_t stream) {
+                   const MView3& O, void* ws, cudaStream_t stream, const PeerOut* peers) {
   const int H = K.H, T = K.T, Dh = K.Dh;
   const float qscale = kLog2e / std::sqrt(static_cast<float>(Dh));
   float* part_o = nullptr;
@@ -304,8 +311,18 @@ void decode_launch(const DecodePlan& p, const View3& Q, const View3& K, const Vi
         Q.data, Q.sH, Q.sD, K.data, K.sH, K.sT, K.sD, V.data, V.sH, V.sT, V.sD, T, Dh,
         p.keys_per_split, qscale, O.data, O.sH, O.sD, part_o, part_ml);
   }
-  if (p.nsplit > 1)
-    decode_merge_kernel<<<H, 128, 0, stream>>>(part_o, part_ml, p.nsplit, Dh, O.data, O.sH, O.sD);
+  const PeerOut none{};
+  if (p.nsplit > 1) {
+    decode_merge_kernel<<<H, 128, 0, stream>>>(part_o, part_ml, p.nsplit, Dh, O.data, O.sH, O.sD,
+                                               peers ? *peers : none);
+  } else if (peers) {
+    // One key range per head: the attention kernel stored O itself; copy the
+    // rows (unit head-dim stride, checked by the caller) to the replicas.
+    for (int i = 0; i < peers->n; ++i)
+      ATTNB_CUDA(cudaMemcpy2DAsync(peers->dst[i], O.sH * sizeof(float), O.data,
+                                   O.sH * sizeof(float), Dh * sizeof(float), H,
+                                   cudaMemcpyDeviceToDevice, stream));
+  }
 }
 
 }  // namespace attnb

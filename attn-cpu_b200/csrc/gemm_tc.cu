@@ -27,6 +27,7 @@
 // round-to-nearest fp32 sums carry the long-K accumulation.
 #include <algorithm>
 #include <atomic>
+#include <type_traits>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -47,6 +48,11 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = (SPLIT3 ? 2 : 1) * (A_BYTES + B_BYTES);
   static constexpr int STAGES = (200 * 1024) / STAGE_BYTES;
   static constexpr int SMEM = STAGES * STAGE_BYTES + 1024;    // + alignment slack
+  // Peer-output form: each epilogue warp turns its 32 rows x 32 columns
+  // around in shared memory (rows padded to 36 floats) before storing them.
+  static constexpr int XPOSE_ROW = 36;
+  static constexpr int XPOSE_BYTES = 4 * 32 * XPOSE_ROW * 4;
+  static constexpr int SMEM_BCAST = SMEM + XPOSE_BYTES;
   // Two accumulator slots; in 3xTF32 mode each slot holds a "big" (hi*hi)
   // and a "small" (hi*lo + lo*hi) accumulator.
   static constexpr int SLOT_COLS = (SPLIT3 ? 2 : 1) * BN;
@@ -110,14 +116,76 @@ __device__ __forceinline__ void store32(float* crow, int row, int col0, const fl
   }
 }
 
-template <int BN, bool SPLIT3>
+// Peer-output epilogue for 32 consecutive columns of the 32 rows [row0,
+// row0 + 32) that one warp holds (lane = row).  The values are those of
+// store32; they are turned around through the warp's block of shared memory
+// `xp` ([32][XROW] floats) and stored by row segments -- eight lanes write one
+// row's 128 contiguous bytes -- to C and to every replica in `peers`, so each
+// store instruction moves four whole 128-byte lines (whole NVLink writes for
+// a replica on another GPU).
+template <int XROW>
+__device__ __forceinline__ void store32_bcast(float* __restrict__ C, int64_t ldc, int row0,
+                                              int lane, int col0, const float* acc, int M, int N,
+                                              float alpha, float beta,
+                                              const float* __restrict__ bias, bool c_vec,
+                                              float* xp, const PeerOut& peers) {
+  const int row = row0 + lane;
+  float v[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) v[j] = alpha * acc[j];
+  if (beta != 0.f && row < M) {
+    const float* crow = C + (int64_t)row * ldc;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < N) v[j] = fmaf(beta, crow[col0 + j], v[j]);
+  }
+  if (bias) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (col0 + j < N) v[j] += __ldg(bias + col0 + j);
+  }
+  __syncwarp();  // the previous chunk's reads of xp are done
+  float* mine = xp + lane * XROW;
+#pragma unroll
+  for (int j = 0; j < 32; j += 4)
+    *reinterpret_cast<float4*>(mine + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+  __syncwarp();
+  const int c4 = (lane & 7) * 4;
+  const int col = col0 + c4;
+#pragma unroll 2
+  for (int it = 0; it < 8; ++it) {
+    const int r = it * 4 + (lane >> 3);
+    const int grow = row0 + r;
+    if (grow >= M || col >= N) continue;
+    const float4 q = *reinterpret_cast<const float4*>(xp + r * XROW + c4);
+    const int64_t off = (int64_t)grow * ldc + col;
+    if (c_vec && col + 4 <= N) {
+      *reinterpret_cast<float4*>(C + off) = q;
+#pragma unroll
+      for (int p = 0; p < kMaxPeerOut; ++p)
+        if (p < peers.n) *reinterpret_cast<float4*>(peers.dst[p] + off) = q;
+    } else {
+      const float e[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        if (col + k >= N) break;
+        C[off + k] = e[k];
+#pragma unroll
+        for (int p = 0; p < kMaxPeerOut; ++p)
+          if (p < peers.n) peers.dst[p][off + k] = e[k];
+      }
+    }
+  }
+}
+
+template <int BN, bool SPLIT3, bool BCAST = false>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA_hi,
                    const __grid_constant__ CUtensorMap tmA_lo,
                    const __grid_constant__ CUtensorMap tmB_hi,
                    const __grid_constant__ CUtensorMap tmB_lo, int M, int N, int Kp,
                    float* __restrict__ C, int64_t ldc, float alpha, float beta,
-                   const float* __restrict__ bias, int* status) {
+                   const float* __restrict__ bias, int* status, const PeerOut peers) {
   using Cfg = GemmCfg<BN, SPLIT3>;
   constexpr int STAGES = Cfg::STAGES;
   constexpr uint32_t IDESC = idesc_tf32(BM, BN);
@@ -277,6 +345,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int quarter = warp & 3;  // TMEM lanes [32*quarter, 32*quarter + 32)
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
     const bool c_vec = ((ldc & 3) == 0) && ((reinterpret_cast<uintptr_t>(C) & 15u) == 0);
+    // Peer-output form: this warp's transpose block, past the operand ring.
+    float* xp = nullptr;
+    if constexpr (BCAST)
+      xp = reinterpret_cast<float*>(smem_raw + (tiles_base - smem_addr(smem_raw)) +
+                                    STAGES * Cfg::STAGE_BYTES) +
+           quarter * 32 * Cfg::XPOSE_ROW;
     int g = 0;
     bool ok = true;
     for (int tile = blockIdx.x; ok && tile < num_tiles; tile += gridDim.x) {
@@ -311,9 +385,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (lane == 0) mbar_arrive(smem_addr(&tempty_bar[slot]));
         }
         if (!ok) break;
+        if constexpr (BCAST) {
 #pragma unroll
-        for (int j = 0; j < BN / 32; ++j)
-          store32(crow, row, tn * BN + j * 32, &acc[j * 32], M, N, alpha, beta, bias, c_vec);
+          for (int j = 0; j < BN / 32; ++j)
+            store32_bcast<Cfg::XPOSE_ROW>(C, ldc, tm * BM + quarter * 32, lane, tn * BN + j * 32,
+                                          &acc[j * 32], M, N, alpha, beta, bias, c_vec, xp,
+                                          peers);
+        } else {
+#pragma unroll
+          for (int j = 0; j < BN / 32; ++j)
+            store32(crow, row, tn * BN + j * 32, &acc[j * 32], M, N, alpha, beta, bias, c_vec);
+        }
       } else {
         const int slot = g & 1;
         const uint32_t use = (g >> 1) & 1;
@@ -327,7 +409,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           float v[32];
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-          store32(crow, row, tn * BN + j * 32, v, M, N, alpha, beta, bias, c_vec);
+          if constexpr (BCAST)
+            store32_bcast<Cfg::XPOSE_ROW>(C, ldc, tm * BM + quarter * 32, lane, tn * BN + j * 32,
+                                          v, M, N, alpha, beta, bias, c_vec, xp, peers);
+          else
+            store32(crow, row, tn * BN + j * 32, v, M, N, alpha, beta, bias, c_vec);
         }
         tc_fence_before();
         __syncwarp();
@@ -335,6 +421,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++g;
       }
     }
+    // Stores to the replicas are visible system-wide before this CTA retires,
+    // so a collective that follows the kernel orders every reader after them.
+    if constexpr (BCAST) __threadfence_system();
   }
 
   tc_fence_before();
@@ -643,26 +732,27 @@ __global__ void scale_c_kernel(float* C, int64_t ldc, int M, int N, float beta,
   }
 }
 
-template <int BN, bool SPLIT3>
+template <int BN, bool SPLIT3, bool BCAST = false>
 void launch_gemm(const GemmPlan& p, const CUtensorMap& a_hi, const CUtensorMap& a_lo,
                  const CUtensorMap& b_hi, const CUtensorMap& b_lo, float* C, int64_t ldc,
                  float alpha, float beta, const float* bias, int* status, int num_sms,
-                 cudaStream_t s) {
+                 cudaStream_t s, const PeerOut& peers = PeerOut{}) {
   using Cfg = GemmCfg<BN, SPLIT3>;
+  constexpr int smem = BCAST ? Cfg::SMEM_BCAST : Cfg::SMEM;
   static std::atomic<uint64_t> configured{0};  // one bit per device
   int dev = 0;
   ATTNB_CUDA(cudaGetDevice(&dev));
   const uint64_t bit = 1ull << (dev & 63);
   if (!(configured.load() & bit)) {
-    ATTNB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT3>,
-                                    cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM));
+    ATTNB_CUDA(cudaFuncSetAttribute(gemm_tc_kernel<BN, SPLIT3, BCAST>,
+                                    cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     configured.fetch_or(bit);
   }
   const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
   const int grid = std::min(tiles, num_sms);
-  ATTNB_CUDA(launch_pdl(gemm_tc_kernel<BN, SPLIT3>, dim3(grid), dim3(kThreads), Cfg::SMEM, s,
+  ATTNB_CUDA(launch_pdl(gemm_tc_kernel<BN, SPLIT3, BCAST>, dim3(grid), dim3(kThreads), smem, s,
                         a_hi, a_lo, b_hi, b_lo, p.M, p.N, p.Kp, C, ldc, alpha, beta, bias,
-                        status));
+                        status, peers));
 }
 
 // Output tile width: the widest (256 for 1xTF32, 128 for 3xTF32, whose MMAs
@@ -705,10 +795,16 @@ GemmPlan gemm_plan(int M, int N, int K, int precision) {
 
 void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, const float* B,
               int64_t ldb, bool b_kmajor, float* C, int64_t ldc, float alpha, float beta,
-              const float* bias, void* ws, int* status, int num_sms, cudaStream_t s) {
+              const float* bias, void* ws, int* status, int num_sms, cudaStream_t s,
+              const PeerOut* peers) {
   if (p.M <= 0 || p.N <= 0 || p.K <= 0) return;
+  const bool bcast = peers != nullptr && peers->n > 0;
   if (alpha == 0.f && bias == nullptr) {
     if (beta != 1.f) gemm_scale_bias(C, ldc, p.M, p.N, beta, nullptr, num_sms, s);
+    if (bcast)  // no product to fuse with: copy the rows to the replicas
+      for (int i = 0; i < peers->n; ++i)
+        ATTNB_CUDA(cudaMemcpy2DAsync(peers->dst[i], ldc * sizeof(float), C, ldc * sizeof(float),
+                                     p.N * sizeof(float), p.M, cudaMemcpyDeviceToDevice, s));
     return;
   }
   // 1xTF32, one 128x64 tile per CTA, aligned rows: the raw operands go
@@ -720,7 +816,7 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
     auto aligned = [](const float* x, int64_t ld) {
       return (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && ld % 4 == 0;
     };
-    if (!p.split3 && a_kmajor && pick_bn(p.M, p.N, false, num_sms) == 64 &&
+    if (!bcast && !p.split3 && a_kmajor && pick_bn(p.M, p.N, false, num_sms) == 64 &&
         tiles64 <= num_sms && aligned(A, lda) && aligned(B, ldb)) {
       const CUtensorMap ta = make_tmap_2d(A, p.M, p.K, lda, BM, BK);
       const CUtensorMap tb = b_kmajor ? make_tmap_2d(B, p.N, p.K, ldb, 64, BK)
@@ -750,26 +846,34 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
   const CUtensorMap tA_hi = make_tmap_2d(a_hi, p.M, p.Kp, p.Kp, BM, BK);
   const CUtensorMap tB_hi = make_tmap_2d(b_hi, p.N, p.Kp, p.Kp, bn, BK);
   ProfScope prof("gemm_tc", s);
-  if (p.split3) {
-    const CUtensorMap tA_lo = make_tmap_2d(a_lo, p.M, p.Kp, p.Kp, BM, BK);
-    const CUtensorMap tB_lo = make_tmap_2d(b_lo, p.N, p.Kp, p.Kp, bn, BK);
-    if (bn == 128)
-      launch_gemm<128, true>(p, tA_hi, tA_lo, tB_hi, tB_lo, C, ldc, alpha, beta, bias, status,
-                             num_sms, s);
-    else
-      launch_gemm<64, true>(p, tA_hi, tA_lo, tB_hi, tB_lo, C, ldc, alpha, beta, bias, status,
-                            num_sms, s);
-  } else {
-    if (bn == 256)
-      launch_gemm<256, false>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias, status,
-                              num_sms, s);
-    else if (bn == 128)
-      launch_gemm<128, false>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias, status,
-                              num_sms, s);
-    else
-      launch_gemm<64, false>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias, status,
-                             num_sms, s);
-  }
+  const PeerOut none{};
+  const PeerOut& po = bcast ? *peers : none;
+  // The two forms (plain C, or C plus replicas) share the kernel's template.
+  const auto run = [&](auto bcast_tag) {
+    constexpr bool BC = decltype(bcast_tag)::value;
+    if (p.split3) {
+      const CUtensorMap tA_lo = make_tmap_2d(a_lo, p.M, p.Kp, p.Kp, BM, BK);
+      const CUtensorMap tB_lo = make_tmap_2d(b_lo, p.N, p.Kp, p.Kp, bn, BK);
+      if (bn == 128)
+        launch_gemm<128, true, BC>(p, tA_hi, tA_lo, tB_hi, tB_lo, C, ldc, alpha, beta, bias,
+                                   status, num_sms, s, po);
+      else
+        launch_gemm<64, true, BC>(p, tA_hi, tA_lo, tB_hi, tB_lo, C, ldc, alpha, beta, bias,
+                                  status, num_sms, s, po);
+    } else {
+      if (bn == 256)
+        launch_gemm<256, false, BC>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias,
+                                    status, num_sms, s, po);
+      else if (bn == 128)
+        launch_gemm<128, false, BC>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias,
+                                    status, num_sms, s, po);
+      else
+        launch_gemm<64, false, BC>(p, tA_hi, tA_hi, tB_hi, tB_hi, C, ldc, alpha, beta, bias,
+                                   status, num_sms, s, po);
+    }
+  };
+  if (bcast) run(std::true_type{});
+  else run(std::false_type{});
 }
 
 void gemm_scale_bias(float* C, int64_t ldc, int M, int N, float beta, const float* bias,

@@ -22,6 +22,29 @@ struct MView3 {
   int64_t sH, sT, sD;
 };
 
+// ------------------------------------------------------------ peer memory
+// Replicas of an output on other GPUs (peer pointers mapped into this
+// process) that a kernel writes besides the output itself: every element
+// stored to the output is also stored, at the same offset from dst[i] (same
+// strides), to each replica.
+constexpr int kMaxPeerOut = 7;
+struct PeerOut {
+  float* dst[kMaxPeerOut];
+  int n;
+};
+// Flag arrays of a cross-GPU barrier (peer.cu): `local` is this rank's array
+// of n epochs, peer[r] rank r's array as mapped into this process.
+constexpr int kMaxRanks = 8;
+struct PeerFlags {
+  uint64_t* local;
+  uint64_t* peer[kMaxRanks];
+  int n, rank;
+};
+// Enqueues the barrier for `epoch` on s; a wait longer than limit_ns raises
+// the status word.
+void peer_barrier(const PeerFlags& f, uint64_t epoch, uint64_t limit_ns, int* status,
+                  cudaStream_t s);
+
 // ------------------------------------------------------------ decode (K4)
 // Split-KV plan for one decode step: how many key ranges each head is cut
 // into and how long each range is.
@@ -34,8 +57,10 @@ DecodePlan decode_plan(const View3& Q, const View3& K, const View3& V, int num_s
 // Scratch bytes the plan needs (0 when nsplit == 1).
 size_t decode_workspace_bytes(const DecodePlan& p, int H, int Dh);
 // O[h, :] for every head; `ws` holds decode_workspace_bytes(p, ...) bytes.
+// With `peers`, every element of O is also stored into each replica.
 void decode_launch(const DecodePlan& p, const View3& Q, const View3& K, const View3& V,
-                   const MView3& O, void* ws, cudaStream_t stream);
+                   const MView3& O, void* ws, cudaStream_t stream,
+                   const PeerOut* peers = nullptr);
 
 // ------------------------------------------- generic prefill (CUDA cores)
 // O[h,l,:] for any strides and head size; exact fp32 online softmax.
@@ -160,6 +185,7 @@ void gemm_scale_bias(float* C, int64_t ldc, int M, int N, float beta, const floa
 size_t gemm_workspace_bound(int M, int N, int K, int precision);
 void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, const float* B,
               int64_t ldb, bool b_kmajor, float* C, int64_t ldc, float alpha, float beta,
-              const float* bias, void* ws, int* status, int num_sms, cudaStream_t s);
+              const float* bias, void* ws, int* status, int num_sms, cudaStream_t s,
+              const PeerOut* peers = nullptr);
 
 }  // namespace attnb

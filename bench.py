@@ -39,6 +39,11 @@ import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
+# Sharded SGEMM and attention block at N > 1: the GEMM kernels store their
+# output tiles straight into every GPU's copy (peer memory over NVLink)
+# instead of an all-gather after them.  ATTNB_PEER_OUTPUT=0 times the
+# all-gather form.
+PEER_OUTPUT = os.environ.get("ATTNB_PEER_OUTPUT", "1") != "0"
 sys.path.insert(0, os.path.join(ROOT, "attn-cpu_b200"))
 
 # Algorithmic work per call, per workload.
@@ -297,10 +302,16 @@ def setup_sharded(w: str, precision):
         Q = torch.randn(c["H"], c["Dh"], device="cuda", generator=g)
         K = torch.randn(c["H"], c["T"], c["Dh"], device="cuda", generator=g)
         V = torch.randn(c["H"], c["T"], c["Dh"], device="cuda", generator=g)
+        if PEER_OUTPUT:
+            sd = parallel.ShardedDecode(c["H"], c["Dh"], ops=ops)
+            return (lambda: sd.step(Q, K, V)), sd.close
         return lambda: parallel.attn_step_sharded(Q, K, V, ops=ops)
     if w.startswith("sgemm"):
         A = torch.rand(c["M"], c["K"], device="cuda", generator=g) * 2 - 1
         B = torch.rand(c["K"], c["N"], device="cuda", generator=g) * 2 - 1
+        if PEER_OUTPUT:
+            sg = parallel.ShardedGemm(c["M"], c["N"], ops=ops)
+            return (lambda: sg.forward(A, B)), sg.close
         return lambda: parallel.gemm_sharded(A, B, ops=ops)
     if w == "block":
         D, H = c["D"], c["H"]
@@ -308,8 +319,9 @@ def setup_sharded(w: str, precision):
         Wi = torch.randn(3 * D, D, device="cuda", generator=g) * 0.02
         Wo = torch.randn(D, D, device="cuda", generator=g) * 0.02
         mha = parallel.ShardedMHA(Wi, torch.zeros(3 * D, device="cuda"), Wo,
-                                  torch.zeros(D, device="cuda"), H, ops=ops)
-        return lambda: mha.forward(x)
+                                  torch.zeros(D, device="cuda"), H, ops=ops,
+                                  peer_output=PEER_OUTPUT)
+        return (lambda: mha.forward(x)), mha.close
     raise KeyError(f"{w} has no sharded form")
 
 
@@ -467,9 +479,14 @@ def measure_sharded(w: str, rank: int, world: int, steps: int, warmup: int, prec
 
     flush = w in ("prefill", "sgemm")
     run = setup_sharded(w, precision)
+    close = None
+    if isinstance(run, tuple):
+        run, close = run
     times = time_device(run, steps, warmup, world, flush=flush)
     capi.stream_status()
     ms = max_over_ranks(sum(times), world) / steps
+    if close is not None:
+        close()  # collective: the peer buffers are unmapped on every rank
     del run
     torch.cuda.empty_cache()
     ms1 = None
@@ -485,7 +502,9 @@ def measure_sharded(w: str, rank: int, world: int, steps: int, warmup: int, prec
     r = {"w": w, "prec": precision if w != "decode" else "fp32", "scaling": "strong",
          "v": round(value, 2), "u": WORKLOADS[w]["unit"], "ms": round(ms, 4),
          "par": {"prefill": "heads", "decode": "heads", "block": "heads+a2a",
-                 "sgemm": "C rows", "sgemm-large": "C rows"}[w] + f" x{world}"}
+                 "sgemm": "C rows", "sgemm-large": "C rows"}[w]
+         + ("" if w == "prefill" else "+peer stores" if PEER_OUTPUT else "+all-gather")
+         + f" x{world}"}
     if ms1 is not None:
         v1 = work / (ms1 * 1e-3) / scale
         r.update(n1=round(v1, 2), eff=round(value / (world * v1), 3))

@@ -144,6 +144,57 @@ ATTNB_API int attnb_gemm_ex_dev(int trans_a, int trans_b, const float* A, int ld
                       int ldb, const float* bias, float* C, int ldc, int M, int N, int K,
                       float alpha, float beta, int precision, void* stream);
 
+/* attnb_gemm_ex_dev whose epilogue also writes every element of C, at the
+ * same offset (same ldc), into each of the `nreplicas` (0..7) buffers in
+ * `replicas` -- typically the same rows of C's replicas on the other GPUs of
+ * the node, opened with attnb_ipc_import -- so the product and its broadcast
+ * over NVLink are one kernel: the stores leave tile by tile while the
+ * remaining tiles are still being multiplied.  Each replica must have C's
+ * alignment modulo 16 bytes.  Replicas are complete once the stream has
+ * passed the call (the kernel fences its stores system-wide before it
+ * retires); the caller orders the readers on the other GPUs after that, e.g.
+ * with a collective.  No reference counterpart: the reference has no
+ * multi-device code.  It assembles C on every rank for the row-sharded SGEMM
+ * and the sharded MHA block's output rows. */
+ATTNB_API int attnb_gemm_ex_bcast_dev(int trans_a, int trans_b, const float* A, int lda,
+                                      const float* B, int ldb, const float* bias, float* C,
+                                      int ldc, float* const* replicas, int nreplicas, int M,
+                                      int N, int K, float alpha, float beta, int precision,
+                                      void* stream);
+
+/* Device memory shared between the processes of one node (no counterpart in
+ * the reference).  attnb_ipc_export writes the 64-byte handle of the device
+ * allocation that holds `dptr` and dptr's byte offset in it; another process
+ * passes both to attnb_ipc_import, which maps the allocation into the
+ * current device's context (once per handle; later imports share it) and
+ * returns the address that corresponds to `dptr`.  attnb_ipc_close releases
+ * one import (any address inside the mapping).  The exporting process keeps
+ * the allocation alive until every importer has closed it. */
+#define ATTNB_IPC_HANDLE_BYTES 64
+/* A device allocation of its own (cudaMalloc on the current device) for
+ * buffers that other processes will import; attnb_ipc_free releases it. */
+ATTNB_API int attnb_ipc_alloc(size_t bytes, void** dptr);
+ATTNB_API int attnb_ipc_free(void* dptr);
+ATTNB_API int attnb_ipc_export(const void* dptr, void* handle, uint64_t* offset);
+ATTNB_API int attnb_ipc_import(const void* handle, uint64_t offset, void** dptr);
+ATTNB_API int attnb_ipc_close(void* dptr);
+
+/* Barrier of `nranks` GPUs over peer memory (no counterpart in the
+ * reference).  Every rank owns an array of nranks uint64 epochs, zeroed
+ * before first use, that every other rank has mapped (attnb_ipc_import);
+ * peer_flags[r] is rank r's array as mapped here (peer_flags[rank] is not
+ * read).  The call enqueues one small kernel on `stream` that makes this
+ * stream's earlier stores visible system-wide, writes `epoch` into slot
+ * `rank` of every other rank's array, and waits until every slot of
+ * `flags` (its own array) holds at least `epoch`: work enqueued after it on
+ * any rank sees everything every rank enqueued before it.  All ranks pass
+ * the same epoch, starting at 1 and growing by one per barrier.  The wait is
+ * bounded (limit_us microseconds, 0 = 2 s): a rank that never arrives makes
+ * the others raise the device status word, reported by attnb_stream_status
+ * as ATTNB_ERR_DEVICE_TIMEOUT, and return. */
+ATTNB_API int attnb_peer_barrier_dev(uint64_t* flags, uint64_t* const* peer_flags, int nranks,
+                                     int rank, uint64_t epoch, int limit_us, void* stream);
+
 /* y[T,N] = x[T,K] . W[N,K]^T + b[N] on device pointers (b may be NULL).
  * The projection step of attn::mha_block_dense (src/attn_dispatch.cpp:45-95,
  * include/gemm_16x16.h:7-60, include/pack_16x16.h:9-25); ldx >= K, ldw >= K,
@@ -160,6 +211,17 @@ ATTNB_API int attnb_attn_step_dense(const attnb_tensor* Q, const attnb_tensor* K
                           const attnb_tensor* V, attnb_mtensor* O);
 ATTNB_API int attnb_attn_step_dense_dev(const attnb_tensor* Q, const attnb_tensor* K,
                               const attnb_tensor* V, attnb_mtensor* O, void* stream);
+/* attnb_attn_step_dense_dev that also stores every element of O, at the same
+ * offset (same strides), into each of the `nreplicas` (0..7) buffers in
+ * `replicas` -- the same heads of O's replicas on the other GPUs (see
+ * attnb_ipc_import); O needs a unit head-dim stride when nreplicas > 0.  The
+ * stores are fenced system-wide before the kernel retires.  No reference
+ * counterpart (the reference has no multi-device code): the head-sharded
+ * decode step assembles O on every rank with it. */
+ATTNB_API int attnb_attn_step_dense_bcast_dev(const attnb_tensor* Q, const attnb_tensor* K,
+                                              const attnb_tensor* V, attnb_mtensor* O,
+                                              float* const* replicas, int nreplicas,
+                                              void* stream);
 /* The decode step for callers that may not allocate device memory (a custom
  * allocator or pool that owns the device, a hot path where allocation is
  * forbidden, a fixed memory footprint).  No counterpart in the reference.
