@@ -27,7 +27,7 @@ EXPORTED = [
     "attnb_profile_enable", "attnb_profile_read", "attnb_host_alloc", "attnb_host_free",
     "attnb_sgemm", "attnb_gemm_jit", "attnb_sgemm_dev", "attnb_gemm_ex_dev",
     "attnb_gemm_ex_bcast_dev", "attnb_ipc_alloc", "attnb_ipc_free", "attnb_ipc_export", "attnb_ipc_import", "attnb_ipc_close",
-    "attnb_linear_dev",
+    "attnb_linear_dev", "attnb_weight_pack_dev", "attnb_weight_free", "attnb_linear_packed_dev",
     "attnb_attn_step_dense", "attnb_attn_step_dense_dev", "attnb_attn_step_dense_noalloc",
     "attnb_attn_step_dense_bcast_dev", "attnb_peer_barrier_dev",
     "attnb_attn_block_dense", "attnb_attn_block_dense_dev",
@@ -83,6 +83,10 @@ def lib() -> ctypes.CDLL:
         L.attnb_gemm_ex_dev.argtypes = [i, i, vp, i, vp, i, vp, vp, i, i, i, i, f, f, i, vp]
         L.attnb_gemm_ex_bcast_dev.argtypes = [i, i, vp, i, vp, i, vp, vp, i,
                                               ctypes.POINTER(vp), i, i, i, i, f, f, i, vp]
+        L.attnb_weight_pack_dev.argtypes = [vp, i, i, i, i, ctypes.POINTER(vp), vp]
+        L.attnb_weight_free.argtypes = [vp]
+        L.attnb_linear_packed_dev.argtypes = [i, vp, i, vp, vp, vp, i, i, ctypes.POINTER(vp), i,
+                                              vp]
         L.attnb_ipc_alloc.argtypes = [ctypes.c_size_t, ctypes.POINTER(vp)]
         L.attnb_ipc_free.argtypes = [vp]
         L.attnb_ipc_export.argtypes = [vp, vp, ctypes.POINTER(ctypes.c_uint64)]
@@ -92,8 +96,7 @@ def lib() -> ctypes.CDLL:
         L.attnb_attn_step_dense_dev.argtypes = [T, T, T, T, vp]
         L.attnb_attn_step_dense_noalloc.argtypes = [T, T, T, T, vp]
         L.attnb_attn_step_dense_bcast_dev.argtypes = [T, T, T, T, ctypes.POINTER(vp), i, vp]
-        L.attnb_peer_barrier_dev.argtypes = [vp, ctypes.POINTER(vp), i, i, ctypes.c_uint64, i,
-                                             vp]
+        L.attnb_peer_barrier_dev.argtypes = [vp, ctypes.POINTER(vp), i, i, i, vp]
         L.attnb_attn_block_dense.argtypes = [T, T, T, T, i, i]
         L.attnb_attn_block_dense_dev.argtypes = [T, T, T, T, i, i, vp]
         L.attnb_attn_block_dense_batched_dev.argtypes = [T, T, T, T, i, i64, i64, i64, i64, i, i,
@@ -240,6 +243,51 @@ def ipc_close(ptr: int) -> None:
     check(lib().attnb_ipc_close(ptr))
 
 
+class PackedWeight:
+    """A projection weight W [N, K] (float32 CUDA tensor, unit column stride)
+    packed once on the current device for repeated y = x W^T
+    (attnb_weight_pack_dev); the packing is enqueued on `stream`."""
+
+    def __init__(self, W, precision=None, stream=None):
+        import torch
+
+        if W.dim() != 2 or W.stride(1) != 1 or W.dtype != torch.float32:
+            raise ValueError("PackedWeight: W must be 2-D float32 with a unit column stride")
+        self.N, self.K = W.shape
+        self._h = ctypes.c_void_p()
+        check(lib().attnb_weight_pack_dev(W.data_ptr(), W.stride(0), self.N, self.K,
+                                          PREC[precision], ctypes.byref(self._h),
+                                          _stream(stream)))
+
+    def close(self) -> None:
+        if self._h:
+            check(lib().attnb_weight_free(self._h))
+            self._h = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # interpreter shutdown: the library may be gone
+            pass
+
+
+def linear_packed_dev(x, W: PackedWeight, b, y, trans_x=False, replicas=(), stream=None) -> None:
+    """y = op(x) @ W^T + b (b may be None), op(x) = x.T when trans_x; y is also
+    stored into each address in `replicas` (see gemm_ex_bcast_dev)."""
+    M = x.shape[1] if trans_x else x.shape[0]
+    K = x.shape[0] if trans_x else x.shape[1]
+    if K != W.K or tuple(y.shape) != (M, W.N):
+        raise ValueError("linear_packed_dev: shapes do not match")
+    if x.stride(1) != 1 or y.stride(1) != 1:
+        raise ValueError("linear_packed_dev: operands need a unit column stride")
+    if x.dtype != y.dtype or str(x.dtype) != "torch.float32":
+        raise ValueError("linear_packed_dev: x and y must be float32")
+    arr = (ctypes.c_void_p * max(1, len(replicas)))(*[int(r) for r in replicas])
+    check(lib().attnb_linear_packed_dev(int(trans_x), x.data_ptr(), x.stride(0), W._h,
+                                        b.data_ptr() if b is not None else None, y.data_ptr(),
+                                        y.stride(0), M, arr, len(replicas), _stream(stream)))
+
+
 def linear_dev(x, W, b, y, precision=None, stream=None) -> None:
     """y = x @ W^T + b (b may be None)."""
     T_, K = x.shape
@@ -265,14 +313,14 @@ def attn_step_dense_bcast_dev(Q, K, V, O, replicas, stream=None) -> None:
                                                 len(replicas), _stream(stream)))
 
 
-def peer_barrier_dev(flags: int, peer_flags: list, rank: int, epoch: int, limit_us: int = 0,
+def peer_barrier_dev(flags: int, peer_flags: list, rank: int, limit_us: int = 0,
                      stream=None) -> None:
-    """Enqueue the peer-memory barrier (attnb_peer_barrier_dev): `flags` is
-    this rank's epoch array, peer_flags[r] rank r's array as mapped here (any
-    value at index `rank`)."""
+    """Enqueue the next peer-memory barrier (attnb_peer_barrier_dev): `flags`
+    is this rank's array (one epoch per rank, then its barrier count),
+    peer_flags[r] rank r's array as mapped here (any value at index `rank`)."""
     n = len(peer_flags)
     arr = (ctypes.c_void_p * n)(*[int(p) if p else None for p in peer_flags])
-    check(lib().attnb_peer_barrier_dev(flags, arr, n, rank, epoch, limit_us, _stream(stream)))
+    check(lib().attnb_peer_barrier_dev(flags, arr, n, rank, limit_us, _stream(stream)))
 
 
 def attn_step_dense_noalloc(Q, K, V, O, stream=None) -> None:

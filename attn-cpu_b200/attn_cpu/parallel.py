@@ -106,6 +106,13 @@ class DeviceOps:
     def decode_bcast(self, q, k, v, o, replicas):
         self.capi.attn_step_dense_bcast_dev(q, k, v, o, replicas)
 
+    def pack_weight(self, W):
+        """W [N, K] packed once for y = x W^T (in this object's precision)."""
+        return self.capi.PackedWeight(W, precision=self.precision)
+
+    def linear_packed(self, x, Wp, b, y, trans_x=False, replicas=()):
+        self.capi.linear_packed_dev(x, Wp, b, y, trans_x=trans_x, replicas=replicas)
+
     def gemm_ex(self, A, B, C, trans_a, trans_b, bias):
         self.capi.gemm_ex_dev(A, B, C, trans_a=trans_a, trans_b=trans_b, bias=bias,
                               precision=self.precision)
@@ -234,28 +241,28 @@ class PeerGroup:
     where a collective of the communication library costs tens.  Every rank
     calls barrier() at the same points of its stream; work enqueued after a
     barrier on any rank sees every store that any rank enqueued before it
-    (including kernel stores into other ranks' memory).  Waits are bounded: a
-    rank that never arrives shows as ATTNB_ERR_DEVICE_TIMEOUT on the others
-    (capi.stream_status).  Collective construction and close()."""
+    (including kernel stores into other ranks' memory).  The barrier count
+    lives on the device, so steps captured in a CUDA graph replay correctly.
+    Waits are bounded: a rank that never arrives shows as
+    ATTNB_ERR_DEVICE_TIMEOUT on the others (capi.stream_status).  Collective
+    construction and close()."""
 
     def __init__(self, group=None):
         from . import capi
 
         self.capi = capi
         self.rank, self.world = _world(group)
-        # one uint64 epoch per rank (two float32 words each), zeroed
-        self.flags = PeerReplicas((2 * self.world,), group, zero=True)
+        # one uint64 epoch per rank, then this rank's barrier count (two
+        # float32 words each), zeroed
+        self.flags = PeerReplicas((2 * (self.world + 1),), group, zero=True)
         ptrs = [0] * self.world
         for r, p in self.flags.peers:
             ptrs[r] = p
         ptrs[self.rank] = self.flags.local.data_ptr()  # own slot: not read
         self._ptrs = ptrs
-        self.epoch = 0
 
     def barrier(self, limit_us: int = 0) -> None:
-        self.epoch += 1
-        self.capi.peer_barrier_dev(self.flags.local.data_ptr(), self._ptrs, self.rank,
-                                   self.epoch, limit_us)
+        self.capi.peer_barrier_dev(self.flags.local.data_ptr(), self._ptrs, self.rank, limit_us)
 
     def close(self) -> None:
         self.flags.close()
@@ -344,6 +351,12 @@ class ShardedMHA:
         self.peer_output = can if peer_output is None else bool(peer_output)
         self._y = {}  # (B, T) -> PeerReplicas
         self._sync = PeerGroup(group) if self.peer_output else None
+        # The B200 ops pack both projection weights once: the module's weights
+        # are fixed at construction (the reference repacks them per call).
+        self._packed = None
+        if hasattr(self.ops, "pack_weight"):
+            self._packed = (self.ops.pack_weight(self.shard.W_in) if h1 > h0 else None,
+                            self.ops.pack_weight(self.W_out))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         squeeze = x.dim() == 2
@@ -356,7 +369,9 @@ class ShardedMHA:
         x2 = x.reshape(rows, D).contiguous()
         # 1) local heads' [q | k | v] = x W_in_local^T + b_in_local
         qkv = torch.empty(rows, 3 * hl * Dh, dtype=x.dtype, device=x.device)
-        if hl:
+        if hl and self._packed is not None:
+            self.ops.linear_packed(x2, self._packed[0], s.b_in, qkv)
+        elif hl:
             self.ops.linear(x2, s.W_in, s.b_in, qkv)
         qkv3 = qkv.view(B, T, 3 * hl * Dh)
         # 2) attention of the local heads, all sequences in one call, written
@@ -382,14 +397,19 @@ class ShardedMHA:
             yb = self._y.get((B, T))
             if yb is None:
                 yb = self._y[(B, T)] = PeerReplicas((rows, D), self.group)
-            if r1 > r0:
+            if r1 > r0 and self._packed is not None:
+                self.ops.linear_packed(ctxT_mine, self._packed[1], self.b_out, yb.local[r0:r1],
+                                       trans_x=True, replicas=yb.replicas(r0 * D * 4))
+            elif r1 > r0:
                 self.ops.gemm_ex_bcast(ctxT_mine, self.W_out, yb.local[r0:r1],
                                        yb.replicas(r0 * D * 4), True, True, self.b_out)
             self._sync.barrier()
             y = yb.local.view(B, T, D)
             return y[0] if squeeze else y
         y_rows = torch.empty(r1 - r0, D, dtype=x.dtype, device=x.device)
-        if r1 > r0:
+        if r1 > r0 and self._packed is not None:
+            self.ops.linear_packed(ctxT_mine, self._packed[1], self.b_out, y_rows, trans_x=True)
+        elif r1 > r0:
             self.ops.gemm_ex(ctxT_mine, self.W_out, y_rows, True, True, self.b_out)
         counts = [shard_range(rows, r, self.world)[1] - shard_range(rows, r, self.world)[0]
                   for r in range(self.world)]
@@ -404,6 +424,11 @@ class ShardedMHA:
         if self._sync is not None:
             self._sync.close()
             self._sync = None
+        if self._packed is not None:
+            for w in self._packed:
+                if w is not None:
+                    w.close()
+            self._packed = None
 
 
 def gemm_sharded(A: torch.Tensor, B: torch.Tensor, group=None, ops=None,

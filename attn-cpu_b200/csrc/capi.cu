@@ -523,6 +523,93 @@ int attnb_gemm_ex_bcast_dev(int trans_a, int trans_b, const float* A, int lda, c
   });
 }
 
+// -------------------------------------------------------- packed weights
+struct attnb_packed_weight {
+  int device, N, K, precision;
+  void* mem;  // hi, then lo in 3xTF32 (gemm_packed_bytes)
+  float* hi;
+  float* lo;
+};
+
+int attnb_weight_pack_dev(const float* W, int ldw, int N, int K, int precision,
+                          attnb_packed_weight** out, void* stream) {
+  return guarded(__func__, [&] {
+    if (!out) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null output handle");
+    *out = nullptr;
+    if (!W) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    if (N <= 0 || K <= 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "N and K must be positive");
+    if (ldw < K) fail(ATTNB_ERR_INVALID_ARGUMENT, "leading dimension smaller than the row length");
+    const int prec = resolve_precision(precision);
+    const bool split3 = prec != ATTNB_PREC_TF32;
+    DeviceCtx& c = current_ctx();
+    const size_t bytes = gemm_packed_bytes(N, K, split3);
+    void* mem = nullptr;
+    const cudaError_t e = cudaMalloc(&mem, bytes);
+    if (e == cudaErrorMemoryAllocation) {
+      cudaGetLastError();
+      fail(ATTNB_ERR_OUT_OF_MEMORY, "cudaMalloc of a packed weight failed");
+    }
+    ATTNB_CUDA(e);
+    std::unique_ptr<attnb_packed_weight> w(new attnb_packed_weight{c.device, N, K, prec, mem,
+                                                                   nullptr, nullptr});
+    w->hi = static_cast<float*>(mem);
+    w->lo = split3 ? reinterpret_cast<float*>(static_cast<char*>(mem) + bytes / 2) : nullptr;
+    gemm_pack_b(W, ldw, true, N, K, split3, w->hi, w->lo, c.num_sms, as_stream(stream));
+    const cudaError_t le = cudaGetLastError();
+    if (le != cudaSuccess) {
+      cudaFree(mem);
+      ATTNB_CUDA(le);
+    }
+    *out = w.release();
+  });
+}
+
+int attnb_weight_free(attnb_packed_weight* w) {
+  return guarded(__func__, [&] {
+    if (!w) return;
+    int dev = 0;
+    ATTNB_CUDA(cudaGetDevice(&dev));
+    if (dev != w->device) ATTNB_CUDA(cudaSetDevice(w->device));
+    const cudaError_t e = cudaFree(w->mem);
+    if (dev != w->device) cudaSetDevice(dev);
+    delete w;
+    ATTNB_CUDA(e);
+  });
+}
+
+int attnb_linear_packed_dev(int trans_x, const float* x, int ldx, const attnb_packed_weight* W,
+                            const float* b, float* y, int ldy, int M, float* const* replicas,
+                            int nreplicas, void* stream) {
+  return guarded(__func__, [&] {
+    if (!W) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null packed weight");
+    if (M <= 0) return;
+    if (!x || !y) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null data pointer");
+    if (trans_x != 0 && trans_x != 1) fail(ATTNB_ERR_INVALID_ARGUMENT, "trans_x must be 0 or 1");
+    if (ldx < (trans_x ? M : W->K) || ldy < W->N)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "leading dimension smaller than the row length");
+    if (nreplicas < 0 || nreplicas > kMaxPeerOut)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "nreplicas must be in [0, 7]");
+    if (nreplicas > 0 && !replicas) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null replica list");
+    PeerOut po{};
+    po.n = nreplicas;
+    for (int i = 0; i < nreplicas; ++i) {
+      if (!replicas[i]) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null replica pointer");
+      if (((reinterpret_cast<uintptr_t>(replicas[i]) ^ reinterpret_cast<uintptr_t>(y)) & 15u) != 0)
+        fail(ATTNB_ERR_INVALID_ARGUMENT, "replicas must have y's alignment modulo 16 bytes");
+      po.dst[i] = replicas[i];
+    }
+    DeviceCtx& c = current_ctx();
+    if (c.device != W->device)
+      fail(ATTNB_ERR_INVALID_ARGUMENT, "the packed weight lives on another device");
+    cudaStream_t s = as_stream(stream);
+    const GemmPlan p = gemm_plan(M, W->N, W->K, W->precision);
+    void* ws = dev_scratch(c, p.ws_bytes, s);
+    gemm_run(p, x, ldx, trans_x == 0, nullptr, 0, true, y, ldy, 1.f, 0.f, b, ws, c.status,
+             c.num_sms, s, &po, W->hi, W->lo);
+    ATTNB_CUDA(cudaGetLastError());
+  });
+}
+
 // ------------------------------------------------------------ peer memory
 namespace {
 // Device memory of other processes opened in this one.  A handle can be
@@ -725,13 +812,12 @@ int attnb_attn_step_dense_bcast_dev(const attnb_tensor* Q, const attnb_tensor* K
 }
 
 int attnb_peer_barrier_dev(uint64_t* flags, uint64_t* const* peer_flags, int nranks, int rank,
-                           uint64_t epoch, int limit_us, void* stream) {
+                           int limit_us, void* stream) {
   return guarded(__func__, [&] {
     if (nranks < 1 || nranks > kMaxRanks)
       fail(ATTNB_ERR_INVALID_ARGUMENT, "nranks must be in [1, 8]");
     if (rank < 0 || rank >= nranks) fail(ATTNB_ERR_INVALID_ARGUMENT, "rank out of range");
     if (!flags || (nranks > 1 && !peer_flags)) fail(ATTNB_ERR_INVALID_ARGUMENT, "Null pointer");
-    if (epoch == 0) fail(ATTNB_ERR_INVALID_ARGUMENT, "epochs start at 1");
     if (limit_us < 0 || limit_us > 10000000)
       fail(ATTNB_ERR_INVALID_ARGUMENT, "limit_us must be in [0, 1e7] (0: the default 2 s)");
     PeerFlags f{};
@@ -747,7 +833,7 @@ int attnb_peer_barrier_dev(uint64_t* flags, uint64_t* const* peer_flags, int nra
     DeviceCtx& c = current_ctx();
     // Default: the 2 s limit of the kernels' other bounded waits.
     const uint64_t limit_ns = limit_us ? (uint64_t)limit_us * 1000ull : 2000000000ull;
-    peer_barrier(f, epoch, limit_ns, c.status, as_stream(stream));
+    peer_barrier(f, limit_ns, c.status, as_stream(stream));
     ATTNB_CUDA(cudaGetLastError());
   });
 }

@@ -148,6 +148,13 @@ __device__ __forceinline__ void grid_dep_wait() {
   asm volatile("griddepcontrol.wait;" ::: "memory");
 }
 
+// Programmatic dependent launch: this CTA is done with what the dependent
+// grid needs scheduled early; the dependent still reads results only after
+// its griddepcontrol.wait (the whole grid finished).
+__device__ __forceinline__ void grid_dep_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Barrier among the `nthreads` threads (a multiple of 32) that use barrier `id`.
 __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");

@@ -158,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 2) decode_vec_kernel(
   const size_t pidx = (size_t)h * nsplit + split;
   cta_merge_and_store(sm_m, sm_l, sm_acc, nwarps, Dh, nsplit == 1 ? O + h * osH : nullptr, osD,
                       part_o ? part_o + pidx * Dh : nullptr, part_ml ? part_ml + pidx : nullptr);
+  grid_dep_launch();  // the split merge may be scheduled once every CTA gets here
 }
 
 // Any strides / head size: scores of the key range go to shared memory, then
@@ -225,30 +226,107 @@ __global__ void __launch_bounds__(kThreads) decode_generic_kernel(
   if (nsplit > 1 && threadIdx.x == 0) part_ml[pidx] = make_float2(M, L);
 }
 
-// Merge the nsplit partials of each head.
-__global__ void decode_merge_kernel(const float* __restrict__ part_o,
-                                    const float2* __restrict__ part_ml, int nsplit, int Dh,
-                                    float* __restrict__ O, int64_t osH, int64_t osD,
-                                    const PeerOut peers) {
-  const int h = blockIdx.x;
+// Merge the nsplit partials of each head (one CTA of kMergeThreads per head):
+//   m* = max_s m_s,  w_s = 2^(m_s - m*),  L = sum_s w_s l_s,
+//   O[d] = sum_s w_s acc_s[d] / L.
+// The split maxima, weights and L are reductions over all threads; the sum
+// over splits is spread over thread groups (each group a strided subset of
+// the splits, each thread one float4 of the head), so the loads of
+// different splits are in flight together rather than one after another.
+constexpr int kMergeThreads = 128;
+constexpr int kMergeMaxW = 1024;  // split weights kept in shared memory
+
+__device__ __forceinline__ float block_reduce(float v, bool is_max, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float u = __shfl_xor_sync(0xffffffffu, v, o);
+    v = is_max ? fmaxf(v, u) : v + u;
+  }
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = red[0];
+#pragma unroll
+  for (int w = 1; w < kMergeThreads / 32; ++w) r = is_max ? fmaxf(r, red[w]) : r + red[w];
+  __syncthreads();
+  return r;
+}
+
+__global__ void __launch_bounds__(kMergeThreads) decode_merge_kernel(
+    const float* __restrict__ part_o, const float2* __restrict__ part_ml, int nsplit, int Dh,
+    float* __restrict__ O, int64_t osH, int64_t osD, const PeerOut peers) {
+  grid_dep_wait();  // the partials come from the split kernel launched before this one
+  __shared__ float red[kMergeThreads / 32];
+  __shared__ float wsh[kMergeMaxW];
+  __shared__ float4 part[kMergeThreads];
+  const int h = blockIdx.x, t = threadIdx.x;
   const float2* ml = part_ml + (size_t)h * nsplit;
-  float M = -INFINITY;
-  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, ml[s].x);
-  float L = 0.f;
-  for (int s = 0; s < nsplit; ++s) L += fast_exp2(ml[s].x - M) * ml[s].y;
-  const float invL = 1.f / L;
-  for (int d = threadIdx.x; d < Dh; d += blockDim.x) {
-    float o = 0.f;
-    for (int s = 0; s < nsplit; ++s)
-      o += fast_exp2(ml[s].x - M) * part_o[((size_t)h * nsplit + s) * Dh + d];
+  const float* po = part_o + (size_t)h * nsplit * Dh;
+  float mx = -INFINITY;
+  for (int s = t; s < nsplit; s += kMergeThreads) mx = fmaxf(mx, ml[s].x);
+  const float M = block_reduce(mx, true, red);
+  float lsum = 0.f;
+  for (int s = t; s < nsplit; s += kMergeThreads) {
+    const float2 v = ml[s];
+    const float w = v.x == -INFINITY ? 0.f : fast_exp2(v.x - M);
+    if (s < kMergeMaxW) wsh[s] = w;
+    lsum = fmaf(w, v.y, lsum);
+  }
+  const float invL = 1.f / block_reduce(lsum, false, red);  // also orders the wsh writes
+  auto weight = [&](int s) {
+    if (s < kMergeMaxW) return wsh[s];
+    const float m = ml[s].x;
+    return m == -INFINITY ? 0.f : fast_exp2(m - M);
+  };
+  auto put = [&](int d, float v) {
     const int64_t off = h * osH + d * osD;
-    O[off] = o * invL;
+    O[off] = v;
     // Replicas on other GPUs (the sharded decode step's output heads).
 #pragma unroll
     for (int p = 0; p < kMaxPeerOut; ++p)
-      if (p < peers.n) peers.dst[p][off] = o * invL;
+      if (p < peers.n) peers.dst[p][off] = v;
+  };
+  const int nd4 = Dh / 4;
+  if (Dh % 4 == 0 && nd4 <= kMergeThreads && (reinterpret_cast<uintptr_t>(po) & 15u) == 0) {
+    const int groups = kMergeThreads / nd4;
+    const int d4 = t % nd4, gi = t / nd4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (gi < groups) {
+#pragma unroll 4
+      for (int s = gi; s < nsplit; s += groups) {
+        const float w = weight(s);
+        const float4 v = *reinterpret_cast<const float4*>(po + (size_t)s * Dh + 4 * d4);
+        acc.x = fmaf(w, v.x, acc.x);
+        acc.y = fmaf(w, v.y, acc.y);
+        acc.z = fmaf(w, v.z, acc.z);
+        acc.w = fmaf(w, v.w, acc.w);
+      }
+    }
+    part[t] = acc;
+    __syncthreads();
+    if (t < nd4) {
+      float4 o = part[t];
+      for (int g = 1; g < groups; ++g) {
+        const float4 v = part[g * nd4 + t];
+        o.x += v.x;
+        o.y += v.y;
+        o.z += v.z;
+        o.w += v.w;
+      }
+      put(4 * t, o.x * invL);
+      put(4 * t + 1, o.y * invL);
+      put(4 * t + 2, o.z * invL);
+      put(4 * t + 3, o.w * invL);
+    }
+  } else {
+    for (int d = t; d < Dh; d += kMergeThreads) {
+      float o = 0.f;
+#pragma unroll 4
+      for (int s = 0; s < nsplit; ++s) o = fmaf(weight(s), po[(size_t)s * Dh + d], o);
+      put(d, o * invL);
+    }
   }
   if (peers.n > 0) __threadfence_system();
+  grid_dep_launch();
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -313,8 +391,9 @@ void decode_launch(const DecodePlan& p, const View3& Q, const View3& K, const Vi
   }
   const PeerOut none{};
   if (p.nsplit > 1) {
-    decode_merge_kernel<<<H, 128, 0, stream>>>(part_o, part_ml, p.nsplit, Dh, O.data, O.sH, O.sD,
-                                               peers ? *peers : none);
+    ATTNB_CUDA(launch_pdl(decode_merge_kernel, dim3(H), dim3(kMergeThreads), 0, stream,
+                          (const float*)part_o, (const float2*)part_ml, p.nsplit, Dh, O.data,
+                          O.sH, O.sD, peers ? *peers : none));
   } else if (peers) {
     // One key range per head: the attention kernel stored O itself; copy the
     // rows (unit head-dim stride, checked by the caller) to the replicas.

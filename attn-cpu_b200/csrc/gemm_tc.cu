@@ -796,9 +796,10 @@ GemmPlan gemm_plan(int M, int N, int K, int precision) {
 void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, const float* B,
               int64_t ldb, bool b_kmajor, float* C, int64_t ldc, float alpha, float beta,
               const float* bias, void* ws, int* status, int num_sms, cudaStream_t s,
-              const PeerOut* peers) {
+              const PeerOut* peers, const float* pre_b_hi, const float* pre_b_lo) {
   if (p.M <= 0 || p.N <= 0 || p.K <= 0) return;
   const bool bcast = peers != nullptr && peers->n > 0;
+  const bool prepacked = pre_b_hi != nullptr;
   if (alpha == 0.f && bias == nullptr) {
     if (beta != 1.f) gemm_scale_bias(C, ldc, p.M, p.N, beta, nullptr, num_sms, s);
     if (bcast)  // no product to fuse with: copy the rows to the replicas
@@ -816,7 +817,8 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
     auto aligned = [](const float* x, int64_t ld) {
       return (reinterpret_cast<uintptr_t>(x) & 15u) == 0 && ld % 4 == 0;
     };
-    if (!bcast && !p.split3 && a_kmajor && pick_bn(p.M, p.N, false, num_sms) == 64 &&
+    if (!bcast && !prepacked && !p.split3 && a_kmajor &&
+        pick_bn(p.M, p.N, false, num_sms) == 64 &&
         tiles64 <= num_sms && aligned(A, lda) && aligned(B, ldb)) {
       const CUtensorMap ta = make_tmap_2d(A, p.M, p.K, lda, BM, BK);
       const CUtensorMap tb = b_kmajor ? make_tmap_2d(B, p.N, p.K, ldb, 64, BK)
@@ -832,16 +834,22 @@ void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, con
   }
   char* w = static_cast<char*>(ws);
   float* a_hi = reinterpret_cast<float*>(w + p.off_a_hi);
-  float* b_hi = reinterpret_cast<float*>(w + p.off_b_hi);
   float* a_lo = p.split3 ? reinterpret_cast<float*>(w + p.off_a_lo) : nullptr;
-  float* b_lo = p.split3 ? reinterpret_cast<float*>(w + p.off_b_lo) : nullptr;
-  // A -> [M, Kp] and B -> [N, Kp], K-major, in one launch.
+  const float* b_hi = prepacked ? pre_b_hi : reinterpret_cast<float*>(w + p.off_b_hi);
+  const float* b_lo = prepacked ? pre_b_lo
+                                : (p.split3 ? reinterpret_cast<float*>(w + p.off_b_lo) : nullptr);
+  // A -> [M, Kp] and B -> [N, Kp], K-major, in one launch (B only when it
+  // does not come packed already).
   PackJob jobs[2];
   jobs[0] = a_kmajor ? PackJob{A, 0, lda, 1, 1, p.M, p.K, p.M, p.Kp, false, 1.f, a_hi, a_lo}
                      : PackJob{A, 0, lda, 1, 1, p.K, p.M, p.M, p.Kp, true, 1.f, a_hi, a_lo};
-  jobs[1] = b_kmajor ? PackJob{B, 0, ldb, 1, 1, p.N, p.K, p.N, p.Kp, false, 1.f, b_hi, b_lo}
-                     : PackJob{B, 0, ldb, 1, 1, p.K, p.N, p.N, p.Kp, true, 1.f, b_hi, b_lo};
-  pack_launch(jobs, 2, p.split3, num_sms, s);
+  if (!prepacked) {
+    float* bh = const_cast<float*>(b_hi);
+    float* bl = const_cast<float*>(b_lo);
+    jobs[1] = b_kmajor ? PackJob{B, 0, ldb, 1, 1, p.N, p.K, p.N, p.Kp, false, 1.f, bh, bl}
+                       : PackJob{B, 0, ldb, 1, 1, p.K, p.N, p.N, p.Kp, true, 1.f, bh, bl};
+  }
+  pack_launch(jobs, prepacked ? 1 : 2, p.split3, num_sms, s);
   const int bn = pick_bn(p.M, p.N, p.split3, num_sms);
   const CUtensorMap tA_hi = make_tmap_2d(a_hi, p.M, p.Kp, p.Kp, BM, BK);
   const CUtensorMap tB_hi = make_tmap_2d(b_hi, p.N, p.Kp, p.Kp, bn, BK);
@@ -886,6 +894,20 @@ void gemm_scale_bias(float* C, int64_t ldc, int M, int N, float beta, const floa
 
 size_t gemm_workspace_bound(int M, int N, int K, int precision) {
   return gemm_plan(M, N, K, precision).ws_bytes;
+}
+
+size_t gemm_packed_bytes(int rows, int K, bool split3) {
+  const int Kp = (K + BK - 1) / BK * BK;
+  const size_t one = ((size_t)rows * Kp * sizeof(float) + 255) & ~size_t(255);
+  return split3 ? 2 * one : one;
+}
+
+void gemm_pack_b(const float* B, int64_t ldb, bool b_kmajor, int N, int K, bool split3,
+                 float* hi, float* lo, int num_sms, cudaStream_t s) {
+  const int Kp = (K + BK - 1) / BK * BK;
+  const PackJob job = b_kmajor ? PackJob{B, 0, ldb, 1, 1, N, K, N, Kp, false, 1.f, hi, lo}
+                               : PackJob{B, 0, ldb, 1, 1, K, N, N, Kp, true, 1.f, hi, lo};
+  pack_launch(&job, 1, split3, num_sms, s);
 }
 
 }  // namespace attnb

@@ -33,17 +33,17 @@ struct PeerOut {
   int n;
 };
 // Flag arrays of a cross-GPU barrier (peer.cu): `local` is this rank's array
-// of n epochs, peer[r] rank r's array as mapped into this process.
+// of n epochs followed by its own barrier count, peer[r] rank r's array as
+// mapped into this process.
 constexpr int kMaxRanks = 8;
 struct PeerFlags {
   uint64_t* local;
   uint64_t* peer[kMaxRanks];
   int n, rank;
 };
-// Enqueues the barrier for `epoch` on s; a wait longer than limit_ns raises
-// the status word.
-void peer_barrier(const PeerFlags& f, uint64_t epoch, uint64_t limit_ns, int* status,
-                  cudaStream_t s);
+// Enqueues the next barrier on s; a wait longer than limit_ns raises the
+// status word.
+void peer_barrier(const PeerFlags& f, uint64_t limit_ns, int* status, cudaStream_t s);
 
 // ------------------------------------------------------------ decode (K4)
 // Split-KV plan for one decode step: how many key ranges each head is cut
@@ -183,9 +183,18 @@ void gemm_scale_bias(float* C, int64_t ldc, int M, int N, float beta, const floa
                      int num_sms, cudaStream_t s);
 // Scratch bytes of a plan of this size.
 size_t gemm_workspace_bound(int M, int N, int K, int precision);
+// With pre_b_hi (and pre_b_lo in 3xTF32), B is not read: the operand comes
+// already packed by gemm_pack_b for this N, K and precision.
 void gemm_run(const GemmPlan& p, const float* A, int64_t lda, bool a_kmajor, const float* B,
               int64_t ldb, bool b_kmajor, float* C, int64_t ldc, float alpha, float beta,
               const float* bias, void* ws, int* status, int num_sms, cudaStream_t s,
-              const PeerOut* peers = nullptr);
+              const PeerOut* peers = nullptr, const float* pre_b_hi = nullptr,
+              const float* pre_b_lo = nullptr);
+// Bytes of one packed operand of `rows` x K (hi, then lo in 3xTF32, each
+// 256-byte aligned), and the packing of B ([N, K] rows when b_kmajor, else
+// [K, N]) into it, as gemm_run packs B.
+size_t gemm_packed_bytes(int rows, int K, bool split3);
+void gemm_pack_b(const float* B, int64_t ldb, bool b_kmajor, int N, int K, bool split3,
+                 float* hi, float* lo, int num_sms, cudaStream_t s);
 
 }  // namespace attnb

@@ -7,16 +7,19 @@
 // tens of microseconds for that, which is most of a sharded decode step.  This
 // is the same ordering done with one flag per rank pair:
 //
-//   rank r's flag array F_r holds one 64-bit epoch per rank, in device memory
-//   every rank has mapped (CUDA IPC).  At barrier e, rank r's kernel (one
-//   warp) fences its earlier stores system-wide, writes e into slot r of every
-//   other rank's array with a release store, then waits until every slot of
-//   its own array holds at least e (acquire loads).
+//   rank r's flag array F_r holds one 64-bit epoch per rank, plus its own
+//   barrier count, in device memory every rank has mapped (CUDA IPC).  At
+//   each barrier rank r's kernel (one warp) advances its count to e, fences
+//   its earlier stores system-wide, writes e into slot r of every other
+//   rank's array with a release store, then waits until every slot of its own
+//   array holds at least e (acquire loads).
 //
-// Epochs only grow, so no reset is needed between barriers.  The wait is
-// bounded (ATTNB_WAIT_LIMIT_NS): a rank that never arrives makes the others
-// raise the device status word and return, and the host reports
-// ATTNB_ERR_DEVICE_TIMEOUT instead of a hung GPU.
+// Every rank runs the same sequence of barriers, so the counts agree; they
+// live on the device, so a captured CUDA graph replays correctly.  Epochs
+// only grow, so no reset is needed between barriers.  The wait is bounded
+// (ATTNB_WAIT_LIMIT_NS or the caller's limit): a rank that never arrives
+// makes the others raise the device status word and return, and the host
+// reports ATTNB_ERR_DEVICE_TIMEOUT instead of a hung GPU.
 #include "common.cuh"
 #include "kernels.h"
 #include "runtime.h"
@@ -34,8 +37,13 @@ __device__ __forceinline__ uint64_t load_acquire_sys(const uint64_t* p) {
   return v;
 }
 
-__global__ void peer_barrier_kernel(PeerFlags f, uint64_t epoch, uint64_t limit_ns, int* status) {
+__global__ void peer_barrier_kernel(PeerFlags f, uint64_t limit_ns, int* status) {
   const int t = threadIdx.x;
+  grid_dep_wait();  // launched behind the kernel whose stores this barrier publishes
+  // This rank's barrier count (slot n of its own array, written only here).
+  const uint64_t epoch = f.local[f.n] + 1;
+  __syncwarp();
+  if (t == 0) f.local[f.n] = epoch;
   // Earlier kernels on this stream fenced their peer stores before retiring;
   // this fence orders anything else this thread's stream made visible.
   __threadfence_system();
@@ -55,9 +63,8 @@ __global__ void peer_barrier_kernel(PeerFlags f, uint64_t epoch, uint64_t limit_
 
 }  // namespace
 
-void peer_barrier(const PeerFlags& f, uint64_t epoch, uint64_t limit_ns, int* status,
-                  cudaStream_t s) {
-  peer_barrier_kernel<<<1, 32, 0, s>>>(f, epoch, limit_ns, status);
+void peer_barrier(const PeerFlags& f, uint64_t limit_ns, int* status, cudaStream_t s) {
+  ATTNB_CUDA(launch_pdl(peer_barrier_kernel, dim3(1), dim3(32), 0, s, f, limit_ns, status));
 }
 
 }  // namespace attnb

@@ -469,6 +469,31 @@ def kernel_time(run, w: str, steps: int, world: int, flush: bool):
     return max_over_ranks(ms / steps, world), n // max(1, steps)
 
 
+GRAPH_STEPS = 2  # decode steps per CUDA-graph replay (ShardedDecode alternates two buffers)
+
+
+def graphed(run, reps: int):
+    """A CUDA graph of `reps` back-to-back calls of `run` (warmed up first on a
+    side stream, so no allocation happens during capture).  Replaying it
+    costs the host one launch, so microsecond-scale steps are timed on the
+    device rather than behind the host's launch path."""
+    import torch
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(3):
+            run()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(reps):
+            run()
+    torch.cuda.synchronize()
+    return g
+
+
 def measure_sharded(w: str, rank: int, world: int, steps: int, warmup: int, precision):
     """Strong scaling: one problem over all ranks, collectives inside the step,
     beside the same problem on one GPU through the single-GPU entry point
@@ -482,17 +507,26 @@ def measure_sharded(w: str, rank: int, world: int, steps: int, warmup: int, prec
     close = None
     if isinstance(run, tuple):
         run, close = run
+    # The decode step is tens of microseconds per rank: its peer-store form
+    # (kernels only, no collective) and the one-GPU step are replayed from
+    # CUDA graphs of GRAPH_STEPS steps, both alike.
+    use_graph = w == "decode" and PEER_OUTPUT
+    reps = GRAPH_STEPS if use_graph else 1
+    if use_graph:
+        run = graphed(run, reps).replay
     times = time_device(run, steps, warmup, world, flush=flush)
     capi.stream_status()
-    ms = max_over_ranks(sum(times), world) / steps
+    ms = max_over_ranks(sum(times), world) / (steps * reps)
+    del run
     if close is not None:
         close()  # collective: the peer buffers are unmapped on every rank
-    del run
     torch.cuda.empty_cache()
     ms1 = None
     if rank == 0:
         run1 = setup_workload(w, 0, precision, host=False)[0]
-        ms1 = sum(time_device(run1, steps, warmup, 1, flush)) / steps
+        if use_graph:
+            run1 = graphed(run1, reps).replay
+        ms1 = sum(time_device(run1, steps, warmup, 1, flush)) / (steps * reps)
         del run1
         torch.cuda.empty_cache()
     barrier(world)
@@ -505,6 +539,8 @@ def measure_sharded(w: str, rank: int, world: int, steps: int, warmup: int, prec
                  "sgemm": "C rows", "sgemm-large": "C rows"}[w]
          + ("" if w == "prefill" else "+peer stores" if PEER_OUTPUT else "+all-gather")
          + f" x{world}"}
+    if use_graph:
+        r["graph"] = f"{reps} steps per replay"
     if ms1 is not None:
         v1 = work / (ms1 * 1e-3) / scale
         r.update(n1=round(v1, 2), eff=round(value / (world * v1), 3))

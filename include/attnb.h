@@ -180,20 +180,44 @@ ATTNB_API int attnb_ipc_import(const void* handle, uint64_t offset, void** dptr)
 ATTNB_API int attnb_ipc_close(void* dptr);
 
 /* Barrier of `nranks` GPUs over peer memory (no counterpart in the
- * reference).  Every rank owns an array of nranks uint64 epochs, zeroed
- * before first use, that every other rank has mapped (attnb_ipc_import);
+ * reference).  Every rank owns an array of nranks + 1 uint64 words, zeroed
+ * before first use, that every other rank has mapped (attnb_ipc_import):
+ * one epoch slot per rank and, last, this rank's own barrier count.
  * peer_flags[r] is rank r's array as mapped here (peer_flags[rank] is not
- * read).  The call enqueues one small kernel on `stream` that makes this
- * stream's earlier stores visible system-wide, writes `epoch` into slot
- * `rank` of every other rank's array, and waits until every slot of
- * `flags` (its own array) holds at least `epoch`: work enqueued after it on
- * any rank sees everything every rank enqueued before it.  All ranks pass
- * the same epoch, starting at 1 and growing by one per barrier.  The wait is
+ * read).  The call enqueues one small kernel on `stream` that advances the
+ * count to e, makes this stream's earlier stores visible system-wide, writes
+ * e into slot `rank` of every other rank's array, and waits until every slot
+ * of `flags` (its own array) holds at least e: work enqueued after it on any
+ * rank sees everything every rank enqueued before it.  Every rank must make
+ * the same sequence of barrier calls.  The count lives on the device, so a
+ * CUDA graph that captured the call replays it correctly.  The wait is
  * bounded (limit_us microseconds, 0 = 2 s): a rank that never arrives makes
  * the others raise the device status word, reported by attnb_stream_status
  * as ATTNB_ERR_DEVICE_TIMEOUT, and return. */
 ATTNB_API int attnb_peer_barrier_dev(uint64_t* flags, uint64_t* const* peer_flags, int nranks,
-                                     int rank, uint64_t epoch, int limit_us, void* stream);
+                                     int rank, int limit_us, void* stream);
+
+/* A projection weight W [N, K] (the B operand of y = x W^T) packed once for
+ * repeated products (no counterpart in the reference, whose projections
+ * repack per call; its shape-keyed weight cache, src/attn_dispatch.cpp:46,
+ * is not reproduced: a packed weight is tied to the handle, not to a shape).
+ * attnb_weight_pack_dev allocates device memory on the current device
+ * (released by attnb_weight_free) and enqueues the packing of W (device
+ * pointer, ldw >= K) for `precision` on `stream`.
+ * attnb_linear_packed_dev: y[M,N] = op(x) . W^T + b[N] (b may be NULL), op(x)
+ * = x stored [M,K] (trans_x = 0, ldx >= K) or x^T with x stored [K,M]
+ * (trans_x = 1, ldx >= M), ldy >= N, in the weight's precision; like
+ * attnb_gemm_ex_bcast_dev it also stores y into the `nreplicas` (0..7)
+ * replicas (same ldy, y's alignment modulo 16 bytes).  The sharded MHA block
+ * packs its weights once and runs both projections through it. */
+typedef struct attnb_packed_weight attnb_packed_weight;
+ATTNB_API int attnb_weight_pack_dev(const float* W, int ldw, int N, int K, int precision,
+                                    attnb_packed_weight** out, void* stream);
+ATTNB_API int attnb_weight_free(attnb_packed_weight* w);
+ATTNB_API int attnb_linear_packed_dev(int trans_x, const float* x, int ldx,
+                                      const attnb_packed_weight* W, const float* b, float* y,
+                                      int ldy, int M, float* const* replicas, int nreplicas,
+                                      void* stream);
 
 /* y[T,N] = x[T,K] . W[N,K]^T + b[N] on device pointers (b may be NULL).
  * The projection step of attn::mha_block_dense (src/attn_dispatch.cpp:45-95,

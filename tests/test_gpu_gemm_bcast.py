@@ -153,26 +153,50 @@ def test_decode_bcast_vs_oracle_and_replicas(cuda):
 
 
 def test_peer_barrier_single_gpu(cuda):
-    """The peer-memory barrier with both flag arrays on this GPU: when the
-    other rank's slot already holds the epoch the kernel returns and has
-    written its own epoch into the other rank's array; when nothing ever
-    writes the slot, the bounded wait expires after 0.2 s, the status word
-    reports ATTNB_ERR_DEVICE_TIMEOUT and the context stays usable."""
+    """The peer-memory barrier with both flag arrays on this GPU (rank 0 of
+    two): when the other rank's slot already holds the next epoch the kernel
+    returns, has advanced its own count and written the epoch into the other
+    rank's array; when nothing ever writes the slot, the bounded wait expires
+    after 0.2 s, the status word reports ATTNB_ERR_DEVICE_TIMEOUT and the
+    context stays usable."""
     import torch
     from attn_cpu import capi
 
-    mine = torch.zeros(2, dtype=torch.int64, device="cuda")
-    other = torch.zeros(2, dtype=torch.int64, device="cuda")
-    mine[1] = 5  # rank 1 has reached epoch 5
-    capi.peer_barrier_dev(mine.data_ptr(), [0, other.data_ptr()], 0, 3)
+    mine = torch.zeros(3, dtype=torch.int64, device="cuda")   # [slot 0, slot 1, count]
+    other = torch.zeros(3, dtype=torch.int64, device="cuda")
+    mine[1] = 1  # rank 1 has reached barrier 1
+    capi.peer_barrier_dev(mine.data_ptr(), [0, other.data_ptr()], 0)
     capi.stream_status()
-    assert other.tolist() == [3, 0]
-    mine.zero_()
-    capi.peer_barrier_dev(mine.data_ptr(), [0, other.data_ptr()], 0, 7, limit_us=200000)
+    assert mine.tolist() == [0, 1, 1] and other.tolist() == [1, 0, 0]
+    capi.peer_barrier_dev(mine.data_ptr(), [0, other.data_ptr()], 0, limit_us=200000)
     with pytest.raises(capi.AttnbError) as e:
         capi.stream_status()
     assert e.value.code == capi.ERR_DEVICE_TIMEOUT
-    assert other.tolist() == [7, 0]
+    assert mine.tolist() == [0, 1, 2] and other.tolist() == [2, 0, 0]
     x = torch.ones(4, device="cuda")
     assert float((x * 2).sum()) == 8.0
     capi.stream_status()  # cleared
+
+
+def test_peer_barrier_in_cuda_graph(cuda):
+    """The barrier count lives on the device: three replays of a captured
+    barrier advance it three times (each replay passing, as the other rank's
+    slot is set ahead)."""
+    import torch
+    from attn_cpu import capi
+
+    mine = torch.zeros(3, dtype=torch.int64, device="cuda")
+    other = torch.zeros(3, dtype=torch.int64, device="cuda")
+    mine[1] = 100
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        capi.peer_barrier_dev(mine.data_ptr(), [0, other.data_ptr()], 0)  # outside the graph
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            capi.peer_barrier_dev(mine.data_ptr(), [0, other.data_ptr()], 0)
+    torch.cuda.synchronize()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    capi.stream_status()
+    assert mine[2].item() == 4 and other[0].item() == 4
