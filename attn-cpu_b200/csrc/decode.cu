@@ -339,9 +339,12 @@ DecodePlan decode_plan(const View3& Q, const View3& K, const View3& V, int num_s
   p.fast = Q.sD == 1 && K.sD == 1 && V.sD == 1 && Dh % 4 == 0 && Dh <= 256 &&
            aligned16(Q.data) && aligned16(K.data) && aligned16(V.data) && Q.sH % 4 == 0 &&
            K.sH % 4 == 0 && K.sT % 4 == 0 && V.sH % 4 == 0 && V.sT % 4 == 0;
-  // About eight CTAs per SM over all heads (a few waves of equal ranges); each
-  // split keeps at least 64 keys so the merge stays cheap.
-  int per_sm = 8;
+  // Two CTAs per SM over all heads (the kernel's residency: one wave of long
+  // key ranges); each split keeps at least 64 keys so the merge stays cheap.
+  // Measured with graph-replayed steps at T = 4096, Dh = 128: at 256 heads
+  // 150 us against 160 us with eight per SM (several waves of shorter
+  // ranges), at 32 heads 27 us against 34 us.
+  int per_sm = 2;
   if (const char* e = std::getenv("ATTNB_DECODE_CTAS_PER_SM")) per_sm = std::max(1, std::atoi(e));
   const int slots = std::max(1, num_sms) * per_sm;
   int ns = std::max(1, slots / std::max(1, H));

@@ -365,7 +365,13 @@ def setup_workload(w: str, rank: int, precision, host: bool = True):
             hQ, hK, hV = (t.cpu().pin_memory() for t in (Q, K, V))
             nQ, nK, nV = hQ.numpy(), hK.numpy(), hV.numpy()
             e2e = lambda: attn_cpu.attn_step_dense(nQ, nK, nV)
-        return run, e2e, 4 * (Q.numel() + K.numel() + V.numel()), 4 * O.numel(), 2  # + merge
+        # Launches: the split kernel, plus the split merge when the library's
+        # plan (two CTAs per SM over all heads, at least 64 keys a range) cuts
+        # a head's keys into more than one range.
+        sms = torch.cuda.get_device_properties(0).multi_processor_count
+        nsplit = min(max(1, 2 * sms // H), (T + 63) // 64)
+        launches = 1 if nsplit == 1 else 2
+        return run, e2e, 4 * (Q.numel() + K.numel() + V.numel()), 4 * O.numel(), launches
     if w.startswith("sgemm"):
         M, N, K = c["M"], c["N"], c["K"]
         A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1

@@ -35,10 +35,11 @@ def test_noalloc_matches_dev_entry_point_twice(cuda):
     import torch
     from attn_cpu import capi
 
-    # Decode config shape (B=8 x H=32 heads, T=4096, Dh=128): the plan splits
-    # each head's keys, so the fixed scratch is used.  Different inputs on the
-    # two calls: the second must not see the first call's partials.
-    H, T, Dh = 256, 4096, 128
+    # The decode config's head shape (T=4096, Dh=128) with 64 heads, few enough
+    # that the plan splits each head's keys, so the fixed scratch is used.
+    # Different inputs on the two calls: the second must not see the first
+    # call's partials.
+    H, T, Dh = 64, 4096, 128
     for seed in (1, 2):
         g = torch.Generator(device="cuda").manual_seed(seed)
         Q = torch.randn(H, Dh, device="cuda", generator=g)
