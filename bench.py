@@ -70,8 +70,8 @@ WORKLOADS = {
 NCU_TRAFFIC = {
     ("prefill", "3xtf32"): 3.22e6,     # attn_tc, [1,8,512,64]: raw Q/K/V read once
     ("prefill-large", "3xtf32"): 5.00e8,  # attn_tc [1,32,4096,128]: packed K/V re-read via L2
-    ("decode", "3xtf32"): 1.0798e9,    # decode: K + V once (1.0737e9) + split partials
-    ("decode", "tf32"): 1.0798e9,
+    ("decode", "3xtf32"): 1.0778e9,    # decode: K + V once (1.0737e9) + output, one range a head
+    ("decode", "tf32"): 1.0778e9,
     ("sgemm-large", "3xtf32"): 51.15e9,  # gemm_tc 16384^3: packed operands re-read ~12x
     ("block", "3xtf32"): 6.93e9,       # gemm_tc QKV (5.11e9) + output (1.82e9) projections
 }
