@@ -559,20 +559,19 @@ def compact(w: str, res: dict, precision) -> dict:
     roofline fraction (of the TF32 rate, or of HBM for decode; the dominant
     kernel of each workload is named in dominant_of), e2e and the SM clock."""
     rf = res["roofline"]
-    out = {"w": w, "prec": precision if w != "decode" else "fp32", "v": res["value"],
+    out = {"w": w, "prec": precision if w != "decode" else "fp32", "v": round(res["value"], 1),
            "u": res["unit"], "ms": round(res["ms_per_step"], 4),
-           "k_ms": round(rf["kernel_ms_per_step"], 4), "frac": rf["frac"]}
+           "k_ms": round(rf["kernel_ms_per_step"], 4), "frac": round(rf["frac"], 3)}
     if "frac_of_3xtf32_cap" in rf:
-        out["frac3x"] = rf["frac_of_3xtf32_cap"]
+        out["frac3x"] = round(rf["frac_of_3xtf32_cap"], 3)
     if res.get("e2e"):
-        out["e2e"] = res["e2e"]["value"]
+        out["e2e"] = round(res["e2e"]["value"], 2)
     if res.get("e2e_resident"):
-        out["e2e_res"] = res["e2e_resident"]["value"]
+        out["e2e_res"] = round(res["e2e_resident"]["value"], 1)
     clk = res.get("clocks") or {}
-    if clk:
+    if clk.get("reasons"):  # the SM clock only when something held it down
         out["mhz"] = clk.get("sm_mhz")
-        if clk.get("reasons"):
-            out["why"] = clk["reasons"]
+        out["why"] = clk["reasons"]
     return out
 
 
@@ -827,10 +826,10 @@ def main():
                 "config": config_of(args.workload, world),
                 "e2e": head.get("e2e"), "roofline": head["roofline"],
                 "gpu_launches": head["gpu_launches"], "clocks": head["clocks"],
-                "cpu_baseline": cpu, "also": also}
-        line["host_binding"] = binding
+                "cpu_baseline": cpu, "host_binding": binding}
         if head.get("e2e_resident"):
             line["e2e_resident"] = head["e2e_resident"]
+        line["also"] = also  # last, so the end of the line carries the other configs
         print(json.dumps(line, separators=(",", ":")), flush=True)
     if world > 1:
         import torch.distributed as dist
